@@ -1,0 +1,284 @@
+#!/usr/bin/env python3
+"""Benchmark: batch-1 greedy decode tokens/s, stories110M shape, on B200.
+
+One step = one full greedy decode of seq_len = 1024 positions (8 seeded prompt
+tokens teacher-forced, then argmax feedback), from a reset KV cache, on
+seeded N(0, 0.02) fp32 weights of the stories110M shape (438 MB of weights,
+larger than the 126 MB L2, so every token streams its weights from HBM).
+
+  value  device-resident run: the decode's CUDA graph chain is enqueued with
+         inputs already on the GPU, timed with CUDA events on its stream.
+  e2e    the drop-in C API path: pt_forward_step(ctx, token) per position
+         (host token in, host token out), timed with CUDA events around the
+         whole loop.
+
+N > 1 (torchrun): the layer pipeline over N GPUs (pt_dist_forward_step), the
+last rank holding embedding + classifier as in the pitorch ring.
+
+--impl reference times the reference's own host C decode (oracle/_ref, built
+from the reference sources) on this host's CPU on a bounded sample of
+positions per step.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from pitorch_b200 import synth  # noqa: E402
+
+MODEL = "stories110M"
+N_PROMPT = 8
+METRIC = "batch-1 decode tokens/s (stories110M shape)"
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def decode_bytes_per_token(cfg, pos):
+    """Algorithmic HBM bytes of one decode position: all weights read once
+    (tied classifier = embedding table, read once by the classifier, plus one
+    embedding row), the KV cache read for positions <= pos and one KV row
+    written per layer."""
+    dim, hidden, L, nh, nkv, V, seq = cfg
+    kvd = nkv * (dim // nh)
+    weights = 4 * (V * dim + L * (2 * dim + 2 * dim * dim + 2 * kvd * dim + 3 * hidden * dim) + dim)
+    kv = 4 * (2 * L * (pos + 1) * kvd + 2 * L * kvd)
+    return weights + kv + 4 * dim
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    import oracle
+    cfg = synth.CONFIGS[MODEL]
+    blob = synth.make_blob(cfg)
+    prompt = synth.make_prompt(cfg[5], N_PROMPT)
+    impl = "reference" if oracle.ref_available() else "port"
+    m = oracle.Model(blob, impl=impl)
+    sample = 24   # positions per step: a bounded sample of the 1024-position decode
+    for _ in range(args.warmup):
+        m.decode_greedy(prompt, sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.decode_greedy(prompt, sample)
+    dt = time.perf_counter() - t0
+    v = sample * args.steps / dt
+    line = {
+        "metric": METRIC, "value": v, "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{MODEL} batch-1 greedy decode", "positions_per_step": sample,
+                   "prompt": N_PROMPT, "parallelism": "cpu-1thread"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": impl,
+                         "sample": f"first {sample} positions of the seeded 110M decode per step"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline_sample(blob, prompt):
+    import oracle
+    impl = "reference" if oracle.ref_available() else "port"
+    m = oracle.Model(blob, impl=impl)
+    n = 96
+    t0 = time.perf_counter()
+    m.decode_greedy(prompt, n)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": 1, "kind": impl,
+            "sample": f"positions 0..{n - 1} of the seeded 110M greedy decode, single thread"}
+
+
+def run_single(args):
+    import ctypes as C
+    import pitorch_b200
+    from pitorch_b200 import api
+    L = pitorch_b200.lib()
+    cfg = synth.CONFIGS[MODEL]
+    dim, hidden, nl, nh, nkv, V, seq = cfg
+    blob = synth.make_blob(cfg)
+    prompt = synth.make_prompt(V, N_PROMPT)
+    ctx = api.Context(blob)
+    dec = ctx.ptc_decoder()
+    pctx = ctx.ptc_ctx()
+    timer = L.ptc_timer_create(pctx)
+
+    def device_run(n_steps):
+        for _ in range(n_steps):
+            L.ptc_decoder_reset(dec)
+            L.ptc_decoder_generate_begin(dec, api.ip(prompt), N_PROMPT)
+            L.ptc_decoder_enqueue_steps(dec, seq)
+
+    # warm-up (also checks the stream against the host path below)
+    for _ in range(args.warmup):
+        device_run(1)
+    L.ptc_sync(pctx)
+    toks_dev = np.zeros(seq, np.int32)
+    L.ptc_decoder_read_tokens(dec, api.ip(toks_dev), seq)
+
+    # ---- device-resident timed region (CUDA events on the decode stream) ----
+    # Per-step resets/prompt loads are part of each step (tiny H2D copies).
+    L.ptc_sync(pctx)
+    with ClockSampler(0) as clk:
+        ms_total = 0.0
+        for _ in range(args.steps):
+            L.ptc_decoder_reset(dec)
+            L.ptc_decoder_generate_begin(dec, api.ip(prompt), N_PROMPT)
+            L.ptc_timer_start(timer)
+            L.ptc_decoder_enqueue_steps(dec, seq)
+            L.ptc_timer_stop(timer)
+            ms_total += L.ptc_timer_ms(timer)
+    ms_per_step = ms_total / args.steps
+    value = seq / (ms_per_step / 1000.0)
+
+    # ---- e2e through pt_forward_step (host token in / host token out) -------
+    ctx.ctx.sync_logits = 0
+    e2e_steps = max(1, min(args.steps, 3))
+    L.ptc_sync(pctx)
+    t0 = time.perf_counter()
+    L.ptc_timer_start(timer)
+    toks_host = None
+    for _ in range(e2e_steps):
+        toks_host = ctx.decode_greedy(prompt, seq)
+    L.ptc_timer_stop(timer)
+    e2e_ms = L.ptc_timer_ms(timer) / e2e_steps
+    e2e_wall_ms = 1000 * (time.perf_counter() - t0) / e2e_steps
+    e2e_value = seq / (e2e_ms / 1000.0)
+    streams_match = bool(np.array_equal(toks_host, toks_dev))
+
+    # ---- roofline of the dominant kernel: the classifier (k_cls) ------------
+    n_cls = 50
+    L.ptc_sync(pctx)
+    L.ptc_timer_start(timer)
+    for _ in range(n_cls):
+        L.ptc_decoder_enqueue_head(dec)
+    L.ptc_timer_stop(timer)
+    cls_ms = L.ptc_timer_ms(timer) / n_cls
+    cls_bytes = 4 * (V * dim + V + 2 * dim)
+    hbm, src = peaks()
+    cls_gbs = cls_bytes / (cls_ms / 1000.0) / 1e9
+
+    # whole-step roofline (bytes per token over the decode)
+    mean_bytes = np.mean([decode_bytes_per_token(cfg, p) for p in range(seq)])
+    step_gbs = mean_bytes * seq / (ms_per_step / 1000.0) / 1e9
+
+    L.ptc_timer_destroy(timer)
+    ctx.close()
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02) fp32 weights, seeded 8-token prompt)",
+        "config": {"workload": f"{MODEL} batch-1 greedy decode, {seq} positions per step",
+                   "model": MODEL, "global_batch": 1, "seq_len": seq, "parallelism": "none",
+                   "l2_policy": "weights 438 MB > 126 MB L2: every token re-streams from HBM"},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "api": "pt_forward_step per position",
+                "h2d_bytes_per_step": 8 * seq, "d2h_bytes_per_step": 4 * seq,
+                "wall_ms_per_step": e2e_wall_ms, "token_stream_equals_device_loop": streams_match},
+        "roofline": {"kernel": "k_cls (final rmsnorm + 32000x768 classifier matvec + argmax)",
+                     "bound": "hbm", "achieved": cls_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": cls_gbs / hbm, "peak_source": f"{src} hbm_gbs",
+                     "traffic": None, "bytes_per_launch": cls_bytes, "ms_per_launch": cls_ms},
+        "step_roofline": {"bytes_per_token": float(mean_bytes), "achieved": step_gbs, "peak": hbm,
+                          "unit": "GB/s", "frac": step_gbs / hbm,
+                          "roofline_tokens_per_s": hbm * 1e9 / mean_bytes},
+        "gpu_launches": args.steps * seq * (5 * nl + 1),
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(blob, prompt)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    if world > 1 or args.gpus > 1:
+        from pitorch_b200 import pipeline_bench
+        return pipeline_bench.run(args, rank, world)
+    return run_single(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

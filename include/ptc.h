@@ -1,0 +1,165 @@
+/*
+ * ptc.h -- the thin C ABI between pitorch_b200's C host layer and its
+ * sm_100a CUDA kernels. Plain pointers, ints and sizes only; no CUDA or
+ * C++ types cross it (streams are passed as void *).
+ *
+ * The pitorch-compatible API (pt.h, llama2.h, pt_train.h, pt_shard.h,
+ * pt_text.h, pt_dist_pipeline.h) is implemented in C on top of these calls.
+ * Each entry point names the reference interface it replaces.
+ *
+ * Error convention: CUDA failures print the call site and abort(), the host
+ * analogue of the reference's panic() (pitorch/runtime/gpu.c:107-108). Only
+ * the communication waits return an error code (-1), as the reference's
+ * recv_raw does on timeout (pitorch/dist/transport/pt_link_gpio.c:134-136).
+ */
+#ifndef PTC_H
+#define PTC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- runtime: replaces pitorch/runtime/{gpu.c,arena.c} ------------------ */
+
+typedef struct ptc_ctx ptc_ctx;
+
+/* Number of CUDA devices visible to this process. */
+int ptc_device_count(void);
+
+/* Open a context on `device`: its own stream and ONE device arena of
+ * `arena_bytes` (bump-allocated, 256-byte aligned), replacing
+ * qpu_enable + gpu_arena_init (pitorch/runtime/gpu.c:75-103, arena.c:10-16).
+ * arena_bytes == 0 picks a size large enough for the caller's later
+ * requests (the arena then grows in chunks instead). */
+ptc_ctx *ptc_create(int device, size_t arena_bytes);
+void ptc_destroy(ptc_ctx *c);
+
+/* Bump allocation from the arena (gpu_arena_alloc, arena.c:18-26). */
+void *ptc_alloc(ptc_ctx *c, size_t bytes);
+/* Arena high-water mark and reset to a mark (gpu_arena_reset, arena.c:28-31). */
+size_t ptc_arena_used(const ptc_ctx *c);
+void ptc_arena_reset(ptc_ctx *c, size_t mark);
+
+void *ptc_stream(ptc_ctx *c);
+int ptc_device(const ptc_ctx *c);
+int ptc_sm_count(const ptc_ctx *c);
+void ptc_sync(ptc_ctx *c);
+void ptc_h2d(ptc_ctx *c, void *dst, const void *src, size_t bytes);
+void ptc_d2h(ptc_ctx *c, void *dst, const void *src, size_t bytes);
+void ptc_d2d(ptc_ctx *c, void *dst, const void *src, size_t bytes);
+void ptc_memset(ptc_ctx *c, void *dst, int value, size_t bytes);
+
+/* Page-locked host buffers for the staged copies of the drop-in paths. */
+void *ptc_host_alloc(size_t bytes);
+void ptc_host_free(void *p);
+
+/* Upload a llama2.c .bin image (or a SHRD shard) into the arena so that the
+ * first tensor (at byte offset `header_bytes`) starts 256-byte aligned.
+ * Returns the device address of byte 0 of the image. The host keeps the
+ * mapping host_base -> device_base (pitorch/pt.c:56-58 points pt_weights_t
+ * into the caller's blob; the device copy keeps the same offsets). */
+void *ptc_upload_image(ptc_ctx *c, const void *image, size_t bytes, size_t header_bytes);
+
+/* ---- matvec: replaces smatvec_tmu (pitorch/ops/matvec/matvec.c:13-86) ---- */
+
+/* y = W . x, W row-major [rows, cols], all DEVICE pointers, on `stream`
+ * (NULL = legacy default stream). Any shape; 128-bit path when cols % 4 == 0
+ * and W/x are 16-byte aligned. Asynchronous. */
+void ptc_matvec(const float *W, const float *x, float *y, int rows, int cols, void *stream);
+
+/* Same contract as pitorch's pt_matvec_fn callback (llama2.h:74-75) and the
+ * Pi's matvec_gpu wrapper (pt.c:21-25): HOST pointers, synchronous. W is
+ * looked up among images uploaded with ptc_upload_image (and the registered
+ * transposed-weight scratch); an unknown W is staged to the device first.
+ * x is staged in, y copied back. */
+void ptc_matvec_host(const float *W, const float *x, float *y, int rows, int cols);
+
+/* Register / unregister a host range whose device copy ptc_matvec_host may
+ * use instead of staging (the host-base -> device-base map). */
+void ptc_register_range(const void *host, const void *dev, size_t bytes, ptc_ctx *owner);
+void ptc_unregister_ctx(ptc_ctx *owner);
+
+/* ---- decode: replaces pt_forward / pt_forward_layers_range /
+ *      pt_forward_head + argmax (pitorch/model/llama2.c:220-303,
+ *      pitorch/pt.c:267-271) ---------------------------------------------- */
+
+typedef struct ptc_decoder ptc_decoder;
+
+/* Model shape, same field order as pt_config_t (llama2.h:10-18). */
+typedef struct {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len;
+} ptc_config;
+
+/* DEVICE weight pointers, same field order as pt_weights_t (llama2.h:20-33).
+ * Per-layer tensors hold `n_layers` (local) layers; absent parts are NULL. */
+typedef struct {
+    const float *token_embedding, *rms_att_weight, *wq, *wk, *wv, *wo,
+        *rms_ffn_weight, *w1, *w2, *w3, *rms_final_weight, *wcls;
+} ptc_weights;
+
+/* A decoder owns the decode state (residual x, q, attention output, FFN
+ * hidden, logits, KV cache [L][n_kv][seq][hd]) and two captured CUDA graphs
+ * of one position: layers [0, n_layers) of `w`, preceded by the embedding
+ * lookup when has_embed and followed by the head (final rmsnorm, classifier,
+ * argmax) when has_head. */
+ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, const ptc_weights *w,
+                                int has_embed, int has_head);
+void ptc_decoder_destroy(ptc_decoder *d);
+
+/* Zero the KV cache (pt_reset_kv, pitorch/pt.c:273-280). */
+void ptc_decoder_reset(ptc_decoder *d);
+
+/* One position. Input: `token` when has_embed, else the residual stream
+ * previously set with ptc_decoder_set_x. Returns the argmax token when
+ * has_head (else -1). If logits_host is non-NULL the vocab logits are
+ * copied there. Synchronous. */
+int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logits_host);
+
+/* Residual stream access (the [pos | x] hand-off of the pipeline,
+ * pitorch/dist/pt_dist_pipeline.c:296-357). */
+void ptc_decoder_set_x(ptc_decoder *d, const float *x_host);
+void ptc_decoder_get_x(ptc_decoder *d, float *x_host);
+/* Final-normalised x left by the head (pt_forward_head normalises s->x in
+ * place, llama2.c:293). */
+void ptc_decoder_get_xnorm(ptc_decoder *d, float *x_host);
+float *ptc_decoder_x_dev(ptc_decoder *d);
+float *ptc_decoder_logits_dev(ptc_decoder *d);
+
+/* Staged pieces, enqueued on the context stream without synchronising
+ * (pt_forward_embed / pt_forward_layers_range / pt_forward_head,
+ * llama2.c:220-295). Layer indices are local to the decoder's weights.
+ * ptc_decoder_fetch_next synchronises and returns the last head's argmax. */
+void ptc_decoder_enqueue_embed(ptc_decoder *d, int token);
+void ptc_decoder_enqueue_layers(ptc_decoder *d, int pos, int l_start, int l_end);
+void ptc_decoder_enqueue_head(ptc_decoder *d);
+int ptc_decoder_fetch_next(ptc_decoder *d, float *logits_host);
+
+/* Device-resident greedy decode of positions [0, n_pos): prompt tokens are
+ * teacher-forced, then argmax feeds back on the device (no host round
+ * trip per token). out_tokens[p] = token emitted at position p (host). */
+void ptc_decoder_generate(ptc_decoder *d, const int *prompt, int n_prompt, int n_pos,
+                          int *out_tokens);
+
+/* Benchmark hooks: enqueue the device-loop step graph n times without
+ * synchronising (inputs already resident), and time it with CUDA events on
+ * the decoder's stream. ptc_decoder_generate_begin loads the prompt and
+ * resets position 0. */
+void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, int n_prompt);
+void ptc_decoder_enqueue_steps(ptc_decoder *d, int n);
+void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n);
+
+/* ---- CUDA event timing on a context's stream ----------------------------- */
+typedef struct ptc_timer ptc_timer;
+ptc_timer *ptc_timer_create(ptc_ctx *c);
+void ptc_timer_start(ptc_timer *t);
+void ptc_timer_stop(ptc_timer *t);
+float ptc_timer_ms(ptc_timer *t);     /* synchronises on the stop event */
+void ptc_timer_destroy(ptc_timer *t);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,198 @@
+// ptc_common.cuh -- shared device helpers for the sm_100a kernels.
+//
+// * Error handling: a failed CUDA call in the product path prints the call
+//   site and aborts, the host analogue of the reference's panic()
+//   (pitorch/runtime/gpu.c:107-108, pitorch/pt.c:50-54).
+// * pitorch's libm-free math (pitorch/ops/core/pt_math.c) restated for the
+//   device with explicitly rounded multiplies/adds (__fmul_rn/__fadd_rn),
+//   so nvcc cannot contract them into FMAs and every result carries the
+//   same bits as the host C build. RoPE angles at positions up to 1023 are
+//   sensitive to this.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+
+#define PTC_CHECK(call)                                                        \
+    do {                                                                       \
+        cudaError_t e_ = (call);                                               \
+        if (e_ != cudaSuccess) {                                               \
+            fprintf(stderr, "pitorch_b200: CUDA error %s (%s) at %s:%d: %s\n", \
+                    cudaGetErrorName(e_), cudaGetErrorString(e_), __FILE__,    \
+                    __LINE__, #call);                                          \
+            abort();                                                           \
+        }                                                                      \
+    } while (0)
+
+#define PTC_FATAL(...)                                        \
+    do {                                                      \
+        fprintf(stderr, "pitorch_b200: fatal: " __VA_ARGS__); \
+        fputc('\n', stderr);                                  \
+        abort();                                              \
+    } while (0)
+
+namespace ptc {
+
+// ---------------------------------------------------------------------------
+// pitorch math on the device (pt_math.c), bit-compatible with the host build.
+// ---------------------------------------------------------------------------
+
+// pt_math.c:8-25
+__device__ __forceinline__ float pt_expf(float x) {
+    if (x > 88.7f) return 3.4028235e+38f;
+    if (x < -87.3f) return 0.0f;
+    float t = __fmul_rn(x, 1.4426950408889634f);
+    int n = __float2int_rz(__fadd_rn(t, t >= 0.0f ? 0.5f : -0.5f));
+    float r = __fsub_rn(x, __fmul_rn((float)n, 0.6931471805599453f));
+    float p = 0.0083333333f;
+    p = __fadd_rn(0.0416666667f, __fmul_rn(r, p));
+    p = __fadd_rn(0.1666666667f, __fmul_rn(r, p));
+    p = __fadd_rn(0.5f, __fmul_rn(r, p));
+    p = __fadd_rn(1.0f, __fmul_rn(r, p));
+    p = __fadd_rn(1.0f, __fmul_rn(r, p));
+    return __fmul_rn(p, __int_as_float((n + 127) << 23));
+}
+
+// pt_math.c:31-44
+__device__ __forceinline__ float pt_logf(float x) {
+    if (x <= 0.0f) return -3.4028235e+38f;
+    uint32_t u = __float_as_uint(x);
+    int e = (int)((u >> 23) & 0xFF) - 127;
+    float m = __uint_as_float((u & 0x007FFFFFu) | 0x3F800000u);
+    if (m > 1.41421356f) { m = __fmul_rn(m, 0.5f); e++; }
+    float f = __fsub_rn(m, 1.0f);
+    float s = 0.11111111f;
+    s = __fadd_rn(-0.125f, __fmul_rn(f, s));
+    s = __fadd_rn(0.14285714f, __fmul_rn(f, s));
+    s = __fadd_rn(-0.16666667f, __fmul_rn(f, s));
+    s = __fadd_rn(0.2f, __fmul_rn(f, s));
+    s = __fadd_rn(-0.25f, __fmul_rn(f, s));
+    s = __fadd_rn(0.33333333f, __fmul_rn(f, s));
+    s = __fadd_rn(-0.5f, __fmul_rn(f, s));
+    s = __fadd_rn(1.0f, __fmul_rn(f, s));
+    return __fadd_rn(__fmul_rn(f, s), __fmul_rn((float)e, 0.69314718f));
+}
+
+// pt_math.c:58-62
+__device__ __forceinline__ float pt_reduce_2pi(float x) {
+    float k = __fmul_rn(x, 0.15915494309190f);
+    k = (float)__float2int_rz(__fadd_rn(k, k >= 0.0f ? 0.5f : -0.5f));
+    return __fsub_rn(x, __fmul_rn(k, 6.28318530717959f));
+}
+
+// pt_math.c:64-74
+__device__ __forceinline__ float pt_sinf(float x) {
+    x = pt_reduce_2pi(x);
+    if (x > 1.57079632679490f) x = __fsub_rn(3.14159265358979f, x);
+    else if (x < -1.57079632679490f) x = __fsub_rn(-3.14159265358979f, x);
+    float z = __fmul_rn(x, x);
+    float s = 0.00000275573f;
+    s = __fadd_rn(-0.00019841270f, __fmul_rn(z, s));
+    s = __fadd_rn(0.00833333333f, __fmul_rn(z, s));
+    s = __fadd_rn(-0.16666666667f, __fmul_rn(z, s));
+    s = __fadd_rn(1.0f, __fmul_rn(z, s));
+    return __fmul_rn(x, s);
+}
+
+// pt_math.c:76-87
+__device__ __forceinline__ float pt_cosf(float x) {
+    x = pt_reduce_2pi(x);
+    float sign = 1.0f;
+    if (x > 1.57079632679490f) { x = __fsub_rn(3.14159265358979f, x); sign = -1.0f; }
+    else if (x < -1.57079632679490f) { x = __fsub_rn(-3.14159265358979f, x); sign = -1.0f; }
+    float z = __fmul_rn(x, x);
+    float c = 0.00002480159f;
+    c = __fadd_rn(-0.00138888889f, __fmul_rn(z, c));
+    c = __fadd_rn(0.04166666667f, __fmul_rn(z, c));
+    c = __fadd_rn(-0.50000000000f, __fmul_rn(z, c));
+    c = __fadd_rn(1.0f, __fmul_rn(z, c));
+    return __fmul_rn(sign, c);
+}
+
+// pt_math.c:92-102 (IEEE division: the library is built without fast math)
+__device__ __forceinline__ float pt_sqrtf(float x) {
+    if (x <= 0.0f) return 0.0f;
+    float y = __uint_as_float(0x1fbd1df5u + (__float_as_uint(x) >> 1));
+    for (int i = 0; i < 3; i++) y = __fmul_rn(0.5f, __fadd_rn(y, __fdiv_rn(x, y)));
+    return y;
+}
+
+// 1 / pt_sqrtf(sum_sq / dim + 1e-5), the rmsnorm scale of pt_ops.c:9.
+__device__ __forceinline__ float rms_scale(float sum_sq, int dim) {
+    return __fdiv_rn(1.0f, pt_sqrtf(__fadd_rn(__fdiv_rn(sum_sq, (float)dim), 1e-5f)));
+}
+
+// The RoPE rotation angle of pt_ops.c:36-37 for even index i.
+__device__ __forceinline__ float rope_theta(int i, int head_dim, int pos) {
+    float e = __fdiv_rn(__fmul_rn(-9.210340372f, (float)(i % head_dim)), (float)head_dim);
+    return __fmul_rn((float)pos, pt_expf(e));
+}
+
+// silu(a) * b as pitorch computes it: a / (1 + exp(-a)), then times b
+// (pt_ops.c:28-31 followed by vec_mul, pt_ops.c:56-59).
+__device__ __forceinline__ float silu_mul(float a, float b) {
+    return __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, pt_expf(-a))), b);
+}
+
+// ---------------------------------------------------------------------------
+// Warp helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Streaming 128-bit load of weights: read-only path, no L1 allocation
+// (weights are touched once per token).
+__device__ __forceinline__ float4 ldg_stream(const float4 *p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    acc = fmaf(a.w, b.w, acc);
+    return acc;
+}
+
+// Programmatic dependent launch (sm_90+): wait for the producer grid's
+// memory, and let the next grid in the stream start its prologue early.
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Order-preserving map of a float to uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t float_key(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Argmax key: value in the high word, inverted index in the low word, so the
+// 64-bit max picks the largest value and, among equals, the lowest index --
+// the strict '>' scan of pt_ops.c:65-70.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    return ((unsigned long long)float_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+    return (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+}
+
+}  // namespace ptc

@@ -1,0 +1,48 @@
+// ptc_decode.cuh -- device-side data layout of one decode context.
+#pragma once
+
+#include <stdint.h>
+
+namespace ptc {
+
+// Per-step control block, resident in device memory. The decode kernels read
+// the position and input token from here, and the classifier kernel's last
+// CTA writes the argmax and (in device-loop mode) advances the position, so
+// a whole greedy decode can run without host round trips.
+struct StepState {
+    int pos;                  // position being decoded
+    int tok;                  // input token at pos
+    int next;                 // argmax of this step's logits
+    int n_prompt;             // device-loop mode: prompt length
+    int mode;                 // 0: host drives pos/tok; 1: device loop
+    int pad0;
+    unsigned done;            // classifier CTAs finished (reset by the last)
+    unsigned pad1;
+    unsigned long long amax;  // packed (value, index) running argmax
+    int *tokens;              // device-loop mode: token stream [seq]
+};
+
+// Everything the decode kernels need for one model replica.
+struct DecodeModel {
+    int dim, hidden, L, nh, nkv, V, seq, hd, kvd;
+    // weights, device pointers into the uploaded .bin image
+    const float *emb, *rms_att, *wq, *wk, *wv, *wo, *rms_ffn, *w1, *w2, *w3,
+        *rms_final, *wcls;
+    // activations
+    float *x;        // [dim] residual stream
+    float *xn;       // [dim] final-normalised x (pt_forward_head's in-place rmsnorm)
+    float *q;        // [dim] post-RoPE query
+    float *att;      // [dim] attention output (input of wo)
+    float *hb;       // [hidden] silu(w1 x) * (w3 x)
+    float *logits;   // [V]
+    // KV cache, head-major: [L][nkv][seq][hd]
+    float *kc, *vc;
+    // attention split-K partials: [nh][n_chunks][hd + 2] and per-head tickets
+    float *att_part;
+    unsigned *att_ticket;
+    int att_chunk;   // positions per attention CTA
+    int n_chunks;    // ceil(seq / att_chunk)
+    StepState *step;
+};
+
+}  // namespace ptc

@@ -1,0 +1,283 @@
+// ptc_decoder.cu -- decode state and the captured CUDA graphs of one
+// position (host side of the decode kernels).
+//
+// Two graphs are captured per decoder, both built from the same PDL-chained
+// kernels (ptc_decode_kernels.cu):
+//   host graph:   [copy {pos, token} from pinned memory] -> kernels ->
+//                 [copy argmax to pinned memory]   (pt_forward_step path)
+//   device graph: kernels only; position and token advance on the device,
+//                 so a whole greedy decode is a chain of graph launches.
+#include <string.h>
+
+#include "../../include/ptc.h"
+#include "ptc_common.cuh"
+#include "ptc_decode.cuh"
+#include "ptc_internal.h"
+
+using ptc::DecodeModel;
+using ptc::StepState;
+
+struct HostIO {
+    int pos;
+    int tok;
+    int next;
+    int pad;
+};
+
+struct ptc_decoder {
+    ptc_ctx *ctx;
+    cudaStream_t stream;
+    DecodeModel m;
+    int has_embed, has_head, n_sm;
+    HostIO *io;            // pinned
+    float *stage;          // pinned staging for logits / x
+    int *d_tokens;         // [seq + 1]
+    int mode;              // current StepState.mode on the device
+    cudaGraphExec_t g_host, g_dev;
+};
+
+static bool pdl_enabled() {
+    const char *e = getenv("PTC_NO_PDL");
+    return !(e && e[0] == '1');
+}
+
+static void enqueue_kernels(ptc_decoder *d, cudaStream_t s) {
+    const DecodeModel &m = d->m;
+    if (d->has_embed && m.L == 0) ptc::launch_embed(m, s);
+    for (int l = 0; l < m.L; l++) ptc::launch_layer(m, l, d->has_embed && l == 0, s);
+    if (d->has_head) ptc::launch_head(m, d->n_sm, s);
+}
+
+static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
+    cudaStream_t s = d->stream;
+    cudaGraph_t g;
+    PTC_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    if (host_io)
+        PTC_CHECK(cudaMemcpyAsync(d->m.step, d->io, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
+    enqueue_kernels(d, s);
+    if (host_io && d->has_head)
+        PTC_CHECK(cudaMemcpyAsync(&d->io->next, &d->m.step->next, sizeof(int), cudaMemcpyDeviceToHost, s));
+    PTC_CHECK(cudaStreamEndCapture(s, &g));
+    cudaGraphExec_t ge;
+    PTC_CHECK(cudaGraphInstantiate(&ge, g, 0));
+    PTC_CHECK(cudaGraphDestroy(g));
+    return ge;
+}
+
+static void set_mode(ptc_decoder *d, int mode) {
+    if (d->mode == mode) return;
+    PTC_CHECK(cudaMemcpyAsync(&d->m.step->mode, &mode, sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    d->mode = mode;
+}
+
+extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, const ptc_weights *w,
+                                           int has_embed, int has_head) {
+    PTC_CHECK(cudaSetDevice(ptc_device(c)));
+    ptc_decoder *d = new ptc_decoder();
+    memset(&d->m, 0, sizeof(d->m));
+    d->ctx = c;
+    d->stream = ptc_ctx_stream(c);
+    d->has_embed = has_embed;
+    d->has_head = has_head;
+    d->n_sm = ptc_sm_count(c);
+    DecodeModel &m = d->m;
+    m.dim = cfg->dim;
+    m.hidden = cfg->hidden_dim;
+    m.L = cfg->n_layers;
+    m.nh = cfg->n_heads;
+    m.nkv = cfg->n_kv_heads;
+    m.V = cfg->vocab_size;
+    m.seq = cfg->seq_len;
+    m.hd = m.dim / m.nh;
+    m.kvd = m.nkv * m.hd;
+    if (m.dim % 4 || m.hidden % 4 || m.hd % 2)
+        PTC_FATAL("decode needs dim, hidden_dim multiples of 4 and an even head_dim (got %d, %d, %d)",
+                  m.dim, m.hidden, m.hd);
+    if (m.dim > 2048 || m.hidden > 2048) PTC_FATAL("decode supports dim, hidden_dim <= 2048");
+    if (m.nh % m.nkv) PTC_FATAL("n_heads must be a multiple of n_kv_heads");
+    m.emb = w->token_embedding;
+    m.rms_att = w->rms_att_weight;
+    m.wq = w->wq;
+    m.wk = w->wk;
+    m.wv = w->wv;
+    m.wo = w->wo;
+    m.rms_ffn = w->rms_ffn_weight;
+    m.w1 = w->w1;
+    m.w2 = w->w2;
+    m.w3 = w->w3;
+    m.rms_final = w->rms_final_weight;
+    m.wcls = w->wcls;
+    if (has_embed && !m.emb) PTC_FATAL("decoder with embedding but no token_embedding");
+    if (has_head && (!m.wcls || !m.rms_final)) PTC_FATAL("decoder with head but no classifier");
+
+    m.x = (float *)ptc_alloc(c, m.dim * 4);
+    m.xn = (float *)ptc_alloc(c, m.dim * 4);
+    m.q = (float *)ptc_alloc(c, m.dim * 4);
+    m.att = (float *)ptc_alloc(c, m.dim * 4);
+    m.hb = (float *)ptc_alloc(c, (size_t)m.hidden * 4);
+    m.logits = (float *)ptc_alloc(c, (size_t)m.V * 4);
+    size_t kv = (size_t)m.L * m.seq * m.kvd * 4;
+    m.kc = (float *)ptc_alloc(c, kv ? kv : 4);
+    m.vc = (float *)ptc_alloc(c, kv ? kv : 4);
+    m.att_chunk = 32;
+    if (!ptc::decode_attn_limits_ok(m.hd, m.att_chunk)) PTC_FATAL("head_dim %d too large", m.hd);
+    m.n_chunks = (m.seq + m.att_chunk - 1) / m.att_chunk;
+    m.att_part = (float *)ptc_alloc(c, (size_t)m.nh * m.n_chunks * (m.hd + 2) * 4);
+    m.att_ticket = (unsigned *)ptc_alloc(c, (size_t)m.nh * 4);
+    m.step = (StepState *)ptc_alloc(c, sizeof(StepState));
+    d->d_tokens = (int *)ptc_alloc(c, (size_t)(m.seq + 1) * 4);
+
+    cudaStream_t s = d->stream;
+    PTC_CHECK(cudaMemsetAsync(m.x, 0, m.dim * 4, s));
+    PTC_CHECK(cudaMemsetAsync(m.kc, 0, kv ? kv : 4, s));
+    PTC_CHECK(cudaMemsetAsync(m.vc, 0, kv ? kv : 4, s));
+    PTC_CHECK(cudaMemsetAsync(m.att_ticket, 0, (size_t)m.nh * 4, s));
+    StepState st;
+    memset(&st, 0, sizeof(st));
+    st.tokens = d->d_tokens;
+    PTC_CHECK(cudaMemcpyAsync(m.step, &st, sizeof(st), cudaMemcpyHostToDevice, s));
+    PTC_CHECK(cudaStreamSynchronize(s));
+    d->mode = 0;
+
+    d->io = (HostIO *)ptc_host_alloc(sizeof(HostIO));
+    memset(d->io, 0, sizeof(HostIO));
+    size_t stage = (size_t)(m.V > m.dim ? m.V : m.dim) * 4;
+    d->stage = (float *)ptc_host_alloc(stage);
+
+    d->g_host = capture(d, true);
+    d->g_dev = capture(d, false);
+    (void)pdl_enabled;
+    return d;
+}
+
+extern "C" void ptc_decoder_destroy(ptc_decoder *d) {
+    if (!d) return;
+    cudaStreamSynchronize(d->stream);
+    cudaGraphExecDestroy(d->g_host);
+    cudaGraphExecDestroy(d->g_dev);
+    ptc_host_free(d->io);
+    ptc_host_free(d->stage);
+    delete d;  // device buffers belong to the context arena
+}
+
+extern "C" void ptc_decoder_reset(ptc_decoder *d) {
+    size_t kv = (size_t)d->m.L * d->m.seq * d->m.kvd * 4;
+    if (kv) {
+        PTC_CHECK(cudaMemsetAsync(d->m.kc, 0, kv, d->stream));
+        PTC_CHECK(cudaMemsetAsync(d->m.vc, 0, kv, d->stream));
+    }
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+}
+
+extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logits_host) {
+    if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
+    if (d->has_embed && (token < 0 || token >= d->m.V))
+        PTC_FATAL("token %d outside [0, %d)", token, d->m.V);
+    set_mode(d, 0);
+    d->io->pos = pos;
+    d->io->tok = token;
+    PTC_CHECK(cudaGraphLaunch(d->g_host, d->stream));
+    if (logits_host && d->has_head) {
+        PTC_CHECK(cudaMemcpyAsync(d->stage, d->m.logits, (size_t)d->m.V * 4, cudaMemcpyDeviceToHost,
+                                  d->stream));
+        PTC_CHECK(cudaStreamSynchronize(d->stream));
+        memcpy(logits_host, d->stage, (size_t)d->m.V * 4);
+    } else {
+        PTC_CHECK(cudaStreamSynchronize(d->stream));
+    }
+    return d->has_head ? d->io->next : -1;
+}
+
+extern "C" void ptc_decoder_set_x(ptc_decoder *d, const float *x_host) {
+    memcpy(d->stage, x_host, (size_t)d->m.dim * 4);
+    PTC_CHECK(cudaMemcpyAsync(d->m.x, d->stage, (size_t)d->m.dim * 4, cudaMemcpyHostToDevice, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+}
+
+static void get_vec(ptc_decoder *d, const float *src, float *x_host) {
+    PTC_CHECK(cudaMemcpyAsync(d->stage, src, (size_t)d->m.dim * 4, cudaMemcpyDeviceToHost, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    memcpy(x_host, d->stage, (size_t)d->m.dim * 4);
+}
+
+extern "C" void ptc_decoder_get_x(ptc_decoder *d, float *x_host) { get_vec(d, d->m.x, x_host); }
+extern "C" void ptc_decoder_get_xnorm(ptc_decoder *d, float *x_host) { get_vec(d, d->m.xn, x_host); }
+extern "C" float *ptc_decoder_x_dev(ptc_decoder *d) { return d->m.x; }
+extern "C" float *ptc_decoder_logits_dev(ptc_decoder *d) { return d->m.logits; }
+
+extern "C" void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, int n_prompt) {
+    if (!d->has_embed || !d->has_head) PTC_FATAL("device-loop decode needs embedding and head");
+    if (n_prompt < 1 || n_prompt > d->m.seq) PTC_FATAL("prompt length %d outside [1, %d]", n_prompt, d->m.seq);
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= d->m.V) PTC_FATAL("prompt token %d outside [0, %d)", prompt[i], d->m.V);
+    PTC_CHECK(cudaMemcpyAsync(d->d_tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, d->stream));
+    StepState st;
+    memset(&st, 0, sizeof(st));
+    st.pos = 0;
+    st.tok = prompt[0];
+    st.n_prompt = n_prompt;
+    st.mode = 1;
+    st.tokens = d->d_tokens;
+    PTC_CHECK(cudaMemcpyAsync(d->m.step, &st, sizeof(st), cudaMemcpyHostToDevice, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    d->mode = 1;
+}
+
+extern "C" void ptc_decoder_enqueue_steps(ptc_decoder *d, int n) {
+    for (int i = 0; i < n; i++) PTC_CHECK(cudaGraphLaunch(d->g_dev, d->stream));
+}
+
+extern "C" void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n) {
+    // tokens[p + 1] is the token emitted at position p.
+    PTC_CHECK(cudaMemcpyAsync(out_tokens, d->d_tokens + 1, (size_t)n * 4, cudaMemcpyDeviceToHost, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+}
+
+extern "C" void ptc_decoder_generate(ptc_decoder *d, const int *prompt, int n_prompt, int n_pos,
+                                     int *out_tokens) {
+    if (n_pos > d->m.seq) PTC_FATAL("n_pos %d exceeds seq_len %d", n_pos, d->m.seq);
+    ptc_decoder_reset(d);
+    ptc_decoder_generate_begin(d, prompt, n_prompt);
+    ptc_decoder_enqueue_steps(d, n_pos);
+    ptc_decoder_read_tokens(d, out_tokens, n_pos);
+}
+
+// ---- staged, eager launches --------------------------------------------------
+
+static void put_step_int(ptc_decoder *d, int *field, int v) {
+    // Pageable source: the runtime reads it before returning.
+    PTC_CHECK(cudaMemcpyAsync(field, &v, sizeof(int), cudaMemcpyHostToDevice, d->stream));
+}
+
+extern "C" void ptc_decoder_enqueue_embed(ptc_decoder *d, int token) {
+    if (!d->has_embed) PTC_FATAL("decoder has no embedding");
+    if (token < 0 || token >= d->m.V) PTC_FATAL("token %d outside [0, %d)", token, d->m.V);
+    set_mode(d, 0);
+    put_step_int(d, &d->m.step->tok, token);
+    ptc::launch_embed(d->m, d->stream);
+}
+
+extern "C" void ptc_decoder_enqueue_layers(ptc_decoder *d, int pos, int l_start, int l_end) {
+    if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
+    if (l_start < 0 || l_end > d->m.L || l_start > l_end)
+        PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
+    set_mode(d, 0);
+    put_step_int(d, &d->m.step->pos, pos);
+    for (int l = l_start; l < l_end; l++) ptc::launch_layer(d->m, l, false, d->stream);
+}
+
+extern "C" void ptc_decoder_enqueue_head(ptc_decoder *d) {
+    if (!d->has_head) PTC_FATAL("decoder has no head");
+    set_mode(d, 0);
+    ptc::launch_head(d->m, d->n_sm, d->stream);
+}
+
+extern "C" int ptc_decoder_fetch_next(ptc_decoder *d, float *logits_host) {
+    PTC_CHECK(cudaMemcpyAsync(&d->io->next, &d->m.step->next, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+    if (logits_host)
+        PTC_CHECK(cudaMemcpyAsync(d->stage, d->m.logits, (size_t)d->m.V * 4, cudaMemcpyDeviceToHost, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    if (logits_host) memcpy(logits_host, d->stage, (size_t)d->m.V * 4);
+    return d->io->next;
+}

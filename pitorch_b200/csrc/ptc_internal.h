@@ -1,0 +1,27 @@
+// ptc_internal.h -- declarations shared between the CUDA translation units
+// of libpitorch_b200 (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include "../../include/ptc.h"
+
+struct ptc_chunk {
+    void *base;
+    size_t size;
+    size_t used;
+};
+
+bool ptc_lookup_range(const void *host, size_t bytes, const void **dev, ptc_ctx **owner);
+cudaStream_t ptc_ctx_stream(ptc_ctx *c);
+int ptc_ctx_device(ptc_ctx *c);
+
+namespace ptc {
+struct DecodeModel;
+void launch_layer(const DecodeModel &m, int l, bool from_embedding, cudaStream_t s);
+void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s);
+void launch_embed(const DecodeModel &m, cudaStream_t s);
+int decode_attn_limits_ok(int hd, int chunk);
+void launch_matvec(const float *W, const float *x, float *y, int rows, int cols, cudaStream_t s);
+}  // namespace ptc

@@ -1,0 +1,123 @@
+"""GPU decode parity through the pitorch C API (pt_pi_init, pt_forward_step,
+pt_reset_kv, the staged llama2.h calls and the device-loop generator).
+
+Truth is the reference's own host C on the same seeded synthetic weights and
+prompt (tests/golden/decode_*.npz) and, for per-position logits, the oracle
+restatement pinned to it. Tolerance: max|dlogit| / max|logit| <= 1e-4 per
+position; greedy token streams must be identical.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import golden, rel_err
+from pitorch_b200 import api, synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def check_stream(ctx, name, n_pos=None):
+    g = golden(f"decode_{name}.npz")
+    n = int(g["n_pos"]) if n_pos is None else n_pos
+    toks, logits = ctx.decode_greedy(g["prompt"], n, want_logits=True)
+    assert np.array_equal(toks, g["tokens"][:n]), f"token stream diverged at {np.argmax(toks != g['tokens'][:n])}"
+    for r, row in zip(g["rows"], g["logits_rows"]):
+        if r < n:
+            assert rel_err(logits[r], row) <= TOL, (name, int(r))
+    # per-position summaries of the reference logits
+    am = np.abs(logits).max(axis=1)
+    assert np.all(np.abs(am - g["logit_absmax"][:n]) <= TOL * g["logit_absmax"][:n] + 1e-7)
+    return toks, logits
+
+
+def test_tiny_decode_matches_reference(ptlib):
+    ctx = api.Context(synth.make_blob("tiny"))
+    toks, logits = check_stream(ctx, "tiny")
+    m = oracle.Model(synth.make_blob("tiny"))
+    _, ref = m.decode_greedy(golden("decode_tiny.npz")["prompt"], 64, want_logits=True)
+    for p in range(64):
+        assert rel_err(logits[p], ref[p]) <= TOL, p
+    ctx.close()
+
+
+def test_15M_decode_full_sequence(ptlib):
+    ctx = api.Context(synth.make_blob("stories15M"))
+    toks, logits = check_stream(ctx, "stories15M")
+    assert ctx.pos == 256
+    ctx.close()
+
+
+@pytest.mark.parametrize("name", ["stories42M", "stories110M"])
+def test_larger_models_decode_prefix(ptlib, name):
+    ctx = api.Context(synth.make_blob(name))
+    check_stream(ctx, name)
+    ctx.close()
+
+
+def test_device_loop_generate_equals_host_loop(ptlib):
+    g = golden("decode_stories15M.npz")
+    ctx = api.Context(synth.make_blob("stories15M"))
+    dev = ctx.generate_greedy(g["prompt"], 256)
+    assert np.array_equal(dev, g["tokens"])
+    again = ctx.generate_greedy(g["prompt"], 256)   # KV reset between runs
+    assert np.array_equal(again, dev)
+    ctx.close()
+
+
+def test_reset_kv_restarts_sequence(ptlib):
+    g = golden("decode_tiny.npz")
+    ctx = api.Context(synth.make_blob("tiny"))
+    a = ctx.decode_greedy(g["prompt"], 20)
+    b = ctx.decode_greedy(g["prompt"], 20)
+    assert np.array_equal(a, b) and ctx.pos == 20
+    ctx.close()
+
+
+def test_staged_calls_match_monolithic(ptlib):
+    """pt_forward_embed + pt_forward_layers_range (split) + pt_forward_head on a
+    pt_alloc_state state equals pt_forward (dev/host/test_stage_forward.c)."""
+    L = ptlib
+    blob = synth.make_blob("tiny")
+    buf = C.create_string_buffer(blob, len(blob))
+    cfg = api.pt_config_t()
+    w = api.pt_weights_t()
+    L.pt_load_config(C.byref(cfg), C.cast(buf, C.c_void_p))
+    L.pt_load_weights(C.byref(w), C.byref(cfg), C.cast(buf, C.c_void_p))
+    s_ref, s_stg = api.pt_state_t(), api.pt_state_t()
+    L.pt_alloc_state(C.byref(s_ref), C.byref(cfg))
+    L.pt_alloc_state(C.byref(s_stg), C.byref(cfg))
+    m = oracle.Model(blob)
+    tok_r = tok_s = 1
+    for pos in range(8):
+        L.pt_forward(C.byref(cfg), C.byref(w), C.byref(s_ref), tok_r, pos, None)
+        lr = np.ctypeslib.as_array(s_ref.logits, shape=(cfg.vocab_size,)).copy()
+        L.pt_forward_embed(C.byref(w), s_stg.x, cfg.dim, tok_s)
+        L.pt_forward_layers_range(C.byref(cfg), C.byref(w), C.byref(s_stg), pos, 0, 1, None)
+        L.pt_forward_layers_range(C.byref(cfg), C.byref(w), C.byref(s_stg), pos, 1, 2, None)
+        L.pt_forward_head(C.byref(cfg), C.byref(w), C.byref(s_stg), None)
+        ls = np.ctypeslib.as_array(s_stg.logits, shape=(cfg.vocab_size,)).copy()
+        m.forward_embed(tok_r)
+        m.forward_layers_range(pos, 0, 2)
+        m.forward_head()
+        assert rel_err(lr, m.logits()) <= TOL
+        assert rel_err(ls, lr) <= TOL
+        tok_r = tok_s = int(np.argmax(lr))
+    L.pt_free_state(C.byref(s_ref))
+    L.pt_free_state(C.byref(s_stg))
+
+
+def test_matvec_callback_is_gpu(ptlib):
+    """ctx.matvec is the GPU pt_matvec_fn (pitorch/pt.c:21-25 contract)."""
+    ctx = api.Context(synth.make_blob("tiny"))
+    fn = api.MATVEC_FN(ctx.ctx.matvec)
+    cfg = ctx.cfg
+    W = ctx.ctx.w.wq  # resident: a pointer into the uploaded image
+    x = np.random.default_rng(0).standard_normal(cfg.dim).astype(np.float32)
+    y = np.zeros(cfg.dim, np.float32)
+    fn(W, api.fp(x), api.fp(y), cfg.dim, cfg.dim)
+    Wn = np.ctypeslib.as_array(W, shape=(cfg.dim, cfg.dim)).copy()
+    assert rel_err(y, oracle.matvec(Wn, x)) <= 1e-5
+    ctx.close()
