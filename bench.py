@@ -166,6 +166,8 @@ def run_single(args):
     L = pitorch_b200.lib()
     cfg = synth.CONFIGS[MODEL]
     dim, hidden, nl, nh, nkv, V, seq = cfg
+    if args.positions:
+        seq = min(args.positions, seq)
     blob = synth.make_blob(cfg)
     prompt = synth.make_prompt(V, N_PROMPT)
     ctx = api.Context(blob)
@@ -269,6 +271,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--positions", type=int, default=0,
+                    help="decode positions per step (default: the model's seq_len, 1024)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

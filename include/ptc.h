@@ -151,6 +151,43 @@ void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, int n_prompt)
 void ptc_decoder_enqueue_steps(ptc_decoder *d, int n);
 void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n);
 
+/* ---- training: replaces pt_forward_train / pt_backward / pt_sgd_update
+ *      and their staged variants (pitorch/train/pt_train.c:171-1383) -------- */
+
+typedef struct ptc_trainer ptc_trainer;
+
+/* Device activations, backward buffers and gradients for sequences of up to
+ * max_T tokens over the `cfg.n_layers` (local) layers of `w`; the embedding
+ * and/or head parts exist when has_embed / has_head. The weights in `w` are
+ * updated in place by the SGD calls. Gradients use the reference layout
+ * (pitorch/train/pt_train.c:334-371) for the owned parts. */
+ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, const ptc_weights *w,
+                                int max_T, int has_embed, int has_head);
+void ptc_trainer_destroy(ptc_trainer *t);
+
+/* zero_grads -> forward -> backward -> SGD; returns the loss (pt.c:339-364). */
+float ptc_trainer_step(ptc_trainer *t, const int *tokens, int T, float lr);
+
+/* Staged pieces (enqueue only, except fwd_head which returns the loss). */
+void ptc_trainer_set_tokens(ptc_trainer *t, const int *tokens, int T);
+void ptc_trainer_zero_grads(ptc_trainer *t);
+void ptc_trainer_fwd_embed(ptc_trainer *t);
+void ptc_trainer_fwd_layers(ptc_trainer *t, int l_start, int l_end);
+float ptc_trainer_fwd_head(ptc_trainer *t);
+void ptc_trainer_bwd_head(ptc_trainer *t);
+void ptc_trainer_bwd_layers(ptc_trainer *t, int l_start, int l_end);
+void ptc_trainer_bwd_embed(ptc_trainer *t);
+void ptc_trainer_sgd_layers(ptc_trainer *t, float lr, int l_start, int l_end);
+void ptc_trainer_sgd_head(ptc_trainer *t, float lr);
+void ptc_trainer_sync(ptc_trainer *t);
+
+/* Device buffers: gradients (n_params floats), residual stream entering
+ * layer l ([T, dim]), and the residual gradient d_res ([T, dim]). */
+size_t ptc_trainer_n_params(ptc_trainer *t);
+float *ptc_trainer_grads(ptc_trainer *t);
+float *ptc_trainer_residual(ptc_trainer *t, int l);
+float *ptc_trainer_dres(ptc_trainer *t);
+
 /* ---- CUDA event timing on a context's stream ----------------------------- */
 typedef struct ptc_timer ptc_timer;
 ptc_timer *ptc_timer_create(ptc_ctx *c);

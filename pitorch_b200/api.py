@@ -111,6 +111,19 @@ def declare(L):
     _sig(L, "pt_load_shard_header", None, P(pt_config_t), P(pt_shard_info_t), C.c_void_p)
     _sig(L, "pt_shard_file_size", C.c_uint, C.c_void_p)
     _sig(L, "pt_make_shard", C.c_ulong, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_ulong)
+    acts, grads, bb, cfgp, wp = P(pt_activations_t), P(pt_grads_t), P(pt_backward_buf_t), P(pt_config_t), P(pt_weights_t)
+    _sig(L, "pt_zero_grads", None, grads)
+    _sig(L, "pt_forward_train", C.c_float, cfgp, wp, acts, i32p, C.c_int, vp, vp)
+    _sig(L, "pt_backward", None, cfgp, wp, grads, acts, bb, i32p, C.c_int, vp, vp)
+    _sig(L, "pt_sgd_update", None, wp, grads, C.c_float, cfgp)
+    _sig(L, "pt_sgd_update_layers", None, wp, grads, C.c_float, cfgp, C.c_int, C.c_int)
+    _sig(L, "pt_sgd_update_head", None, wp, grads, C.c_float, cfgp)
+    _sig(L, "pt_forward_train_embed", None, wp, acts, i32p, C.c_int, C.c_int)
+    _sig(L, "pt_forward_train_layers_range", None, cfgp, wp, acts, C.c_int, C.c_int, C.c_int, vp, vp)
+    _sig(L, "pt_forward_train_head", C.c_float, cfgp, wp, acts, i32p, C.c_int, vp, vp)
+    _sig(L, "pt_backward_head", None, cfgp, wp, grads, acts, bb, i32p, C.c_int, vp, vp)
+    _sig(L, "pt_backward_layers_range", None, cfgp, wp, grads, acts, bb, C.c_int, C.c_int, C.c_int, vp, vp)
+    _sig(L, "pt_backward_embed", None, grads, bb, i32p, C.c_int, C.c_int)
     # thin C ABI (ptc.h)
     _sig(L, "ptc_device_count", C.c_int)
     _sig(L, "ptc_create", vp, C.c_int, C.c_size_t)
@@ -128,6 +141,11 @@ def declare(L):
     _sig(L, "ptc_decoder_enqueue_steps", None, vp, C.c_int)
     _sig(L, "ptc_decoder_read_tokens", None, vp, i32p, C.c_int)
     _sig(L, "ptc_decoder_reset", None, vp)
+    _sig(L, "ptc_decoder_enqueue_embed", None, vp, C.c_int)
+    _sig(L, "ptc_decoder_enqueue_layers", None, vp, C.c_int, C.c_int, C.c_int)
+    _sig(L, "ptc_decoder_enqueue_head", None, vp)
+    _sig(L, "ptc_decoder_fetch_next", C.c_int, vp, f32p)
+    _sig(L, "ptc_decoder_step", C.c_int, vp, C.c_int, C.c_int, f32p)
     _sig(L, "ptc_timer_create", vp, vp)
     _sig(L, "ptc_timer_start", None, vp)
     _sig(L, "ptc_timer_stop", None, vp)

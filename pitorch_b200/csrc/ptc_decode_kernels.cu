@@ -164,28 +164,33 @@ __global__ void __launch_bounds__(256) k_qkv(DecodeModel m, int l, int from_embe
 }
 
 // ---------------------------------------------------------------------------
-// k_attn: grid (n_heads, n_chunks), 4 warps. CTA (h, c) covers positions
-// [c*CH, c*CH+CH) ∩ [0, pos]: scores q.k * 1/sqrt(hd), a chunk-local softmax
-// numerator with pitorch's exp, and the weighted value sum. The last CTA of
-// each head merges the chunks with the usual max-rescaling, which equals
-// softmax-then-weight (llama2.c:250-274) up to float rounding.
+// k_attn: grid (n_heads, n_chunks), 256 threads. CTA (h, c) covers positions
+// [c*CH, c*CH+CH) ∩ [0, pos] (CH = 64): scores q.k * 1/sqrt(hd), a
+// chunk-local softmax numerator with pitorch's exp, and the weighted value
+// sum. The last CTA of each head merges the chunks with the usual
+// max-rescaling, which equals softmax-then-weight (llama2.c:250-274) up to
+// float rounding. Every phase issues its loads independently (4 threads per
+// position for the scores, (float4 column, position group) threads for the
+// values and the merge), so a phase costs one memory round trip.
 // ---------------------------------------------------------------------------
-constexpr int ATT_THREADS = 128;
+constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAX_HD = 256;
-constexpr int ATT_MAX_CHUNK = 64;
+constexpr int ATT_MAX_CHUNKS = 256;
 
 __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
     pdl_trigger();
-    __shared__ float s_q[ATT_MAX_HD];
-    __shared__ float s_p[ATT_MAX_CHUNK];
-    __shared__ float s_o[ATT_THREADS / 32][ATT_MAX_HD];
+    __shared__ __align__(16) float s_q[ATT_MAX_HD];
+    __shared__ float s_p[ATT_MAX_CHUNKS];
+    __shared__ __align__(16) float s_o[ATT_THREADS * 4];
     __shared__ float s_stat[2];
     __shared__ int s_last;
 
     const int h = blockIdx.x, c = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hd = m.hd, CH = m.att_chunk;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hd = m.hd, hd4 = hd >> 2, CH = m.att_chunk;
     const int kvh = h / (m.nh / m.nkv);
+    const int ngrp = ATT_THREADS / hd4;      // position groups for the value pass
+    const int d4 = tid % hd4, grp = tid / hd4;
     pdl_wait();
     const int pos = min(__ldcg(&m.step->pos), m.seq - 1);
     const int t0 = c * CH;
@@ -195,14 +200,20 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
 
     if (t0 <= pos) {
         const int n = min(CH, pos + 1 - t0);
-        for (int d = threadIdx.x; d < hd; d += ATT_THREADS) s_q[d] = __ldcg(m.q + h * hd + d);
+        for (int d = tid; d < hd; d += ATT_THREADS) s_q[d] = __ldcg(m.q + h * hd + d);
         __syncthreads();
-        for (int j = warp; j < n; j += ATT_THREADS / 32) {
-            const float *kr = m.kc + (head_base + t0 + j) * hd;
+        {   // scores: 4 threads per position, float4 loads
+            const int j = tid >> 2, sub = tid & 3;
             float acc = 0.f;
-            for (int d = lane; d < hd; d += 32) acc = fmaf(s_q[d], __ldcg(kr + d), acc);
-            acc = warp_sum(acc);
-            if (lane == 0) s_p[j] = __fmul_rn(acc, scale);
+            if (j < n) {
+                const float4 *kr = reinterpret_cast<const float4 *>(m.kc + (head_base + t0 + j) * hd);
+                const float4 *q4 = reinterpret_cast<const float4 *>(s_q);
+#pragma unroll 16
+                for (int k = sub; k < hd4; k += 4) acc = dot4(__ldcg(kr + k), q4[k], acc);
+            }
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            if (j < n && sub == 0) s_p[j] = __fmul_rn(acc, scale);
         }
         __syncthreads();
         if (warp == 0) {
@@ -211,7 +222,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
             mx = warp_max(mx);
             float sum = 0.f;
             for (int j = lane; j < n; j += 32) {
-                float e = pt_expf(__fsub_rn(s_p[j], mx));
+                const float e = pt_expf(__fsub_rn(s_p[j], mx));
                 s_p[j] = e;
                 sum += e;
             }
@@ -219,49 +230,77 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
             if (lane == 0) { s_stat[0] = mx; s_stat[1] = sum; }
         }
         __syncthreads();
-        for (int d = lane; d < hd; d += 32) {
-            float acc = 0.f;
-            for (int j = warp; j < n; j += ATT_THREADS / 32)
-                acc = fmaf(s_p[j], __ldcg(m.vc + (head_base + t0 + j) * hd + d), acc);
-            s_o[warp][d] = acc;
+        {   // values: thread (float4 column d4, position group grp)
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (grp < ngrp) {
+                const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + t0) * hd);
+#pragma unroll 4
+                for (int j = grp; j < n; j += ngrp) {
+                    const float4 v = __ldcg(vb + (size_t)j * hd4 + d4);
+                    const float e = s_p[j];
+                    o.x = fmaf(e, v.x, o.x); o.y = fmaf(e, v.y, o.y);
+                    o.z = fmaf(e, v.z, o.z); o.w = fmaf(e, v.w, o.w);
+                }
+                reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
+            }
         }
         __syncthreads();
-        for (int d = threadIdx.x; d < hd; d += ATT_THREADS) {
+        for (int d = tid; d < hd; d += ATT_THREADS) {
             float o = 0.f;
-#pragma unroll
-            for (int w = 0; w < ATT_THREADS / 32; w++) o += s_o[w][d];
+            for (int g = 0; g < ngrp; g++) o += s_o[g * hd + d];
             part[d] = o;
         }
-        if (threadIdx.x == 0) { part[hd] = s_stat[0]; part[hd + 1] = s_stat[1]; }
+        if (tid == 0) { part[hd] = s_stat[0]; part[hd + 1] = s_stat[1]; }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         __threadfence();
-        unsigned ticket = atomicAdd(&m.att_ticket[h], 1u);
+        const unsigned ticket = atomicAdd(&m.att_ticket[h], 1u);
         s_last = (ticket == gridDim.y - 1);
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // Merge the nc chunk partials of this head.
     const int nc = pos / CH + 1;
     const float *hp = m.att_part + (size_t)h * m.n_chunks * (hd + 2);
-    float M = -3.4028235e+38f;
-    for (int k = 0; k < nc; k++) M = fmaxf(M, __ldcg(hp + (size_t)k * (hd + 2) + hd));
-    float L = 0.f;
-    for (int k = 0; k < nc; k++) {
-        const float *pk = hp + (size_t)k * (hd + 2);
-        L += __ldcg(pk + hd + 1) * pt_expf(__fsub_rn(__ldcg(pk + hd), M));
+    for (int k = tid; k < nc; k += ATT_THREADS) s_p[k] = __ldcg(hp + (size_t)k * (hd + 2) + hd);
+    __syncthreads();
+    if (warp == 0) {
+        float M = -3.4028235e+38f;
+        for (int k = lane; k < nc; k += 32) M = fmaxf(M, s_p[k]);
+        M = warp_max(M);
+        if (lane == 0) s_stat[0] = M;
     }
-    const float invL = __fdiv_rn(1.0f, L);
-    for (int d = threadIdx.x; d < hd; d += ATT_THREADS) {
-        float o = 0.f;
-        for (int k = 0; k < nc; k++) {
-            const float *pk = hp + (size_t)k * (hd + 2);
-            o = fmaf(pt_expf(__fsub_rn(__ldcg(pk + hd), M)), __ldcg(pk + d), o);
+    __syncthreads();
+    const float M = s_stat[0];
+    for (int k = tid; k < nc; k += ATT_THREADS) s_p[k] = pt_expf(__fsub_rn(s_p[k], M));
+    __syncthreads();
+    if (tid == 0) {
+        float L = 0.f;
+        for (int k = 0; k < nc; k++) L = fmaf(s_p[k], __ldcg(hp + (size_t)k * (hd + 2) + hd + 1), L);
+        s_stat[1] = __fdiv_rn(1.0f, L);
+    }
+    {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (grp < ngrp) {
+            for (int k = grp; k < nc; k += ngrp) {
+                const float *pk = hp + (size_t)k * (hd + 2) + 4 * d4;
+                const float w = s_p[k];
+                o.x = fmaf(w, __ldcg(pk + 0), o.x); o.y = fmaf(w, __ldcg(pk + 1), o.y);
+                o.z = fmaf(w, __ldcg(pk + 2), o.z); o.w = fmaf(w, __ldcg(pk + 3), o.w);
+            }
+            reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
         }
+    }
+    __syncthreads();
+    const float invL = s_stat[1];
+    for (int d = tid; d < hd; d += ATT_THREADS) {
+        float o = 0.f;
+        for (int g = 0; g < ngrp; g++) o += s_o[g * hd + d];
         m.att[h * hd + d] = o * invL;
     }
-    if (threadIdx.x == 0) m.att_ticket[h] = 0u;
+    if (tid == 0) m.att_ticket[h] = 0u;
 }
 
 // ---------------------------------------------------------------------------
@@ -472,6 +511,8 @@ void launch_embed(const DecodeModel &m, cudaStream_t s) {
     launch_pdl(k_embed, dim3((m.dim + 255) / 256), dim3(256), s, m);
 }
 
-int decode_attn_limits_ok(int hd, int chunk) { return hd <= ATT_MAX_HD && chunk <= ATT_MAX_CHUNK; }
+int decode_attn_limits_ok(int hd, int chunk, int n_chunks) {
+    return hd <= ATT_MAX_HD && hd % 4 == 0 && chunk * 4 == ATT_THREADS && n_chunks <= ATT_MAX_CHUNKS;
+}
 
 }  // namespace ptc

@@ -1,0 +1,210 @@
+// ptc_gemm.cu -- shared-memory-tiled fp32 GEMM for the training step.
+//
+// Replaces, for the batched training passes, the per-position matvecs of
+// pitorch/train/pt_train.c (forward: 7 matvecs per layer per position,
+// :204-303; input grads: transposed matvecs, :442-453) and its CPU weight
+// gradient matmul_backward_weight_batched (:475-492), whose QPU counterpart
+// sgemm_rect_tmu (pitorch/ops/gemm/gemm_rect.c:28-104) ships compiled out.
+//
+// C[m][n] = sum_k A(m,k) B(k,n) in fp32 with fp32 accumulation, for the three
+// layouts a linear layer needs (W is [out, in] row-major):
+//   forward   Y[T,out]  = X[T,in] . W^T     A k-contiguous, B k-contiguous
+//   input gr. dX[T,in]  = dY[T,out] . W     A k-contiguous, B n-contiguous
+//   weight gr dW[out,in] += dY^T . X        A m-contiguous, B n-contiguous
+// Tiles of A and B are staged k-major in shared memory (double-buffered,
+// 128-bit global loads where the layout allows), each thread accumulates a
+// TMxTN register block. Long-K products (the classifier input gradient,
+// K = vocab) are split over K into a partial buffer and reduced in a fixed
+// order, so results are deterministic.
+#include "ptc_common.cuh"
+#include "ptc_gemm.h"
+
+namespace ptc {
+
+template <int BM, int BN, int BK, int TM, int TN, bool A_KC, bool B_KC>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    k_gemm(GemmArgs g) {
+    constexpr int NT = (BM / TM) * (BN / TN);
+    __shared__ __align__(16) float As[2][BK][BM + 4];
+    __shared__ __align__(16) float Bs[2][BK][BN + 4];
+
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int split = blockIdx.z;
+    const int kper = (g.K + g.splits - 1) / g.splits;
+    const int kbeg = split * kper;
+    const int kend = min(g.K, kbeg + kper);
+
+    const int tx = tid % (BN / TN), ty = tid / (BN / TN);
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) acc[i][j] = 0.f;
+
+    auto loadA = [&](int buf, int k0) {
+        if (A_KC) {
+            // A(m,k) = A[m*lda + k]: BM rows x BK cols, read along k.
+            for (int e = tid; e < BM * BK; e += NT) {
+                const int r = e / BK, c = e % BK;
+                const int m = m0 + r, k = k0 + c;
+                As[buf][c][r] = (m < g.M && k < kend) ? __ldg(g.A + (size_t)m * g.lda + k) : 0.f;
+            }
+        } else {
+            // A(m,k) = A[k*lda + m]: BK rows x BM cols, read along m.
+            for (int e = tid; e < BM * BK; e += NT) {
+                const int r = e / BM, c = e % BM;
+                const int m = m0 + c, k = k0 + r;
+                As[buf][r][c] = (m < g.M && k < kend) ? __ldg(g.A + (size_t)k * g.lda + m) : 0.f;
+            }
+        }
+    };
+    auto loadB = [&](int buf, int k0) {
+        if (B_KC) {
+            // B(k,n) = B[n*ldb + k]
+            for (int e = tid; e < BN * BK; e += NT) {
+                const int r = e / BK, c = e % BK;
+                const int n = n0 + r, k = k0 + c;
+                Bs[buf][c][r] = (n < g.N && k < kend) ? __ldg(g.B + (size_t)n * g.ldb + k) : 0.f;
+            }
+        } else {
+            // B(k,n) = B[k*ldb + n]
+            for (int e = tid; e < BN * BK; e += NT) {
+                const int r = e / BN, c = e % BN;
+                const int n = n0 + c, k = k0 + r;
+                Bs[buf][r][c] = (n < g.N && k < kend) ? __ldg(g.B + (size_t)k * g.ldb + n) : 0.f;
+            }
+        }
+    };
+
+    int buf = 0;
+    if (kbeg < kend) {
+        loadA(0, kbeg);
+        loadB(0, kbeg);
+    }
+    __syncthreads();
+    for (int k0 = kbeg; k0 < kend; k0 += BK) {
+        if (k0 + BK < kend) {
+            loadA(buf ^ 1, k0 + BK);
+            loadB(buf ^ 1, k0 + BK);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BK; kk++) {
+            float a[TM], b[TN];
+#pragma unroll
+            for (int i = 0; i < TM; i++) a[i] = As[buf][kk][ty * TM + i];
+#pragma unroll
+            for (int j = 0; j < TN; j++) b[j] = Bs[buf][kk][tx * TN + j];
+#pragma unroll
+            for (int i = 0; i < TM; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+        buf ^= 1;
+    }
+
+    // Epilogue
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        const int m = m0 + ty * TM + i;
+        if (m >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const int n = n0 + tx * TN + j;
+            if (n >= g.N) continue;
+            const float v = acc[i][j];
+            if (g.splits > 1) {
+                g.partial[((size_t)split * g.M + m) * g.N + n] = v;
+                continue;
+            }
+            float *c = g.C + (size_t)m * g.ldc + n;
+            switch (g.epi) {
+                case EPI_STORE: *c = v; break;
+                case EPI_ACCUM: *c = *c + v; break;
+                case EPI_RESID: *c = __fadd_rn(g.R[(size_t)m * g.ldr + n], v); break;
+            }
+        }
+    }
+    // RoPE epilogue (q/k projections): pairs (n, n+1) are held by the same
+    // thread since TN is even and tiles start at even n.
+    if (g.epi == EPI_ROPE && g.splits == 1) {
+#pragma unroll
+        for (int i = 0; i < TM; i++) {
+            const int m = m0 + ty * TM + i;
+            if (m >= g.M) continue;
+#pragma unroll
+            for (int j = 0; j < TN; j += 2) {
+                const int n = n0 + tx * TN + j;
+                if (n + 1 >= g.N) continue;
+                const float th = rope_theta(n, g.rope_hd, m);
+                const float cs = pt_cosf(th), sn = pt_sinf(th);
+                const float a0 = acc[i][j], a1 = acc[i][j + 1];
+                float *c = g.C + (size_t)m * g.ldc + n;
+                c[0] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+                c[1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+            }
+        }
+    }
+}
+
+// Fixed-order reduction of split-K partials into C with the epilogue.
+__global__ void k_splitk_reduce(GemmArgs g) {
+    const size_t total = (size_t)g.M * g.N;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total;
+         e += (size_t)gridDim.x * blockDim.x) {
+        float v = 0.f;
+        for (int s = 0; s < g.splits; s++) v += g.partial[(size_t)s * total + e];
+        const int m = (int)(e / g.N), n = (int)(e % g.N);
+        float *c = g.C + (size_t)m * g.ldc + n;
+        switch (g.epi) {
+            case EPI_STORE: *c = v; break;
+            case EPI_ACCUM: *c = *c + v; break;
+            case EPI_RESID: *c = __fadd_rn(g.R[(size_t)m * g.ldr + n], v); break;
+            default: *c = v; break;
+        }
+    }
+}
+
+template <int BM, int BN, int BK, int TM, int TN>
+static void launch_tile(const GemmArgs &g, cudaStream_t s) {
+    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
+    dim3 block((BM / TM) * (BN / TN));
+    if (g.a_kcontig && g.b_kcontig) k_gemm<BM, BN, BK, TM, TN, true, true><<<grid, block, 0, s>>>(g);
+    else if (g.a_kcontig) k_gemm<BM, BN, BK, TM, TN, true, false><<<grid, block, 0, s>>>(g);
+    else if (g.b_kcontig) k_gemm<BM, BN, BK, TM, TN, false, true><<<grid, block, 0, s>>>(g);
+    else k_gemm<BM, BN, BK, TM, TN, false, false><<<grid, block, 0, s>>>(g);
+    PTC_CHECK(cudaGetLastError());
+}
+
+void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
+    if (g.M <= 0 || g.N <= 0) return;
+    if (g.K <= 0) {
+        if (g.epi == EPI_STORE) {
+            for (int m = 0; m < g.M; m++)
+                PTC_CHECK(cudaMemsetAsync(g.C + (size_t)m * g.ldc, 0, (size_t)g.N * 4, s));
+        }
+        return;
+    }
+    const bool big = (long)g.M * g.N >= (long)128 * 128 * n_sm;
+    const long tiles = big ? (long)((g.M + 127) / 128) * ((g.N + 127) / 128)
+                           : (long)((g.M + 63) / 64) * ((g.N + 63) / 64);
+    // Split K when the tile grid cannot fill the GPU and K is long.
+    int splits = 1;
+    if (g.partial && g.epi != EPI_ROPE) {
+        while (tiles * splits * 2 <= 2L * n_sm && g.K / (splits * 2) >= 256 &&
+               (size_t)(splits * 2) * g.M * g.N <= g.partial_cap)
+            splits *= 2;
+    }
+    g.splits = splits;
+    if (big) launch_tile<128, 128, 8, 8, 8>(g, s);
+    else launch_tile<64, 64, 16, 4, 4>(g, s);
+    if (splits > 1) {
+        int blocks = (int)(((size_t)g.M * g.N + 255) / 256);
+        if (blocks > 8 * n_sm) blocks = 8 * n_sm;
+        k_splitk_reduce<<<blocks, 256, 0, s>>>(g);
+        PTC_CHECK(cudaGetLastError());
+    }
+}
+
+}  // namespace ptc

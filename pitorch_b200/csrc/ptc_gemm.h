@@ -1,0 +1,37 @@
+// ptc_gemm.h -- internal interface of the fp32 training GEMM.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace ptc {
+
+enum GemmEpilogue {
+    EPI_STORE = 0,  // C = A.B
+    EPI_ACCUM = 1,  // C += A.B          (weight gradients accumulate)
+    EPI_RESID = 2,  // C = R + A.B       (residual adds of the forward pass)
+    EPI_ROPE = 3,   // C = RoPE_row(A.B) (q/k projections; row index = position)
+};
+
+struct GemmArgs {
+    int M, N, K;
+    const float *A;
+    int lda;
+    bool a_kcontig;   // A(m,k) = A[m*lda+k] if true, else A[k*lda+m]
+    const float *B;
+    int ldb;
+    bool b_kcontig;   // B(k,n) = B[n*ldb+k] if true, else B[k*ldb+n]
+    float *C;
+    int ldc;
+    const float *R;   // residual input (EPI_RESID)
+    int ldr;
+    int epi;
+    int rope_hd;      // head_dim for EPI_ROPE
+    float *partial;   // split-K workspace (may be null: no split)
+    size_t partial_cap;  // floats available in `partial`
+    int splits;       // set by gemm()
+};
+
+void gemm(GemmArgs g, int n_sm, cudaStream_t s);
+
+}  // namespace ptc

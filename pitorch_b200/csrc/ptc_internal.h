@@ -22,6 +22,6 @@ struct DecodeModel;
 void launch_layer(const DecodeModel &m, int l, bool from_embedding, cudaStream_t s);
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s);
 void launch_embed(const DecodeModel &m, cudaStream_t s);
-int decode_attn_limits_ok(int hd, int chunk);
+int decode_attn_limits_ok(int hd, int chunk, int n_chunks);
 void launch_matvec(const float *W, const float *x, float *y, int rows, int cols, cudaStream_t s);
 }  // namespace ptc

@@ -1,0 +1,711 @@
+// ptc_train.cu -- pt_train_step on the GPU: batched forward with saved
+// activations, cross-entropy, the 7-operator backward and SGD.
+//
+// Follows pitorch/train/pt_train.c (forward :171-329, backward :549-866,
+// SGD :870-942, staged variants :946-1383) and the primitives of
+// pitorch/train/pt_backward_ops.c. The reference runs T per-position matvecs
+// per linear layer and a CPU outer-product loop for weight gradients; here
+// every linear layer is one fp32 GEMM over all positions (ptc_gemm.cu) and
+// the elementwise/normalisation/attention work runs as small kernels.
+// Position T-1 carries no loss and is skipped by every backward GEMM, as in
+// pt_train.c:596-605.
+//
+// Buffers (device, sized for max_T and the context's local layers L) use the
+// reference's activation layout (pt_train.h:19-32), e.g. residuals
+// [(L+1), T, dim], att [L, n_heads, T, T], and its gradient layout
+// (pt_train.c:334-371). All are carved from the context arena at creation;
+// a step allocates nothing.
+#include <string.h>
+
+#include "../../include/ptc.h"
+#include "ptc_common.cuh"
+#include "ptc_gemm.h"
+#include "ptc_internal.h"
+
+using ptc::GemmArgs;
+
+namespace ptc {
+
+// ---------------------------------------------------------------------------
+// Elementwise / row kernels
+// ---------------------------------------------------------------------------
+
+// residuals[0][t] = emb[tokens[t]] (pt_train.c:189-191)
+__global__ void k_tr_embed(float *res, const float *emb, const int *tokens, int T, int D) {
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < T * D; e += gridDim.x * blockDim.x) {
+        const int t = e / D, i = e % D;
+        res[e] = emb[(size_t)tokens[t] * D + i];
+    }
+}
+
+// One warp per row: out = (x * s) * w, s = 1/sqrt(mean(x^2)+eps) (pt_ops.c:5-12).
+__global__ void k_tr_rmsnorm(float *out, const float *x, const float *w, int rows, int D) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float *xr = x + (size_t)warp * D;
+    float ss = 0.f;
+    for (int i = lane; i < D; i += 32) ss = fmaf(xr[i], xr[i], ss);
+    ss = warp_sum(ss);
+    const float s = rms_scale(ss, D);
+    float *o = out + (size_t)warp * D;
+    for (int i = lane; i < D; i += 32) o[i] = __fmul_rn(__fmul_rn(xr[i], s), w[i]);
+}
+
+// Causal attention forward, one CTA per (head, t) (pt_train.c:224-259):
+// att row = softmax(q_t . k_s * scale) for s <= t (zeros after t), and
+// att_out[t, h] = sum_s att[s] v_s.
+__global__ void __launch_bounds__(128) k_tr_attn_fwd(const float *q, const float *k, const float *v,
+                                                     float *att, float *out, int T, int nh, int nkv,
+                                                     int hd) {
+    extern __shared__ float sm[];
+    float *s_q = sm;          // [hd]
+    float *s_p = sm + hd;     // [T]
+    __shared__ float s_red[2];
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+    const int D = nh * hd, K = nkv * hd, koff = (h / (nh / nkv)) * hd;
+    const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) s_q[d] = q[(size_t)t * D + h * hd + d];
+    __syncthreads();
+    for (int s = warp; s <= t; s += nwarp) {
+        const float *kr = k + (size_t)s * K + koff;
+        float acc = 0.f;
+        for (int d = lane; d < hd; d += 32) acc = fmaf(s_q[d], kr[d], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) s_p[s] = __fmul_rn(acc, scale);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float mx = -3.4028235e+38f;
+        for (int s = lane; s <= t; s += 32) mx = fmaxf(mx, s_p[s]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int s = lane; s <= t; s += 32) {
+            const float e = pt_expf(__fsub_rn(s_p[s], mx));
+            s_p[s] = e;
+            sum += e;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) s_red[0] = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+    const float inv = s_red[0];
+    float *arow = att + ((size_t)h * T + t) * T;
+    for (int s = threadIdx.x; s < T; s += blockDim.x) {
+        const float p = (s <= t) ? __fmul_rn(s_p[s], inv) : 0.f;
+        if (s <= t) s_p[s] = p;
+        arow[s] = p;
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.f;
+        for (int s = 0; s <= t; s++) o = fmaf(s_p[s], v[(size_t)s * K + koff + d], o);
+        out[(size_t)t * D + h * hd + d] = o;
+    }
+}
+
+// sh = silu(h1) * h3 with the training form (h1 * sig) * h3 (pt_train.c:281-284).
+__global__ void k_tr_silu_gate(float *sh, const float *h1, const float *h3, size_t n) {
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const float a = h1[e];
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, pt_expf(-a)));
+        sh[e] = __fmul_rn(__fmul_rn(a, sig), h3[e]);
+    }
+}
+
+// Per-row cross-entropy (pt_train.c:309-325): one CTA per row t < T-1.
+__global__ void k_tr_ce_rows(const float *logits, const int *tokens, int V, float *loss_rows) {
+    __shared__ float s_r[32];
+    const int t = blockIdx.x;
+    const float *lg = logits + (size_t)t * V;
+    float mx = -3.4028235e+38f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) mx = fmaxf(mx, lg[v]);
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < (blockDim.x >> 5) ? s_r[threadIdx.x] : -3.4028235e+38f;
+        m = warp_max(m);
+        if (threadIdx.x == 0) s_r[0] = m;
+    }
+    __syncthreads();
+    mx = s_r[0];
+    __syncthreads();
+    float sum = 0.f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) sum += pt_expf(__fsub_rn(lg[v], mx));
+    sum = warp_sum(sum);
+    if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += s_r[w];
+        const float tgt = lg[tokens[t + 1]];
+        loss_rows[t] = -(__fsub_rn(__fsub_rn(tgt, mx), pt_logf(s)));
+    }
+}
+
+// loss = (sum_t loss_t) / (T-1), summed in position order as the reference does.
+__global__ void k_tr_loss_sum(const float *loss_rows, int n, float *loss) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    float l = 0.f;
+    for (int t = 0; t < n; t++) l = __fadd_rn(l, loss_rows[t]);
+    *loss = __fdiv_rn(l, (float)n);
+}
+
+// d_logit rows (pt_train.c:609-621): softmax * (1/(T-1)), minus 1/(T-1) at the target.
+__global__ void k_tr_ce_backward(const float *logits, const int *tokens, int V, float invn, float *dl_all) {
+    __shared__ float s_r[32];
+    const int t = blockIdx.x;
+    const float *lg = logits + (size_t)t * V;
+    float *dl = dl_all + (size_t)t * V;
+    float mx = -3.4028235e+38f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) mx = fmaxf(mx, lg[v]);
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < (blockDim.x >> 5) ? s_r[threadIdx.x] : -3.4028235e+38f;
+        m = warp_max(m);
+        if (threadIdx.x == 0) s_r[0] = m;
+    }
+    __syncthreads();
+    mx = s_r[0];
+    __syncthreads();
+    float sum = 0.f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float e = pt_expf(__fsub_rn(lg[v], mx));
+        dl[v] = e;
+        sum += e;
+    }
+    sum = warp_sum(sum);
+    if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += s_r[w];
+        s_r[0] = __fmul_rn(__fdiv_rn(1.0f, s), invn);
+    }
+    __syncthreads();
+    const float f = s_r[0];
+    const int tgt = tokens[t + 1];
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        float x = __fmul_rn(dl[v], f);
+        if (v == tgt) x = __fsub_rn(x, invn);
+        dl[v] = x;
+    }
+}
+
+// rmsnorm backward, one warp per row (pt_backward_ops.c:4-30): dx += ..., and
+// the row's weight-grad contribution d_o * x * inv into dw_rows.
+__global__ void k_tr_rmsnorm_bwd(float *dx, float *dw_rows, const float *d_o, const float *x,
+                                 const float *w, int rows, int D) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float *xr = x + (size_t)warp * D;
+    const float *dor = d_o + (size_t)warp * D;
+    float ss = 0.f, dot = 0.f;
+    for (int i = lane; i < D; i += 32) {
+        ss = fmaf(xr[i], xr[i], ss);
+        dot = fmaf(__fmul_rn(dor[i], w[i]), xr[i], dot);
+    }
+    ss = warp_sum(ss);
+    dot = warp_sum(dot);
+    const float inv = __fdiv_rn(1.0f, pt_sqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), 1e-5f)));
+    const float coeff = __fdiv_rn(__fmul_rn(__fmul_rn(inv, inv), inv), (float)D);
+    float *dxr = dx + (size_t)warp * D;
+    float *dwr = dw_rows + (size_t)warp * D;
+    for (int i = lane; i < D; i += 32) {
+        dwr[i] = __fmul_rn(__fmul_rn(dor[i], xr[i]), inv);
+        const float a = __fmul_rn(__fmul_rn(inv, dor[i]), w[i]);
+        const float b = __fmul_rn(__fmul_rn(coeff, dot), xr[i]);
+        dxr[i] = __fadd_rn(dxr[i], __fsub_rn(a, b));
+    }
+}
+
+// g[i] += sum over rows of dw_rows[t][i], accumulated in row order like the
+// reference's position loop.
+__global__ void k_tr_colsum_accum(float *g, const float *rows_, int n_rows, int D) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= D) return;
+    float acc = g[i];
+    for (int t = 0; t < n_rows; t++) acc = __fadd_rn(acc, rows_[(size_t)t * D + i]);
+    g[i] = acc;
+}
+
+// silu*gate backward (pt_train.c:715-721).
+__global__ void k_tr_silu_bwd(float *d_hid, float *d_hid2, const float *h1, const float *h3, size_t n) {
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        const float a = h1[e];
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, pt_expf(-a)));
+        const float sv = __fmul_rn(a, sig);
+        const float dh = d_hid[e];
+        const float ds = __fmul_rn(dh, h3[e]);
+        d_hid2[e] = __fmul_rn(dh, sv);
+        d_hid[e] = __fmul_rn(__fmul_rn(ds, sig), __fadd_rn(1.0f, __fmul_rn(a, __fsub_rn(1.0f, sig))));
+    }
+}
+
+// Attention backward part 1, one CTA per (head, t < T-1) (pt_train.c:780-812):
+// dS[t][s] = P[t][s] (dP[t][s] - <dP[t], P[t]>) * scale with dP = d_ao . v,
+// and d_q[t] = sum_s dS[t][s] k_s.
+__global__ void __launch_bounds__(128) k_tr_attn_bwd_q(const float *d_ao, const float *att, const float *q,
+                                                       const float *k, const float *v, float *dS,
+                                                       float *d_q, int T, int nh, int nkv, int hd) {
+    extern __shared__ float sm[];
+    float *s_do = sm;         // [hd]
+    float *s_dp = sm + hd;    // [T]
+    __shared__ float s_dot;
+    const int h = blockIdx.x, t = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+    const int D = nh * hd, K = nkv * hd, koff = (h / (nh / nkv)) * hd;
+    const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
+    const float *P = att + ((size_t)h * T + t) * T;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) s_do[d] = d_ao[(size_t)t * D + h * hd + d];
+    __syncthreads();
+    for (int s = warp; s <= t; s += nwarp) {
+        const float *vr = v + (size_t)s * K + koff;
+        float acc = 0.f;
+        for (int d = lane; d < hd; d += 32) acc = fmaf(s_do[d], vr[d], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) s_dp[s] = acc;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float dot = 0.f;
+        for (int s = lane; s <= t; s += 32) dot = fmaf(s_dp[s], P[s], dot);
+        dot = warp_sum(dot);
+        if (lane == 0) s_dot = dot;
+    }
+    __syncthreads();
+    float *dsr = dS + ((size_t)h * T + t) * T;
+    for (int s = threadIdx.x; s < T; s += blockDim.x) {
+        float x = 0.f;
+        if (s <= t) x = __fmul_rn(__fmul_rn(P[s], __fsub_rn(s_dp[s], s_dot)), scale);
+        dsr[s] = x;
+        if (s <= t) s_dp[s] = x;
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float acc = 0.f;
+        for (int s = 0; s <= t; s++) acc = fmaf(s_dp[s], k[(size_t)s * K + koff + d], acc);
+        d_q[(size_t)t * D + h * hd + d] = acc;
+    }
+}
+
+// Attention backward part 2, one CTA per (kv head, s): d_k[s] = sum_t dS[t][s] q_t,
+// d_v[s] = sum_t P[t][s] d_ao_t over t in [s, n_rows) and the query heads of
+// this kv head.
+__global__ void __launch_bounds__(128) k_tr_attn_bwd_kv(const float *d_ao, const float *att, const float *q,
+                                                        const float *dS, float *d_k, float *d_v, int T,
+                                                        int n_rows, int nh, int nkv, int hd) {
+    const int kh = blockIdx.x, s = blockIdx.y;
+    const int D = nh * hd, K = nkv * hd, group = nh / nkv;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float ak = 0.f, av = 0.f;
+        for (int hh = 0; hh < group; hh++) {
+            const int h = kh * group + hh;
+            for (int t = s; t < n_rows; t++) {
+                const size_t rowoff = ((size_t)h * T + t) * T + s;
+                ak = fmaf(dS[rowoff], q[(size_t)t * D + h * hd + d], ak);
+                av = fmaf(att[rowoff], d_ao[(size_t)t * D + h * hd + d], av);
+            }
+        }
+        d_k[(size_t)s * K + kh * hd + d] = ak;
+        d_v[(size_t)s * K + kh * hd + d] = av;
+    }
+}
+
+// RoPE backward (pt_backward_ops.c:52-69) into fresh d_qpre / d_kpre.
+__global__ void k_tr_rope_bwd(float *dq_pre, float *dk_pre, const float *dq, const float *dk, int rows,
+                              int D, int K, int hd) {
+    const int half = D / 2;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < rows * half; e += gridDim.x * blockDim.x) {
+        const int t = e / half, i = 2 * (e % half);
+        const float th = rope_theta(i, hd, t);
+        const float c = pt_cosf(th), s = pt_sinf(th);
+        const float *a = dq + (size_t)t * D + i;
+        float *o = dq_pre + (size_t)t * D + i;
+        o[0] = __fadd_rn(__fmul_rn(a[0], c), __fmul_rn(a[1], s));
+        o[1] = __fadd_rn(__fmul_rn(-a[0], s), __fmul_rn(a[1], c));
+        if (i < K) {
+            const float *b = dk + (size_t)t * K + i;
+            float *ok = dk_pre + (size_t)t * K + i;
+            ok[0] = __fadd_rn(__fmul_rn(b[0], c), __fmul_rn(b[1], s));
+            ok[1] = __fadd_rn(__fmul_rn(-b[0], s), __fmul_rn(b[1], c));
+        }
+    }
+}
+
+// g_emb[tokens[t]] += d_res[t] (pt_train.c:862-863); repeated tokens collide,
+// hence atomics.
+__global__ void k_tr_embed_bwd(float *g_emb, const float *d_res, const int *tokens, int rows, int D) {
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < rows * D; e += gridDim.x * blockDim.x) {
+        const int t = e / D, i = e % D;
+        atomicAdd(g_emb + (size_t)tokens[t] * D + i, d_res[e]);
+    }
+}
+
+// w -= lr * g (pt_train.c:870-873)
+__global__ void k_tr_sgd(float *w, const float *g, size_t n, float lr) {
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x)
+        w[e] = __fsub_rn(w[e], __fmul_rn(lr, g[e]));
+}
+
+}  // namespace ptc
+
+// ---------------------------------------------------------------------------
+// Trainer object
+// ---------------------------------------------------------------------------
+struct ptc_trainer {
+    ptc_ctx *ctx;
+    cudaStream_t s;
+    int n_sm;
+    int D, H, L, nh, nkv, V, seq, hd, K, maxT, T;
+    int has_embed, has_head;
+    ptc_weights w;  // device weights (mutable through casts)
+    // activations
+    float *res, *res_att, *xb_att, *q, *k, *v, *att, *att_out, *xb_ffn, *hb, *hb2, *x_final, *logits;
+    // backward
+    float *d_res, *d_aout, *d_q, *d_k, *d_v, *d_logit, *d_xb, *d_hid, *d_hid2, *sh, *dS, *d_qpre,
+        *d_kpre, *dw_rows, *partial;
+    size_t partial_cap;
+    int *tokens;
+    float *loss_rows, *loss;
+    float *loss_host;  // pinned
+    // gradients (pt_train.c:334-371 layout, absent parts empty)
+    float *g_mem;
+    size_t n_params;
+    float *g_emb, *g_rms_att, *g_wq, *g_wk, *g_wv, *g_wo, *g_rms_ffn, *g_w1, *g_w2, *g_w3, *g_rms_final,
+        *g_wcls;
+};
+
+static int blocks_for(size_t n, int threads, int n_sm) {
+    size_t b = (n + threads - 1) / threads;
+    size_t cap = (size_t)n_sm * 8;
+    return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, const ptc_weights *w,
+                                           int max_T, int has_embed, int has_head) {
+    ptc_trainer *tr = new ptc_trainer();
+    memset(tr, 0, sizeof(*tr));
+    tr->ctx = c;
+    tr->s = ptc_ctx_stream(c);
+    tr->n_sm = ptc_sm_count(c);
+    tr->D = cfg->dim;
+    tr->H = cfg->hidden_dim;
+    tr->L = cfg->n_layers;
+    tr->nh = cfg->n_heads;
+    tr->nkv = cfg->n_kv_heads;
+    tr->V = cfg->vocab_size;
+    tr->seq = cfg->seq_len;
+    tr->hd = tr->D / tr->nh;
+    tr->K = tr->nkv * tr->hd;
+    tr->maxT = max_T;
+    tr->has_embed = has_embed;
+    tr->has_head = has_head;
+    tr->w = *w;
+    if (max_T < 2) PTC_FATAL("training needs max_T >= 2 (got %d)", max_T);
+    if (tr->D % 2 || tr->hd % 2) PTC_FATAL("training needs even dim and head_dim");
+
+    const size_t T = max_T, D = tr->D, H = tr->H, L = tr->L, K = tr->K, V = tr->V, nh = tr->nh;
+    auto A = [&](size_t n) { return (float *)ptc_alloc(c, (n ? n : 1) * 4); };
+    tr->res = A((L + 1) * T * D);
+    tr->res_att = A(L * T * D);
+    tr->xb_att = A(L * T * D);
+    tr->q = A(L * T * D);
+    tr->k = A(L * T * K);
+    tr->v = A(L * T * K);
+    tr->att = A(L * nh * T * T);
+    tr->att_out = A(L * T * D);
+    tr->xb_ffn = A(L * T * D);
+    tr->hb = A(L * T * H);
+    tr->hb2 = A(L * T * H);
+    tr->x_final = A(T * D);
+    tr->logits = has_head ? A(T * V) : nullptr;
+    tr->d_res = A(T * D);
+    tr->d_aout = A(T * D);
+    tr->d_q = A(T * D);
+    tr->d_k = A(T * K);
+    tr->d_v = A(T * K);
+    tr->d_logit = has_head ? A(T * V) : nullptr;
+    tr->d_xb = A(T * D);
+    tr->d_hid = A(T * H);
+    tr->d_hid2 = A(T * H);
+    tr->sh = A(T * H);
+    tr->dS = A(nh * T * T);
+    tr->d_qpre = A(T * D);
+    tr->d_kpre = A(T * K);
+    tr->dw_rows = A(T * D);
+    tr->partial_cap = 8 * T * (D > H ? D : H);
+    tr->partial = A(tr->partial_cap);
+    tr->tokens = (int *)ptc_alloc(c, T * 4);
+    tr->loss_rows = A(T);
+    tr->loss = A(1);
+    tr->loss_host = (float *)ptc_host_alloc(4);
+
+    // gradient layout of pt_train.c:334-371 for the owned parts
+    const size_t Ve = has_embed ? V : 0;
+    size_t n = Ve * D + L * D + L * D * D + 2 * L * K * D + L * D * D + L * D + 3 * L * H * D +
+               (has_head ? D : 0);
+    const bool untied = has_head && w->wcls && w->wcls != w->token_embedding;
+    if (untied) n += V * D;
+    tr->n_params = n;
+    tr->g_mem = A(n);
+    float *p = tr->g_mem;
+    tr->g_emb = has_embed ? p : nullptr; p += Ve * D;
+    tr->g_rms_att = p; p += L * D;
+    tr->g_wq = p; p += L * D * D;
+    tr->g_wk = p; p += L * K * D;
+    tr->g_wv = p; p += L * K * D;
+    tr->g_wo = p; p += L * D * D;
+    tr->g_rms_ffn = p; p += L * D;
+    tr->g_w1 = p; p += L * H * D;
+    tr->g_w2 = p; p += L * D * H;
+    tr->g_w3 = p; p += L * H * D;
+    tr->g_rms_final = has_head ? p : nullptr; p += has_head ? D : 0;
+    tr->g_wcls = untied ? p : (has_head ? tr->g_emb : nullptr);
+    if (has_head && !untied && !has_embed) PTC_FATAL("tied classifier needs the embedding on the same rank");
+    PTC_CHECK(cudaMemsetAsync(tr->g_mem, 0, n * 4, tr->s));
+    PTC_CHECK(cudaStreamSynchronize(tr->s));
+    return tr;
+}
+
+extern "C" void ptc_trainer_destroy(ptc_trainer *tr) {
+    if (!tr) return;
+    cudaStreamSynchronize(tr->s);
+    ptc_host_free(tr->loss_host);
+    delete tr;
+}
+
+extern "C" size_t ptc_trainer_n_params(ptc_trainer *tr) { return tr->n_params; }
+extern "C" float *ptc_trainer_grads(ptc_trainer *tr) { return tr->g_mem; }
+extern "C" float *ptc_trainer_residual(ptc_trainer *tr, int l) {
+    return tr->res + (size_t)l * tr->T * tr->D;
+}
+extern "C" float *ptc_trainer_dres(ptc_trainer *tr) { return tr->d_res; }
+
+static GemmArgs G(int M, int N, int K, const float *A, int lda, bool akc, const float *B, int ldb, bool bkc,
+                  float *C, int ldc, int epi) {
+    GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.M = M; g.N = N; g.K = K;
+    g.A = A; g.lda = lda; g.a_kcontig = akc;
+    g.B = B; g.ldb = ldb; g.b_kcontig = bkc;
+    g.C = C; g.ldc = ldc; g.epi = epi;
+    return g;
+}
+
+static void run_gemm(ptc_trainer *tr, GemmArgs g) {
+    g.partial = tr->partial;
+    g.partial_cap = tr->partial_cap;
+    ptc::gemm(g, tr->n_sm, tr->s);
+}
+
+extern "C" void ptc_trainer_set_tokens(ptc_trainer *tr, const int *tokens, int T) {
+    if (T < 2 || T > tr->maxT) PTC_FATAL("T=%d outside [2, max_T=%d]", T, tr->maxT);
+    if (T > tr->seq) PTC_FATAL("T=%d exceeds seq_len %d", T, tr->seq);
+    for (int t = 0; t < T; t++)
+        if (tokens[t] < 0 || tokens[t] >= tr->V) PTC_FATAL("token %d outside [0, %d)", tokens[t], tr->V);
+    tr->T = T;
+    PTC_CHECK(cudaMemcpyAsync(tr->tokens, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, tr->s));
+}
+
+extern "C" void ptc_trainer_zero_grads(ptc_trainer *tr) {
+    PTC_CHECK(cudaMemsetAsync(tr->g_mem, 0, tr->n_params * 4, tr->s));
+}
+
+// pt_forward_train_embed (pt_train.c:946-952)
+extern "C" void ptc_trainer_fwd_embed(ptc_trainer *tr) {
+    if (!tr->has_embed) PTC_FATAL("trainer has no embedding");
+    const int n = tr->T * tr->D;
+    ptc::k_tr_embed<<<blocks_for(n, 256, tr->n_sm), 256, 0, tr->s>>>(tr->res, tr->w.token_embedding,
+                                                                       tr->tokens, tr->T, tr->D);
+    PTC_CHECK(cudaGetLastError());
+}
+
+// pt_forward_train_layers_range (pt_train.c:954-1061)
+extern "C" void ptc_trainer_fwd_layers(ptc_trainer *tr, int l0, int l1) {
+    const int T = tr->T, D = tr->D, H = tr->H, K = tr->K, nh = tr->nh;
+    cudaStream_t s = tr->s;
+    for (int l = l0; l < l1; l++) {
+        const size_t LD = (size_t)l * T * D, LK = (size_t)l * T * K, LH = (size_t)l * T * H;
+        float *rin = tr->res + LD, *rmid = tr->res_att + LD, *rout = tr->res + (size_t)(l + 1) * T * D;
+        float *xa = tr->xb_att + LD, *xf = tr->xb_ffn + LD;
+        ptc::k_tr_rmsnorm<<<(T + 7) / 8, 256, 0, s>>>(xa, rin, tr->w.rms_att_weight + (size_t)l * D, T, D);
+        GemmArgs g = G(T, D, D, xa, D, true, tr->w.wq + (size_t)l * D * D, D, true, tr->q + LD, D, ptc::EPI_ROPE);
+        g.rope_hd = tr->hd;
+        run_gemm(tr, g);
+        g = G(T, K, D, xa, D, true, tr->w.wk + (size_t)l * K * D, D, true, tr->k + LK, K, ptc::EPI_ROPE);
+        g.rope_hd = tr->hd;
+        run_gemm(tr, g);
+        run_gemm(tr, G(T, K, D, xa, D, true, tr->w.wv + (size_t)l * K * D, D, true, tr->v + LK, K, ptc::EPI_STORE));
+        const size_t smem = (size_t)(tr->hd + T) * 4;
+        ptc::k_tr_attn_fwd<<<dim3(nh, T), 128, smem, s>>>(tr->q + LD, tr->k + LK, tr->v + LK,
+                                                          tr->att + (size_t)l * nh * T * T, tr->att_out + LD,
+                                                          T, nh, tr->nkv, tr->hd);
+        PTC_CHECK(cudaGetLastError());
+        g = G(T, D, D, tr->att_out + LD, D, true, tr->w.wo + (size_t)l * D * D, D, true, rmid, D, ptc::EPI_RESID);
+        g.R = rin;
+        g.ldr = D;
+        run_gemm(tr, g);
+        ptc::k_tr_rmsnorm<<<(T + 7) / 8, 256, 0, s>>>(xf, rmid, tr->w.rms_ffn_weight + (size_t)l * D, T, D);
+        run_gemm(tr, G(T, H, D, xf, D, true, tr->w.w1 + (size_t)l * H * D, D, true, tr->hb + LH, H, ptc::EPI_STORE));
+        run_gemm(tr, G(T, H, D, xf, D, true, tr->w.w3 + (size_t)l * H * D, D, true, tr->hb2 + LH, H, ptc::EPI_STORE));
+        ptc::k_tr_silu_gate<<<blocks_for((size_t)T * H, 256, tr->n_sm), 256, 0, s>>>(tr->sh, tr->hb + LH,
+                                                                                      tr->hb2 + LH, (size_t)T * H);
+        g = G(T, D, H, tr->sh, H, true, tr->w.w2 + (size_t)l * D * H, H, true, rout, D, ptc::EPI_RESID);
+        g.R = rmid;
+        g.ldr = D;
+        run_gemm(tr, g);
+    }
+    PTC_CHECK(cudaGetLastError());
+}
+
+// pt_forward_train_head (pt_train.c:1063-1099): returns the loss (synchronises).
+extern "C" float ptc_trainer_fwd_head(ptc_trainer *tr) {
+    if (!tr->has_head) PTC_FATAL("trainer has no head");
+    const int T = tr->T, D = tr->D, V = tr->V;
+    cudaStream_t s = tr->s;
+    const float *rfin = tr->res + (size_t)tr->L * T * D;
+    ptc::k_tr_rmsnorm<<<(T + 7) / 8, 256, 0, s>>>(tr->x_final, rfin, tr->w.rms_final_weight, T, D);
+    run_gemm(tr, G(T, V, D, tr->x_final, D, true, tr->w.wcls, D, true, tr->logits, V, ptc::EPI_STORE));
+    ptc::k_tr_ce_rows<<<T - 1, 512, 0, s>>>(tr->logits, tr->tokens, V, tr->loss_rows);
+    ptc::k_tr_loss_sum<<<1, 32, 0, s>>>(tr->loss_rows, T - 1, tr->loss);
+    PTC_CHECK(cudaGetLastError());
+    PTC_CHECK(cudaMemcpyAsync(tr->loss_host, tr->loss, 4, cudaMemcpyDeviceToHost, s));
+    PTC_CHECK(cudaStreamSynchronize(s));
+    return *tr->loss_host;
+}
+
+// pt_backward_head (pt_train.c:1103-1171)
+extern "C" void ptc_trainer_bwd_head(ptc_trainer *tr) {
+    const int T = tr->T, D = tr->D, V = tr->V, n = T - 1;
+    cudaStream_t s = tr->s;
+    PTC_CHECK(cudaMemsetAsync(tr->d_res, 0, (size_t)T * D * 4, s));
+    const float invn = 1.0f / (float)(T - 1);
+    ptc::k_tr_ce_backward<<<n, 512, 0, s>>>(tr->logits, tr->tokens, V, invn, tr->d_logit);
+    // d_xb = d_logit . Wcls   [n x D], K = V
+    run_gemm(tr, G(n, D, V, tr->d_logit, V, true, tr->w.wcls, D, false, tr->d_xb, D, ptc::EPI_STORE));
+    const float *rfin = tr->res + (size_t)tr->L * T * D;
+    ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, rfin,
+                                                      tr->w.rms_final_weight, n, D);
+    ptc::k_tr_colsum_accum<<<(D + 127) / 128, 128, 0, s>>>(tr->g_rms_final, tr->dw_rows, n, D);
+    // dWcls += d_logit^T . x_final   [V x D], K = n
+    run_gemm(tr, G(V, D, n, tr->d_logit, V, false, tr->x_final, D, false, tr->g_wcls, D, ptc::EPI_ACCUM));
+    PTC_CHECK(cudaGetLastError());
+}
+
+// pt_backward_layers_range (pt_train.c:1173-1377)
+extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
+    const int T = tr->T, D = tr->D, H = tr->H, K = tr->K, nh = tr->nh, n = T - 1;
+    cudaStream_t s = tr->s;
+    for (int l = l1 - 1; l >= l0; l--) {
+        const size_t LD = (size_t)l * T * D, LK = (size_t)l * T * K, LH = (size_t)l * T * H;
+        const float *W1 = tr->w.w1 + (size_t)l * H * D, *W2 = tr->w.w2 + (size_t)l * D * H;
+        const float *W3 = tr->w.w3 + (size_t)l * H * D, *Wo = tr->w.wo + (size_t)l * D * D;
+        const float *Wq = tr->w.wq + (size_t)l * D * D, *Wk = tr->w.wk + (size_t)l * K * D;
+        const float *Wv = tr->w.wv + (size_t)l * K * D;
+        // FFN
+        ptc::k_tr_silu_gate<<<blocks_for((size_t)n * H, 256, tr->n_sm), 256, 0, s>>>(tr->sh, tr->hb + LH,
+                                                                                      tr->hb2 + LH, (size_t)n * H);
+        run_gemm(tr, G(n, H, D, tr->d_res, D, true, W2, H, false, tr->d_hid, H, ptc::EPI_STORE));
+        run_gemm(tr, G(D, H, n, tr->d_res, D, false, tr->sh, H, false, tr->g_w2 + (size_t)l * D * H, H,
+                       ptc::EPI_ACCUM));
+        ptc::k_tr_silu_bwd<<<blocks_for((size_t)n * H, 256, tr->n_sm), 256, 0, s>>>(
+            tr->d_hid, tr->d_hid2, tr->hb + LH, tr->hb2 + LH, (size_t)n * H);
+        run_gemm(tr, G(n, D, H, tr->d_hid, H, true, W1, D, false, tr->d_xb, D, ptc::EPI_STORE));
+        run_gemm(tr, G(n, D, H, tr->d_hid2, H, true, W3, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
+        run_gemm(tr, G(H, D, n, tr->d_hid, H, false, tr->xb_ffn + LD, D, false, tr->g_w1 + (size_t)l * H * D, D,
+                       ptc::EPI_ACCUM));
+        run_gemm(tr, G(H, D, n, tr->d_hid2, H, false, tr->xb_ffn + LD, D, false, tr->g_w3 + (size_t)l * H * D, D,
+                       ptc::EPI_ACCUM));
+        ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res_att + LD,
+                                                          tr->w.rms_ffn_weight + (size_t)l * D, n, D);
+        ptc::k_tr_colsum_accum<<<(D + 127) / 128, 128, 0, s>>>(tr->g_rms_ffn + (size_t)l * D, tr->dw_rows, n, D);
+        // wo
+        run_gemm(tr, G(n, D, D, tr->d_res, D, true, Wo, D, false, tr->d_aout, D, ptc::EPI_STORE));
+        run_gemm(tr, G(D, D, n, tr->d_res, D, false, tr->att_out + LD, D, false, tr->g_wo + (size_t)l * D * D, D,
+                       ptc::EPI_ACCUM));
+        // attention
+        const size_t smem = (size_t)(tr->hd + T) * 4;
+        const float *att_l = tr->att + (size_t)l * nh * T * T;
+        ptc::k_tr_attn_bwd_q<<<dim3(nh, n), 128, smem, s>>>(tr->d_aout, att_l, tr->q + LD, tr->k + LK, tr->v + LK,
+                                                            tr->dS, tr->d_q, T, nh, tr->nkv, tr->hd);
+        ptc::k_tr_attn_bwd_kv<<<dim3(tr->nkv, n), 64, 0, s>>>(tr->d_aout, att_l, tr->q + LD, tr->dS, tr->d_k,
+                                                              tr->d_v, T, n, nh, tr->nkv, tr->hd);
+        ptc::k_tr_rope_bwd<<<blocks_for((size_t)n * D / 2, 256, tr->n_sm), 256, 0, s>>>(
+            tr->d_qpre, tr->d_kpre, tr->d_q, tr->d_k, n, D, K, tr->hd);
+        run_gemm(tr, G(n, D, D, tr->d_qpre, D, true, Wq, D, false, tr->d_xb, D, ptc::EPI_STORE));
+        run_gemm(tr, G(n, D, K, tr->d_kpre, K, true, Wk, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
+        run_gemm(tr, G(n, D, K, tr->d_v, K, true, Wv, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
+        const float *xa = tr->xb_att + LD;
+        run_gemm(tr, G(D, D, n, tr->d_qpre, D, false, xa, D, false, tr->g_wq + (size_t)l * D * D, D, ptc::EPI_ACCUM));
+        run_gemm(tr, G(K, D, n, tr->d_kpre, K, false, xa, D, false, tr->g_wk + (size_t)l * K * D, D, ptc::EPI_ACCUM));
+        run_gemm(tr, G(K, D, n, tr->d_v, K, false, xa, D, false, tr->g_wv + (size_t)l * K * D, D, ptc::EPI_ACCUM));
+        ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res + LD,
+                                                          tr->w.rms_att_weight + (size_t)l * D, n, D);
+        ptc::k_tr_colsum_accum<<<(D + 127) / 128, 128, 0, s>>>(tr->g_rms_att + (size_t)l * D, tr->dw_rows, n, D);
+    }
+    PTC_CHECK(cudaGetLastError());
+}
+
+// pt_backward_embed (pt_train.c:1379-1383)
+extern "C" void ptc_trainer_bwd_embed(ptc_trainer *tr) {
+    if (!tr->has_embed) PTC_FATAL("trainer has no embedding");
+    const int n = tr->T - 1;
+    ptc::k_tr_embed_bwd<<<blocks_for((size_t)n * tr->D, 256, tr->n_sm), 256, 0, tr->s>>>(
+        tr->g_emb, tr->d_res, tr->tokens, n, tr->D);
+    PTC_CHECK(cudaGetLastError());
+}
+
+static void sgd_range(ptc_trainer *tr, const float *w, const float *g, size_t n, float lr) {
+    if (!n || !w || !g) return;
+    ptc::k_tr_sgd<<<blocks_for(n, 256, tr->n_sm), 256, 0, tr->s>>>((float *)w, g, n, lr);
+}
+
+// pt_sgd_update_layers (pt_train.c:902-929)
+extern "C" void ptc_trainer_sgd_layers(ptc_trainer *tr, float lr, int l0, int l1) {
+    const size_t D = tr->D, H = tr->H, K = tr->K, n = (size_t)(l1 - l0);
+    if (n == 0) return;
+    sgd_range(tr, tr->w.rms_att_weight + l0 * D, tr->g_rms_att + l0 * D, n * D, lr);
+    sgd_range(tr, tr->w.wq + l0 * D * D, tr->g_wq + l0 * D * D, n * D * D, lr);
+    sgd_range(tr, tr->w.wk + l0 * K * D, tr->g_wk + l0 * K * D, n * K * D, lr);
+    sgd_range(tr, tr->w.wv + l0 * K * D, tr->g_wv + l0 * K * D, n * K * D, lr);
+    sgd_range(tr, tr->w.wo + l0 * D * D, tr->g_wo + l0 * D * D, n * D * D, lr);
+    sgd_range(tr, tr->w.rms_ffn_weight + l0 * D, tr->g_rms_ffn + l0 * D, n * D, lr);
+    sgd_range(tr, tr->w.w1 + l0 * H * D, tr->g_w1 + l0 * H * D, n * H * D, lr);
+    sgd_range(tr, tr->w.w2 + l0 * D * H, tr->g_w2 + l0 * D * H, n * D * H, lr);
+    sgd_range(tr, tr->w.w3 + l0 * H * D, tr->g_w3 + l0 * H * D, n * H * D, lr);
+    PTC_CHECK(cudaGetLastError());
+}
+
+// pt_sgd_update_head (pt_train.c:935-942)
+extern "C" void ptc_trainer_sgd_head(ptc_trainer *tr, float lr) {
+    const size_t D = tr->D, V = tr->V;
+    if (tr->has_embed) sgd_range(tr, tr->w.token_embedding, tr->g_emb, V * D, lr);
+    if (tr->has_head) {
+        sgd_range(tr, tr->w.rms_final_weight, tr->g_rms_final, D, lr);
+        if (tr->g_wcls && tr->g_wcls != tr->g_emb) sgd_range(tr, tr->w.wcls, tr->g_wcls, V * D, lr);
+    }
+    PTC_CHECK(cudaGetLastError());
+}
+
+// pt_train_step (pitorch/pt.c:339-364) on a full-model trainer.
+extern "C" float ptc_trainer_step(ptc_trainer *tr, const int *tokens, int T, float lr) {
+    if (!tr->has_embed || !tr->has_head) PTC_FATAL("ptc_trainer_step needs embedding and head");
+    ptc_trainer_set_tokens(tr, tokens, T);
+    ptc_trainer_zero_grads(tr);
+    ptc_trainer_fwd_embed(tr);
+    ptc_trainer_fwd_layers(tr, 0, tr->L);
+    const float loss = ptc_trainer_fwd_head(tr);
+    ptc_trainer_bwd_head(tr);
+    ptc_trainer_bwd_layers(tr, 0, tr->L);
+    ptc_trainer_bwd_embed(tr);
+    ptc_trainer_sgd_head(tr, lr);
+    ptc_trainer_sgd_layers(tr, lr, 0, tr->L);
+    PTC_CHECK(cudaStreamSynchronize(tr->s));
+    return loss;
+}
+
+extern "C" void ptc_trainer_sync(ptc_trainer *tr) { PTC_CHECK(cudaStreamSynchronize(tr->s)); }
