@@ -43,6 +43,17 @@ struct DecodeModel {
     int att_chunk;   // positions per attention CTA
     int n_chunks;    // ceil(seq / att_chunk)
     StepState *step;
+    int *err;        // set (non-zero) by a kernel whose bounded wait expired
 };
+
+// Decode matvec staging: each CTA streams its contiguous block of weight rows
+// through a ring of shared-memory stages filled by bulk (TMA) copies.
+constexpr int MV_THREADS = 256;
+constexpr int MV_STAGES = 4;
+constexpr int MV_STAGE_BYTES = 24 * 1024;
+constexpr int MV_SMEM_BYTES = MV_STAGES * MV_STAGE_BYTES + MV_STAGES * 8;
+
+// Error codes written to DecodeModel::err.
+constexpr int ERR_MBAR_TIMEOUT = 1;
 
 }  // namespace ptc

@@ -21,6 +21,8 @@
 #include "ptc_decode.cuh"
 #include "ptc_internal.h"
 
+#include <string.h>
+
 #include <utility>
 
 namespace ptc {
@@ -94,75 +96,6 @@ __device__ __forceinline__ void store_vec(float *dst, const float4 (&x)[NV], int
     }
 }
 
-__device__ __forceinline__ const float *qkv_row(const DecodeModel &m, int l, int r) {
-    size_t D = m.dim, K = m.kvd;
-    if (r < m.dim) return m.wq + (size_t)l * D * D + (size_t)r * D;
-    r -= m.dim;
-    if (r < m.kvd) return m.wk + (size_t)l * K * D + (size_t)r * D;
-    r -= m.kvd;
-    return m.wv + (size_t)l * K * D + (size_t)r * D;
-}
-
-// ---------------------------------------------------------------------------
-// k_qkv: one warp per row pair (2j, 2j+1) of [wq; wk; wv]. Pairs never
-// straddle q/k/v (dim and kv_dim are even), so RoPE (pt_ops.c:33-49) is
-// applied in the epilogue and k/v go straight into the cache slot of pos.
-// Layer 0 reads its input from the token's embedding row and publishes it
-// as the residual stream x (llama2.c:220-222).
-// ---------------------------------------------------------------------------
-template <int NV>
-__global__ void __launch_bounds__(256) k_qkv(DecodeModel m, int l, int from_embedding) {
-    pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    const int pair = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int c4 = m.dim >> 2;
-    const int r0 = 2 * pair;
-    const bool active = r0 < m.dim + 2 * m.kvd;
-    float4 w0[NV], w1[NV];
-    if (active) {
-        load_row<NV>(w0, qkv_row(m, l, r0), c4, lane);
-        load_row<NV>(w1, qkv_row(m, l, r0 + 1), c4, lane);
-    }
-    pdl_wait();
-    if (!active) return;
-    const int pos = __ldcg(&m.step->pos);
-    if (pos < 0 || pos >= m.seq) return;  // stepped past the cache: no writes
-    float4 xr[NV];
-    if (from_embedding) {
-        const int tok = __ldcg(&m.step->tok);
-        load_act<NV>(xr, m.emb + (size_t)tok * m.dim, c4, lane);
-        if (pair == 0) store_vec<NV>(m.x, xr, c4, lane);
-    } else {
-        load_act<NV>(xr, m.x, c4, lane);
-    }
-    rmsnorm_regs<NV>(xr, m.rms_att + (size_t)l * m.dim, m.dim, lane);
-    const float a0 = row_dot<NV>(w0, xr);
-    const float a1 = row_dot<NV>(w1, xr);
-    if (lane != 0) return;
-    const int hd = m.hd;
-    if (r0 < m.dim + m.kvd) {
-        const bool is_q = r0 < m.dim;
-        const int i = is_q ? r0 : r0 - m.dim;
-        const float th = rope_theta(i, hd, pos);
-        const float c = pt_cosf(th), s = pt_sinf(th);
-        const float o0 = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s));
-        const float o1 = __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c));
-        if (is_q) {
-            m.q[i] = o0;
-            m.q[i + 1] = o1;
-        } else {
-            float *dst = m.kc + (((size_t)l * m.nkv + i / hd) * m.seq + pos) * hd + (i % hd);
-            dst[0] = o0;
-            dst[1] = o1;
-        }
-    } else {
-        const int i = r0 - m.dim - m.kvd;
-        float *dst = m.vc + (((size_t)l * m.nkv + i / hd) * m.seq + pos) * hd + (i % hd);
-        dst[0] = a0;
-        dst[1] = a1;
-    }
-}
-
 // ---------------------------------------------------------------------------
 // k_attn: grid (n_heads, n_chunks), 256 threads. CTA (h, c) covers positions
 // [c*CH, c*CH+CH) ∩ [0, pos] (CH = 64): scores q.k * 1/sqrt(hd), a
@@ -177,7 +110,7 @@ constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAX_HD = 256;
 constexpr int ATT_MAX_CHUNKS = 256;
 
-__global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
+__global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     pdl_trigger();
     __shared__ __align__(16) float s_q[ATT_MAX_HD];
     __shared__ float s_p[ATT_MAX_CHUNKS];
@@ -198,7 +131,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
     const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
     float *part = m.att_part + ((size_t)h * m.n_chunks + c) * (hd + 2);
 
-    if (t0 <= pos) {
+    const int nc = pos / CH + 1;   // chunks holding positions <= pos
+    if (c >= nc) return;           // no positions here: not part of the merge
+    {
         const int n = min(CH, pos + 1 - t0);
         for (int d = tid; d < hd; d += ATT_THREADS) s_q[d] = __ldcg(m.q + h * hd + d);
         __syncthreads();
@@ -245,6 +180,15 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
             }
         }
         __syncthreads();
+        if (nc == 1) {   // one chunk: normalise and finish here
+            const float inv = __fdiv_rn(1.0f, s_stat[1]);
+            for (int d = tid; d < hd; d += ATT_THREADS) {
+                float o = 0.f;
+                for (int g = 0; g < ngrp; g++) o += s_o[g * hd + d];
+                m.att[h * hd + d] = o * inv;
+            }
+            return;
+        }
         for (int d = tid; d < hd; d += ATT_THREADS) {
             float o = 0.f;
             for (int g = 0; g < ngrp; g++) o += s_o[g * hd + d];
@@ -256,13 +200,12 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
     if (tid == 0) {
         __threadfence();
         const unsigned ticket = atomicAdd(&m.att_ticket[h], 1u);
-        s_last = (ticket == gridDim.y - 1);
+        s_last = (ticket == (unsigned)nc - 1);
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
     // Merge the nc chunk partials of this head.
-    const int nc = pos / CH + 1;
     const float *hp = m.att_part + (size_t)h * m.n_chunks * (hd + 2);
     for (int k = tid; k < nc; k += ATT_THREADS) s_p[k] = __ldcg(hp + (size_t)k * (hd + 2) + hd);
     __syncthreads();
@@ -304,120 +247,215 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(DecodeModel m, int l) {
 }
 
 // ---------------------------------------------------------------------------
-// k_resid: x[r] += W[r] . in, one warp per row (wo with in = att, w2 with
-// in = hb); the residual add of llama2.c:277 / :287.
+// k_mv: the decode matvecs. Grid = one CTA per SM; CTA b owns a contiguous
+// block of "items" (a row, or a row pair) and streams the item rows through
+// MV_STAGES shared-memory stages with bulk (TMA) copies signalled on
+// mbarriers. The first stages are issued BEFORE griddepcontrol.wait: weights
+// never depend on the previous kernel, so under programmatic dependent
+// launch this kernel's weight stream overlaps the tail of the previous one.
+// After the wait the CTA loads the (small) input vector from L2 into
+// registers, and each warp reduces its items from shared memory.
+//
+//   MV_QKV    item = row pair (2j, 2j+1) of [wq; wk; wv]; rmsnorm(x) in;
+//             RoPE epilogue, k/v into the KV cache slot of pos
+//             (llama2.c:238-248). Layer 0 reads the token's embedding row.
+//   MV_FFN13  item = hidden unit i: rows w1[i], w3[i]; rmsnorm(x) in;
+//             hb[i] = silu(h1) * h3 (llama2.c:280-285)
+//   MV_RESID  item = row r of W (wo or w2); x[r] += W[r] . in (:276-277, :286-287)
+//   MV_CLS    item = vocab row r; rmsnorm(x, rms_final) in; logits[r] and a
+//             greedy argmax (llama2.c:293-294, pt.c:270)
 // ---------------------------------------------------------------------------
-template <int NV>
-__global__ void __launch_bounds__(128) k_resid(DecodeModel m, const float *W, const float *in,
-                                               int rows, int cols) {
-    pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int c4 = cols >> 2;
-    const bool active = r < rows;
-    float4 w[NV];
-    if (active) load_row<NV>(w, W + (size_t)r * cols, c4, lane);
-    pdl_wait();
-    if (!active) return;
-    float4 xr[NV];
-    load_act<NV>(xr, in, c4, lane);
-    const float a = row_dot<NV>(w, xr);
-    if (lane == 0) m.x[r] = __fadd_rn(__ldcg(m.x + r), a);
-}
+enum MvMode { MV_QKV = 0, MV_FFN13 = 1, MV_RESID = 2, MV_CLS = 3 };
 
-// ---------------------------------------------------------------------------
-// k_ffn13: one warp per hidden unit i: rmsnorm(x) . w1[i] and . w3[i], then
-// hb[i] = silu(h1) * h3 (llama2.c:280-285).
-// ---------------------------------------------------------------------------
-template <int NV>
-__global__ void __launch_bounds__(256) k_ffn13(DecodeModel m, int l) {
-    pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int c4 = m.dim >> 2;
-    const bool active = i < m.hidden;
-    float4 wa[NV], wb[NV];
-    if (active) {
-        const size_t off = (size_t)l * m.hidden * m.dim + (size_t)i * m.dim;
-        load_row<NV>(wa, m.w1 + off, c4, lane);
-        load_row<NV>(wb, m.w3 + off, c4, lane);
+struct MvArgs {
+    const float *W;    // MV_RESID: the matrix; MV_CLS: wcls
+    const float *in;   // MV_RESID input vector
+    int n_items;       // items over the whole grid
+    int cols;          // row length in floats
+    int slots;         // rows per item
+    int per_stage;     // items per shared-memory stage
+    int l;             // layer
+    int from_embedding;
+};
+
+template <int MODE>
+__device__ __forceinline__ void mv_issue(const DecodeModel &m, const MvArgs &a, float *stage, uint64_t *bar,
+                                         int c0, int c1) {
+    const size_t rb = (size_t)a.cols * 4;  // bytes per row
+    const int n = c1 - c0;
+    if (MODE == MV_QKV) {
+        // virtual rows [2c0, 2c1) of [wq; wk; wv], split at the matrix edges
+        const size_t D = m.dim, K = m.kvd;
+        const float *base[3] = {m.wq + (size_t)a.l * D * D, m.wk + (size_t)a.l * K * D,
+                                m.wv + (size_t)a.l * K * D};
+        const int edge[4] = {0, m.dim, m.dim + m.kvd, m.dim + 2 * m.kvd};
+        mbar_expect_tx(bar, (unsigned)(2 * n * rb));
+        const int r0 = 2 * c0, r1 = 2 * c1;
+        for (int s = 0; s < 3; s++) {
+            const int lo = max(r0, edge[s]), hi = min(r1, edge[s + 1]);
+            if (lo < hi)
+                bulk_g2s(stage + (size_t)(lo - r0) * a.cols, base[s] + (size_t)(lo - edge[s]) * a.cols,
+                         (unsigned)((hi - lo) * rb), bar);
+        }
+    } else if (MODE == MV_FFN13) {
+        const size_t off = (size_t)a.l * m.hidden * m.dim + (size_t)c0 * m.dim;
+        mbar_expect_tx(bar, (unsigned)(2 * n * rb));
+        bulk_g2s(stage, m.w1 + off, (unsigned)(n * rb), bar);
+        bulk_g2s(stage + (size_t)a.per_stage * a.cols, m.w3 + off, (unsigned)(n * rb), bar);
+    } else {
+        mbar_expect_tx(bar, (unsigned)(n * rb));
+        bulk_g2s(stage, a.W + (size_t)c0 * a.cols, (unsigned)(n * rb), bar);
     }
-    pdl_wait();
-    if (!active) return;
-    float4 xr[NV];
-    load_act<NV>(xr, m.x, c4, lane);
-    rmsnorm_regs<NV>(xr, m.rms_ffn + (size_t)l * m.dim, m.dim, lane);
-    const float h1 = row_dot<NV>(wa, xr);
-    const float h3 = row_dot<NV>(wb, xr);
-    if (lane == 0) m.hb[i] = silu_mul(h1, h3);
 }
 
-// ---------------------------------------------------------------------------
-// k_cls: final rmsnorm + logits = wcls . x over the vocab rows, with the
-// greedy argmax folded in (pitorch/pt.c:267-271). Warps stride over row
-// pairs; each CTA publishes its best (value, index) key with one 64-bit
-// atomicMax; the last CTA to finish records the token and, in device-loop
-// mode, advances the position (teacher-forcing prompt tokens as the
-// reference's decode loops do, pitorch/text/pt_text.c:343-347).
-// ---------------------------------------------------------------------------
 template <int NV>
-__global__ void __launch_bounds__(256) k_cls(DecodeModel m) {
+__device__ __forceinline__ float smem_row_dot(const float *row, const float4 (&x)[NV], int c4, int lane) {
+    const float4 *r4 = reinterpret_cast<const float4 *>(row);
+    float acc = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const int c = lane + 32 * v;
+        if (c < c4) acc = dot4(r4[c], x[v], acc);
+    }
+    return warp_sum(acc);
+}
+
+template <int NV, int MODE>
+__global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     pdl_trigger();
-    __shared__ unsigned long long s_best[8];
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float *stages = reinterpret_cast<float *>(smem_raw);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw + MV_STAGES * MV_STAGE_BYTES);
+    __shared__ unsigned long long s_best[MV_THREADS / 32];
     __shared__ int s_last;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int nw = (gridDim.x * blockDim.x) >> 5;
-    const int c4 = m.dim >> 2;
-    const int V = m.V;
-    float4 w0[NV], w1[NV];
-    int r = 2 * gw;
-    if (r < V) {
-        load_row<NV>(w0, m.wcls + (size_t)r * m.dim, c4, lane);
-        if (r + 1 < V) load_row<NV>(w1, m.wcls + (size_t)(r + 1) * m.dim, c4, lane);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = MV_THREADS / 32;
+    const int it0 = (int)((long)a.n_items * blockIdx.x / gridDim.x);
+    const int it1 = (int)((long)a.n_items * (blockIdx.x + 1) / gridDim.x);
+    const int ps = a.per_stage;
+    const int n_chunks = (it1 - it0 + ps - 1) / ps;
+    const int stage_floats = MV_STAGE_BYTES / 4;
+    const int c4 = a.cols >> 2;
+
+    if (tid == 0) {
+        for (int s = 0; s < MV_STAGES; s++) mbar_init(&bars[s], 1);
+        mbar_init_fence();
     }
+    __syncthreads();
+    if (tid == 0)
+        for (int k = 0; k < n_chunks && k < MV_STAGES; k++)
+            mv_issue<MODE>(m, a, stages + k * stage_floats, &bars[k], it0 + k * ps, min(it1, it0 + (k + 1) * ps));
+
     pdl_wait();
+    int pos = 0;
+    if (MODE == MV_QKV) pos = __ldcg(&m.step->pos);
     float4 xr[NV];
-    load_act<NV>(xr, m.x, c4, lane);
-    rmsnorm_regs<NV>(xr, m.rms_final, m.dim, lane);
-    if (gw == 0) store_vec<NV>(m.xn, xr, c4, lane);
+    if (MODE == MV_QKV) {
+        if (a.from_embedding) {
+            const int tok = __ldcg(&m.step->tok);
+            load_act<NV>(xr, m.emb + (size_t)tok * m.dim, c4, lane);
+            if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.x, xr, c4, lane);
+        } else {
+            load_act<NV>(xr, m.x, c4, lane);
+        }
+        rmsnorm_regs<NV>(xr, m.rms_att + (size_t)a.l * m.dim, m.dim, lane);
+    } else if (MODE == MV_FFN13) {
+        load_act<NV>(xr, m.x, c4, lane);
+        rmsnorm_regs<NV>(xr, m.rms_ffn + (size_t)a.l * m.dim, m.dim, lane);
+    } else if (MODE == MV_CLS) {
+        load_act<NV>(xr, m.x, c4, lane);
+        rmsnorm_regs<NV>(xr, m.rms_final, m.dim, lane);
+        if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.xn, xr, c4, lane);
+    } else {
+        load_act<NV>(xr, a.in, c4, lane);
+    }
+    const bool pos_ok = (MODE != MV_QKV) || (pos >= 0 && pos < m.seq);
 
     unsigned long long best = 0ull;
-    while (r < V) {
-        const float a0 = row_dot<NV>(w0, xr);
-        const float a1 = (r + 1 < V) ? row_dot<NV>(w1, xr) : 0.f;
-        if (lane == 0) {
-            m.logits[r] = a0;
-            unsigned long long k0 = argmax_key(a0, r);
-            if (k0 > best) best = k0;
-            if (r + 1 < V) {
-                m.logits[r + 1] = a1;
-                unsigned long long k1 = argmax_key(a1, r + 1);
-                if (k1 > best) best = k1;
+    bool ok = true;
+    for (int k = 0; k < n_chunks; k++) {
+        const int s = k % MV_STAGES;
+        const float *stage = stages + s * stage_floats;
+        const bool got = mbar_wait_bounded(&bars[s], (unsigned)((k / MV_STAGES) & 1), m.err, ERR_MBAR_TIMEOUT);
+        if (__syncthreads_or(!got)) {   // block-uniform give-up
+            ok = false;
+            if (tid == 0)   // let copies still in flight land before the CTA exits
+                for (int kk = k + 1; kk < n_chunks && kk < k + MV_STAGES; kk++)
+                    mbar_wait_bounded(&bars[kk % MV_STAGES], (unsigned)((kk / MV_STAGES) & 1), nullptr, 0);
+            break;
+        }
+        const int c0 = it0 + k * ps, c1 = min(it1, c0 + ps);
+        for (int i = c0 + warp; i < c1; i += NW) {
+            const int li = i - c0;
+            if (MODE == MV_QKV) {
+                const float a0 = smem_row_dot<NV>(stage + (size_t)(2 * li) * a.cols, xr, c4, lane);
+                const float a1 = smem_row_dot<NV>(stage + (size_t)(2 * li + 1) * a.cols, xr, c4, lane);
+                if (lane == 0 && pos_ok) {
+                    const int r0 = 2 * i, hd = m.hd;
+                    if (r0 < m.dim + m.kvd) {
+                        const bool is_q = r0 < m.dim;
+                        const int j = is_q ? r0 : r0 - m.dim;
+                        const float th = rope_theta(j, hd, pos);
+                        const float cs = pt_cosf(th), sn = pt_sinf(th);
+                        const float o0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+                        const float o1 = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+                        if (is_q) {
+                            m.q[j] = o0;
+                            m.q[j + 1] = o1;
+                        } else {
+                            float *dst = m.kc + (((size_t)a.l * m.nkv + j / hd) * m.seq + pos) * hd + (j % hd);
+                            dst[0] = o0;
+                            dst[1] = o1;
+                        }
+                    } else {
+                        const int j = r0 - m.dim - m.kvd;
+                        float *dst = m.vc + (((size_t)a.l * m.nkv + j / hd) * m.seq + pos) * hd + (j % hd);
+                        dst[0] = a0;
+                        dst[1] = a1;
+                    }
+                }
+            } else if (MODE == MV_FFN13) {
+                const float h1 = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
+                const float h3 = smem_row_dot<NV>(stage + (size_t)(ps + li) * a.cols, xr, c4, lane);
+                if (lane == 0) m.hb[i] = silu_mul(h1, h3);
+            } else if (MODE == MV_RESID) {
+                const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
+                if (lane == 0) m.x[i] = __fadd_rn(__ldcg(m.x + i), v);
+            } else {
+                const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
+                if (lane == 0) {
+                    m.logits[i] = v;
+                    const unsigned long long key = argmax_key(v, i);
+                    if (key > best) best = key;
+                }
             }
         }
-        r += 2 * nw;
-        if (r < V) {
-            load_row<NV>(w0, m.wcls + (size_t)r * m.dim, c4, lane);
-            if (r + 1 < V) load_row<NV>(w1, m.wcls + (size_t)(r + 1) * m.dim, c4, lane);
+        __syncthreads();
+        if (tid == 0 && k + MV_STAGES < n_chunks) {
+            fence_proxy_async_smem();
+            const int kk = k + MV_STAGES;
+            mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps));
         }
     }
+    (void)ok;
+    if (MODE != MV_CLS) return;
+
     if (lane == 0) s_best[warp] = best;
     __syncthreads();
     StepState *st = m.step;
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         unsigned long long b = 0ull;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) b = (s_best[w] > b) ? s_best[w] : b;
+        for (int w = 0; w < NW; w++) b = s_best[w] > b ? s_best[w] : b;
         if (b) atomicMax(&st->amax, b);
         __threadfence();
-        unsigned ticket = atomicAdd(&st->done, 1u);
+        const unsigned ticket = atomicAdd(&st->done, 1u);
         s_last = (ticket == gridDim.x - 1);
     }
     __syncthreads();
-    if (!s_last || threadIdx.x != 0) return;
+    if (!s_last || tid != 0) return;
     __threadfence();
-    const unsigned long long k = atomicAdd(&st->amax, 0ull);
-    const int next = argmax_key_index(k);
+    const unsigned long long key = atomicAdd(&st->amax, 0ull);
+    const int next = argmax_key_index(key);
     st->next = next;
     st->amax = 0ull;
     st->done = 0u;
@@ -459,42 +497,79 @@ static inline int nv_of(int cols) { return (cols / 4 + 31) / 32; }
 
 // Launch with the programmatic-stream-serialization attribute so that
 // consecutive decode kernels overlap (prologue of N+1 with tail of N).
+// PTC_NO_PDL=1 disables programmatic dependent launch (for A/B timing).
+static bool pdl_on() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("PTC_NO_PDL");
+        on = (e && e[0] == '1') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 template <typename... KArgs, typename... Args>
-static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
+static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                        Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_on() ? 1 : 0;
     PTC_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
-void launch_layer(const DecodeModel &m, int l, bool from_embedding, cudaStream_t s) {
+template <int NV, int MODE>
+static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) {
+    static bool configured = false;  // per instantiation
+    if (!configured) {
+        PTC_CHECK(cudaFuncSetAttribute(k_mv<NV, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       MV_SMEM_BYTES));
+        configured = true;
+    }
+    const int item_bytes = a.slots * a.cols * 4;
+    a.per_stage = MV_STAGE_BYTES / item_bytes;
+    if (a.per_stage < 1) PTC_FATAL("decode row of %d floats does not fit a staging buffer", a.cols);
+    const int grid = a.n_items < n_sm ? a.n_items : n_sm;
+    launch_pdl(k_mv<NV, MODE>, dim3(grid), dim3(MV_THREADS), (size_t)MV_SMEM_BYTES, s, m, a);
+}
+
+static MvArgs mv_args(int n_items, int cols, int slots, int l) {
+    MvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.n_items = n_items;
+    a.cols = cols;
+    a.slots = slots;
+    a.l = l;
+    return a;
+}
+
+void launch_layer(const DecodeModel &m, int l, bool from_embedding, int n_sm, cudaStream_t s) {
     const int nvd = nv_of(m.dim), nvh = nv_of(m.hidden);
-    const int pairs = (m.dim + 2 * m.kvd) / 2;
-    PTC_NV_SWITCH(nvd, launch_pdl(k_qkv<NV>, dim3((pairs + 7) / 8), dim3(256), s, m, l,
-                                  from_embedding ? 1 : 0));
-    launch_pdl(k_attn, dim3(m.nh, m.n_chunks), dim3(ATT_THREADS), s, m, l);
-    const float *wo = m.wo + (size_t)l * m.dim * m.dim;
-    PTC_NV_SWITCH(nvd, launch_pdl(k_resid<NV>, dim3((m.dim + 3) / 4), dim3(128), s, m, wo,
-                                  (const float *)m.att, m.dim, m.dim));
-    PTC_NV_SWITCH(nvd, launch_pdl(k_ffn13<NV>, dim3((m.hidden + 7) / 8), dim3(256), s, m, l));
-    const float *w2 = m.w2 + (size_t)l * m.dim * m.hidden;
-    PTC_NV_SWITCH(nvh, launch_pdl(k_resid<NV>, dim3((m.dim + 3) / 4), dim3(128), s, m, w2,
-                                  (const float *)m.hb, m.dim, m.hidden));
+    MvArgs a = mv_args((m.dim + 2 * m.kvd) / 2, m.dim, 2, l);
+    a.from_embedding = from_embedding ? 1 : 0;
+    PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_QKV>(m, a, n_sm, s)));
+    launch_pdl(k_attn, dim3(m.nh, m.n_chunks), dim3(ATT_THREADS), 0, s, m, l);
+    a = mv_args(m.dim, m.dim, 1, l);
+    a.W = m.wo + (size_t)l * m.dim * m.dim;
+    a.in = m.att;
+    PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_RESID>(m, a, n_sm, s)));
+    a = mv_args(m.hidden, m.dim, 2, l);
+    PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_FFN13>(m, a, n_sm, s)));
+    a = mv_args(m.dim, m.hidden, 1, l);
+    a.W = m.w2 + (size_t)l * m.dim * m.hidden;
+    a.in = m.hb;
+    PTC_NV_SWITCH(nvh, (launch_mv<NV, MV_RESID>(m, a, n_sm, s)));
 }
 
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s) {
-    const int nvd = nv_of(m.dim);
-    int blocks = (m.V / 2 + 7) / 8;
-    if (blocks > 2 * n_sm) blocks = 2 * n_sm;
-    PTC_NV_SWITCH(nvd, launch_pdl(k_cls<NV>, dim3(blocks), dim3(256), s, m));
+    MvArgs a = mv_args(m.V, m.dim, 1, 0);
+    a.W = m.wcls;
+    PTC_NV_SWITCH(nv_of(m.dim), (launch_mv<NV, MV_CLS>(m, a, n_sm, s)));
 }
 
 // x = token_embedding[tok] (llama2.c:220-222) for a decoder whose layer 0
@@ -508,7 +583,7 @@ __global__ void k_embed(DecodeModel m) {
 }
 
 void launch_embed(const DecodeModel &m, cudaStream_t s) {
-    launch_pdl(k_embed, dim3((m.dim + 255) / 256), dim3(256), s, m);
+    launch_pdl(k_embed, dim3((m.dim + 255) / 256), dim3(256), 0, s, m);
 }
 
 int decode_attn_limits_ok(int hd, int chunk, int n_chunks) {

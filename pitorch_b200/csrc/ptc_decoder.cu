@@ -36,15 +36,10 @@ struct ptc_decoder {
     cudaGraphExec_t g_host, g_dev;
 };
 
-static bool pdl_enabled() {
-    const char *e = getenv("PTC_NO_PDL");
-    return !(e && e[0] == '1');
-}
-
 static void enqueue_kernels(ptc_decoder *d, cudaStream_t s) {
     const DecodeModel &m = d->m;
     if (d->has_embed && m.L == 0) ptc::launch_embed(m, s);
-    for (int l = 0; l < m.L; l++) ptc::launch_layer(m, l, d->has_embed && l == 0, s);
+    for (int l = 0; l < m.L; l++) ptc::launch_layer(m, l, d->has_embed && l == 0, d->n_sm, s);
     if (d->has_head) ptc::launch_head(m, d->n_sm, s);
 }
 
@@ -62,6 +57,14 @@ static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
     PTC_CHECK(cudaGraphInstantiate(&ge, g, 0));
     PTC_CHECK(cudaGraphDestroy(g));
     return ge;
+}
+
+// A decode kernel whose bounded wait expired left a code in m.err; report it
+// at the next synchronisation point (the reference's panic analogue).
+static void check_err(ptc_decoder *d) {
+    int e = 0;
+    PTC_CHECK(cudaMemcpy(&e, d->m.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) PTC_FATAL("decode kernel reported error %d (bounded wait on a weight stage expired)", e);
 }
 
 static void set_mode(ptc_decoder *d, int mode) {
@@ -127,6 +130,7 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     m.att_part = (float *)ptc_alloc(c, (size_t)m.nh * m.n_chunks * (m.hd + 2) * 4);
     m.att_ticket = (unsigned *)ptc_alloc(c, (size_t)m.nh * 4);
     m.step = (StepState *)ptc_alloc(c, sizeof(StepState));
+    m.err = (int *)ptc_alloc(c, sizeof(int));
     d->d_tokens = (int *)ptc_alloc(c, (size_t)(m.seq + 1) * 4);
 
     cudaStream_t s = d->stream;
@@ -134,6 +138,7 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     PTC_CHECK(cudaMemsetAsync(m.kc, 0, kv ? kv : 4, s));
     PTC_CHECK(cudaMemsetAsync(m.vc, 0, kv ? kv : 4, s));
     PTC_CHECK(cudaMemsetAsync(m.att_ticket, 0, (size_t)m.nh * 4, s));
+    PTC_CHECK(cudaMemsetAsync(m.err, 0, sizeof(int), s));
     StepState st;
     memset(&st, 0, sizeof(st));
     st.tokens = d->d_tokens;
@@ -148,7 +153,6 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
 
     d->g_host = capture(d, true);
     d->g_dev = capture(d, false);
-    (void)pdl_enabled;
     return d;
 }
 
@@ -187,6 +191,7 @@ extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logit
     } else {
         PTC_CHECK(cudaStreamSynchronize(d->stream));
     }
+    if (d->io->next < 0 || d->io->next >= d->m.V) check_err(d);
     return d->has_head ? d->io->next : -1;
 }
 
@@ -233,6 +238,7 @@ extern "C" void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n) 
     // tokens[p + 1] is the token emitted at position p.
     PTC_CHECK(cudaMemcpyAsync(out_tokens, d->d_tokens + 1, (size_t)n * 4, cudaMemcpyDeviceToHost, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
+    check_err(d);
 }
 
 extern "C" void ptc_decoder_generate(ptc_decoder *d, const int *prompt, int n_prompt, int n_pos,
@@ -265,7 +271,7 @@ extern "C" void ptc_decoder_enqueue_layers(ptc_decoder *d, int pos, int l_start,
         PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
     set_mode(d, 0);
     put_step_int(d, &d->m.step->pos, pos);
-    for (int l = l_start; l < l_end; l++) ptc::launch_layer(d->m, l, false, d->stream);
+    for (int l = l_start; l < l_end; l++) ptc::launch_layer(d->m, l, false, d->n_sm, d->stream);
 }
 
 extern "C" void ptc_decoder_enqueue_head(ptc_decoder *d) {
@@ -280,5 +286,6 @@ extern "C" int ptc_decoder_fetch_next(ptc_decoder *d, float *logits_host) {
         PTC_CHECK(cudaMemcpyAsync(d->stage, d->m.logits, (size_t)d->m.V * 4, cudaMemcpyDeviceToHost, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     if (logits_host) memcpy(logits_host, d->stage, (size_t)d->m.V * 4);
+    check_err(d);
     return d->io->next;
 }

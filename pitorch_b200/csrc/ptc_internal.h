@@ -19,7 +19,7 @@ int ptc_ctx_device(ptc_ctx *c);
 
 namespace ptc {
 struct DecodeModel;
-void launch_layer(const DecodeModel &m, int l, bool from_embedding, cudaStream_t s);
+void launch_layer(const DecodeModel &m, int l, bool from_embedding, int n_sm, cudaStream_t s);
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s);
 void launch_embed(const DecodeModel &m, cudaStream_t s);
 int decode_attn_limits_ok(int hd, int chunk, int n_chunks);
