@@ -151,6 +151,22 @@ void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, int n_prompt)
 void ptc_decoder_enqueue_steps(ptc_decoder *d, int n);
 void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n);
 
+/* ---- GEMM: replaces sgemm_rect_tmu (pitorch/ops/gemm/gemm_rect.h:13-27,
+ *      gemm_rect.c:28-104), C[M][N] (+)= A[M][K] * B[K][N] -------------------- */
+
+/* fp32 GEMM on DEVICE pointers, asynchronous on `stream` (NULL = legacy
+ * default stream). Operand layouts cover the three products of a linear
+ * layer's training step:
+ *   a_kcontig != 0: A(m,k) = A[m*lda + k]   else A(m,k) = A[k*lda + m]
+ *   b_kcontig != 0: B(k,n) = B[n*ldb + k]   else B(k,n) = B[k*ldb + n]
+ * accumulate != 0 adds into C (the reference's accumulate=1), else C is
+ * overwritten. `workspace` (may be NULL) of workspace_floats floats lets
+ * long-K products split K across CTAs into partial sums reduced in a fixed
+ * order; with NULL the product runs unsplit. */
+void ptc_sgemm(int M, int N, int K, const float *A, int lda, int a_kcontig,
+               const float *B, int ldb, int b_kcontig, float *C, int ldc, int accumulate,
+               float *workspace, size_t workspace_floats, void *stream);
+
 /* ---- training: replaces pt_forward_train / pt_backward / pt_sgd_update
  *      and their staged variants (pitorch/train/pt_train.c:171-1383) -------- */
 

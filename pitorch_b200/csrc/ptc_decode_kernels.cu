@@ -523,12 +523,17 @@ static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     PTC_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
+__global__ void k_embed(DecodeModel m);
+
 template <int NV, int MODE>
 static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) {
     static bool configured = false;  // per instantiation
     if (!configured) {
         PTC_CHECK(cudaFuncSetAttribute(k_mv<NV, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        MV_SMEM_BYTES));
+        // Same (maximal) shared-memory carveout for every decode kernel, so
+        // consecutive kernels can co-reside on an SM without reconfiguring L1.
+        PTC_CHECK(cudaFuncSetAttribute(k_mv<NV, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
         configured = true;
     }
     const int item_bytes = a.slots * a.cols * 4;
@@ -553,6 +558,12 @@ void launch_layer(const DecodeModel &m, int l, bool from_embedding, int n_sm, cu
     MvArgs a = mv_args((m.dim + 2 * m.kvd) / 2, m.dim, 2, l);
     a.from_embedding = from_embedding ? 1 : 0;
     PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_QKV>(m, a, n_sm, s)));
+    static bool attn_configured = false;
+    if (!attn_configured) {
+        PTC_CHECK(cudaFuncSetAttribute(k_attn, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        PTC_CHECK(cudaFuncSetAttribute(k_embed, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        attn_configured = true;
+    }
     launch_pdl(k_attn, dim3(m.nh, m.n_chunks), dim3(ATT_THREADS), 0, s, m, l);
     a = mv_args(m.dim, m.dim, 1, l);
     a.W = m.wo + (size_t)l * m.dim * m.dim;

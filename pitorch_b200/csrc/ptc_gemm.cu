@@ -19,6 +19,10 @@
 #include "ptc_common.cuh"
 #include "ptc_gemm.h"
 
+#include <string.h>
+
+#include "../../include/ptc.h"
+
 namespace ptc {
 
 template <int BM, int BN, int BK, int TM, int TN, bool A_KC, bool B_KC>
@@ -208,3 +212,21 @@ void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
 }
 
 }  // namespace ptc
+
+extern "C" void ptc_sgemm(int M, int N, int K, const float *A, int lda, int a_kcontig, const float *B, int ldb,
+                          int b_kcontig, float *C, int ldc, int accumulate, float *workspace,
+                          size_t workspace_floats, void *stream) {
+    int dev = 0, n_sm = 148;
+    PTC_CHECK(cudaGetDevice(&dev));
+    PTC_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    ptc::GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.M = M; g.N = N; g.K = K;
+    g.A = A; g.lda = lda; g.a_kcontig = a_kcontig != 0;
+    g.B = B; g.ldb = ldb; g.b_kcontig = b_kcontig != 0;
+    g.C = C; g.ldc = ldc;
+    g.epi = accumulate ? ptc::EPI_ACCUM : ptc::EPI_STORE;
+    g.partial = workspace;
+    g.partial_cap = workspace ? workspace_floats : 0;
+    ptc::gemm(g, n_sm, (cudaStream_t)stream);
+}
