@@ -167,6 +167,29 @@ void ptc_sgemm(int M, int N, int K, const float *A, int lda, int a_kcontig,
                const float *B, int ldb, int b_kcontig, float *C, int ldc, int accumulate,
                float *workspace, size_t workspace_floats, void *stream);
 
+/* ptc_sgemm for callers that cannot allocate device memory -- no
+ * counterpart in the reference. Code that runs while a stream is being
+ * captured into a CUDA graph, inside an allocator callback, or under a host
+ * framework that owns all device allocations cannot call cudaMalloc and may
+ * have no workspace to pass. This variant takes only the caller's inputs and
+ * output; its split-K partial sums live in one static device array of
+ * PTC_SGEMM_NOALLOC_MAX_MN floats (4 MiB) that every GPU loading the library
+ * keeps until exit. Same product and layouts as ptc_sgemm.
+ *  - Returns 0 on success, -1 (with a message on stderr) when M*N exceeds
+ *    PTC_SGEMM_NOALLOC_MAX_MN or the device set-up fails.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) for that device; make that first call before
+ *    any stream capture.
+ *  - Calls never allocate (no cudaMalloc/cudaFree), but they all share the
+ *    one array: calls that overlap on the GPU (different streams, or other
+ *    threads) race on it and must be serialised by the caller.
+ *  - The array keeps the last call's partials; each call overwrites every
+ *    partial it reads, so nothing needs clearing between calls. */
+#define PTC_SGEMM_NOALLOC_MAX_MN (1u << 20)
+int ptc_sgemm_noalloc(int M, int N, int K, const float *A, int lda, int a_kcontig,
+                      const float *B, int ldb, int b_kcontig, float *C, int ldc, int accumulate,
+                      void *stream);
+
 /* ---- training: replaces pt_forward_train / pt_backward / pt_sgd_update
  *      and their staged variants (pitorch/train/pt_train.c:171-1383) -------- */
 

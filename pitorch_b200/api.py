@@ -137,6 +137,8 @@ def declare(L):
     _sig(L, "ptc_sm_count", C.c_int, vp)
     _sig(L, "ptc_matvec", None, vp, vp, vp, C.c_int, C.c_int, vp)
     _sig(L, "ptc_matvec_host", None, f32p, f32p, f32p, C.c_int, C.c_int)
+    _sig(L, "ptc_sgemm_noalloc", C.c_int, C.c_int, C.c_int, C.c_int, vp, C.c_int, C.c_int, vp, C.c_int,
+         C.c_int, vp, C.c_int, C.c_int, vp)
     _sig(L, "ptc_sgemm", None, C.c_int, C.c_int, C.c_int, vp, C.c_int, C.c_int, vp, C.c_int, C.c_int,
          vp, C.c_int, C.c_int, vp, C.c_size_t, vp)
     _sig(L, "ptc_decoder_generate_begin", None, vp, i32p, C.c_int)
