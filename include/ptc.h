@@ -151,6 +151,18 @@ void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, int n_prompt)
 void ptc_decoder_enqueue_steps(ptc_decoder *d, int n);
 void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n);
 
+/* Weights were updated in place (training): refresh derived device copies. */
+void ptc_decoder_weights_updated(ptc_decoder *d);
+/* 1 when the decoder runs each launch as the single persistent kernel. */
+int ptc_decoder_is_persistent(ptc_decoder *d);
+/* Phase timeline of the persistent kernel (profiling): record, for the
+ * first max_barriers grid barriers of each launch, when CTA 0 finished its
+ * phase work and when the barrier released (%globaltimer ns, 2 entries per
+ * barrier). max_barriers <= 0 turns it off. ptc_decoder_read_trace copies up
+ * to n entries out and returns how many. */
+void ptc_decoder_trace(ptc_decoder *d, int max_barriers);
+int ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, int n);
+
 /* ---- GEMM: replaces sgemm_rect_tmu (pitorch/ops/gemm/gemm_rect.h:13-27,
  *      gemm_rect.c:28-104), C[M][N] (+)= A[M][K] * B[K][N] -------------------- */
 

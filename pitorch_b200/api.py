@@ -145,6 +145,9 @@ def declare(L):
     _sig(L, "ptc_decoder_enqueue_steps", None, vp, C.c_int)
     _sig(L, "ptc_decoder_read_tokens", None, vp, i32p, C.c_int)
     _sig(L, "ptc_decoder_reset", None, vp)
+    _sig(L, "ptc_decoder_is_persistent", C.c_int, vp)
+    _sig(L, "ptc_decoder_trace", None, vp, C.c_int)
+    _sig(L, "ptc_decoder_read_trace", C.c_int, vp, C.POINTER(C.c_ulonglong), C.c_int)
     _sig(L, "ptc_decoder_enqueue_embed", None, vp, C.c_int)
     _sig(L, "ptc_decoder_enqueue_layers", None, vp, C.c_int, C.c_int, C.c_int)
     _sig(L, "ptc_decoder_enqueue_head", None, vp)

@@ -90,6 +90,7 @@ float pt_train_step(pt_context_t *ctx, const int *tokens, int T, float lr) {
     pt_trace_t *tr = ctx->trace;
     pt_trace_begin(tr, "train_step", "train", -1);
     float loss = ptc_trainer_step(trainer(ctx), tokens, T, lr);
+    ptc_decoder_weights_updated(ctx->dev->dec);
     ctx->acts.T = T;
     pt_trace_end(tr);
     return loss;
@@ -173,6 +174,7 @@ void pt_sgd_update(pt_weights_t *w, const pt_grads_t *g, float lr, const pt_conf
     ptc_trainer_sgd_head(t, lr);
     ptc_trainer_sgd_layers(t, lr, 0, ctx->cfg.n_layers);
     ptc_trainer_sync(t);
+    ptc_decoder_weights_updated(ctx->dev->dec);
 }
 
 void pt_sgd_update_layers(pt_weights_t *w, const pt_grads_t *g, float lr, const pt_config_t *cfg,
@@ -181,6 +183,7 @@ void pt_sgd_update_layers(pt_weights_t *w, const pt_grads_t *g, float lr, const 
     pt_context_t *ctx = ctx_of(g, "pt_grads_t");
     ptc_trainer_sgd_layers(trainer(ctx), lr, l_start, l_end);
     ptc_trainer_sync(trainer(ctx));
+    ptc_decoder_weights_updated(ctx->dev->dec);
 }
 
 void pt_sgd_update_head(pt_weights_t *w, const pt_grads_t *g, float lr, const pt_config_t *cfg) {

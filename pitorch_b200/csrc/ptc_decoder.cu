@@ -13,6 +13,7 @@
 #include "ptc_common.cuh"
 #include "ptc_decode.cuh"
 #include "ptc_internal.h"
+#include "ptc_persist.h"
 
 using ptc::DecodeModel;
 using ptc::StepState;
@@ -34,6 +35,10 @@ struct ptc_decoder {
     int *d_tokens;         // [seq + 1]
     int mode;              // current StepState.mode on the device
     cudaGraphExec_t g_host, g_dev;
+    // persistent single-kernel path (ptc_persist.cu)
+    bool persist;
+    ptc::PersistArgs pa;
+    int loop_pos;          // device-loop mode: next position to decode
 };
 
 static void enqueue_kernels(ptc_decoder *d, cudaStream_t s) {
@@ -153,7 +158,70 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
 
     d->g_host = capture(d, true);
     d->g_dev = capture(d, false);
+
+    // Persistent path: one cooperative kernel per launch (see ptc_persist.cu).
+    // Opt-in (PTC_DECODE_PERSIST=1): on B200 its 49 grid-barrier phases per
+    // token currently cost slightly more than the 61-kernel PDL graph.
+    const char *want_persist = getenv("PTC_DECODE_PERSIST");
+    d->persist = m.L > 0 && ptc::persist_supported(m, d->n_sm) && want_persist && want_persist[0] == '1';
+    if (d->persist) {
+        int coop = 0;
+        PTC_CHECK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ptc_device(c)));
+        if (!coop) d->persist = false;
+    }
+    if (d->persist) {
+        ptc::PersistArgs &pa = d->pa;
+        memset(&pa, 0, sizeof(pa));
+        pa.m = m;
+        pa.has_embed = has_embed;
+        pa.has_head = has_head;
+        float *w2t = (float *)ptc_alloc(c, (size_t)m.L * m.hidden * m.dim * 4);
+        pa.w2t = w2t;
+        pa.x1 = (float *)ptc_alloc(c, (size_t)m.dim * 4);
+        pa.max_chunks = d->n_sm / m.nh > 0 ? d->n_sm / m.nh : 1;
+        pa.att_part = (float *)ptc_alloc(c, (size_t)m.nh * pa.max_chunks * (m.hd + 2) * 4);
+        pa.bar = (unsigned *)ptc_alloc(c, 256);
+        ptc::persist_transpose_w2(m, w2t, s);
+        PTC_CHECK(cudaStreamSynchronize(s));
+    }
+    d->loop_pos = 0;
     return d;
+}
+
+// Re-derive device-side copies that depend on the weights (the transposed
+// w2 of the persistent path) after the weights were updated in place.
+extern "C" void ptc_decoder_weights_updated(ptc_decoder *d) {
+    if (!d->persist) return;
+    ptc::persist_transpose_w2(d->m, (float *)d->pa.w2t, d->stream);
+}
+
+extern "C" int ptc_decoder_is_persistent(ptc_decoder *d) { return d->persist ? 1 : 0; }
+
+extern "C" void ptc_decoder_trace(ptc_decoder *d, int max_barriers) {
+    if (!d->persist) return;
+    if (max_barriers <= 0) {
+        d->pa.trace = nullptr;
+        d->pa.trace_cap = 0;
+        return;
+    }
+    d->pa.trace = (unsigned long long *)ptc_alloc(d->ctx, (size_t)2 * max_barriers * 8);
+    d->pa.trace_cap = 2 * max_barriers;
+    PTC_CHECK(cudaMemsetAsync(d->pa.trace, 0, (size_t)2 * max_barriers * 8, d->stream));
+}
+
+extern "C" int ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, int n) {
+    if (!d->persist || !d->pa.trace) return 0;
+    if (n > d->pa.trace_cap) n = d->pa.trace_cap;
+    PTC_CHECK(cudaMemcpyAsync(out, d->pa.trace, (size_t)n * 8, cudaMemcpyDeviceToHost, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    return n;
+}
+
+static void persist_run(ptc_decoder *d, int n_steps) {
+    d->pa.n_steps = n_steps;
+    ptc::persist_launch(d->pa, d->n_sm, d->stream);
+    // every CTA has read the last argmax key; clear it for the next head
+    PTC_CHECK(cudaMemsetAsync(&d->m.step->amax, 0, sizeof(unsigned long long), d->stream));
 }
 
 extern "C" void ptc_decoder_destroy(ptc_decoder *d) {
@@ -182,7 +250,15 @@ extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logit
     set_mode(d, 0);
     d->io->pos = pos;
     d->io->tok = token;
-    PTC_CHECK(cudaGraphLaunch(d->g_host, d->stream));
+    if (d->persist) {
+        PTC_CHECK(cudaMemcpyAsync(d->m.step, d->io, 2 * sizeof(int), cudaMemcpyHostToDevice, d->stream));
+        persist_run(d, 1);
+        if (d->has_head)
+            PTC_CHECK(cudaMemcpyAsync(&d->io->next, &d->m.step->next, sizeof(int), cudaMemcpyDeviceToHost,
+                                      d->stream));
+    } else {
+        PTC_CHECK(cudaGraphLaunch(d->g_host, d->stream));
+    }
     if (logits_host && d->has_head) {
         PTC_CHECK(cudaMemcpyAsync(d->stage, d->m.logits, (size_t)d->m.V * 4, cudaMemcpyDeviceToHost,
                                   d->stream));
@@ -228,9 +304,17 @@ extern "C" void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, in
     PTC_CHECK(cudaMemcpyAsync(d->m.step, &st, sizeof(st), cudaMemcpyHostToDevice, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     d->mode = 1;
+    d->loop_pos = 0;
 }
 
 extern "C" void ptc_decoder_enqueue_steps(ptc_decoder *d, int n) {
+    if (d->persist && d->has_embed && d->has_head) {
+        // one launch decodes up to the end of the cache
+        if (n > d->m.seq - d->loop_pos) n = d->m.seq - d->loop_pos;
+        if (n > 0) persist_run(d, n);
+        d->loop_pos += n > 0 ? n : 0;
+        return;
+    }
     for (int i = 0; i < n; i++) PTC_CHECK(cudaGraphLaunch(d->g_dev, d->stream));
 }
 
