@@ -151,6 +151,17 @@ void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, int n_prompt)
 void ptc_decoder_enqueue_steps(ptc_decoder *d, int n);
 void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n);
 
+/* Pipeline hand-off: device addresses of the step's position / input token,
+ * and layer / embedding launches that take them from the device (set by a
+ * received message or by the previous head) instead of from the host. */
+int *ptc_decoder_pos_dev(ptc_decoder *d);
+int *ptc_decoder_tok_dev(ptc_decoder *d);
+void ptc_decoder_enqueue_layers_devpos(ptc_decoder *d, int l_start, int l_end);
+void ptc_decoder_enqueue_embed_dev(ptc_decoder *d);
+/* Stream helpers for the pipeline's bounded waits: 0 = all queued work on
+ * the context stream finished, 1 = still running after timeout_ms. */
+int ptc_wait_deadline(ptc_ctx *c, int timeout_ms);
+
 /* Weights were updated in place (training): refresh derived device copies. */
 void ptc_decoder_weights_updated(ptc_decoder *d);
 /* 1 when the decoder runs each launch as the single persistent kernel. */

@@ -72,6 +72,12 @@ class pt_dist_result_t(C.Structure):
     _fields_ = [("loss", C.c_float), ("total_ms", C.c_uint)]
 
 
+class pt_dist_t(C.Structure):
+    _fields_ = [("rank", C.c_int), ("world_size", C.c_int), ("l_start", C.c_int), ("l_end", C.c_int),
+                ("has_embed", C.c_int), ("has_head", C.c_int), ("comm", C.c_void_p),
+                ("timeout_ms", C.c_int)]
+
+
 def _sig(L, name, res, *args):
     f = getattr(L, name, None)
     if f is None:
@@ -124,6 +130,19 @@ def declare(L):
     _sig(L, "pt_backward_head", None, cfgp, wp, grads, acts, bb, i32p, C.c_int, vp, vp)
     _sig(L, "pt_backward_layers_range", None, cfgp, wp, grads, acts, bb, C.c_int, C.c_int, C.c_int, vp, vp)
     _sig(L, "pt_backward_embed", None, grads, bb, i32p, C.c_int, C.c_int)
+    dist = P(pt_dist_t)
+    _sig(L, "pt_dist_setup", None, dist, P(pt_shard_info_t), C.c_int, C.c_int)
+    _sig(L, "pt_dist_setup_ctx", C.c_int, dist, ctx, P(pt_shard_info_t), C.c_int, C.c_int)
+    _sig(L, "pt_dist_forward_step", C.c_int, ctx, dist, C.c_int)
+    _sig(L, "pt_dist_generate_greedy", C.c_int, ctx, dist, i32p, C.c_int, C.c_int, i32p)
+    _sig(L, "pt_dist_train_step", pt_dist_result_t, ctx, dist, i32p, C.c_int, C.c_float)
+    _sig(L, "pt_dist_allreduce_grads_avg", C.c_int, ctx, dist)
+    _sig(L, "pt_dist_max_float", C.c_float, ctx, dist, C.c_float)
+    _sig(L, "pt_dist_free", None, dist)
+    _sig(L, "pt_dist_set_verbose", None, dist, C.c_int)
+    _sig(L, "pt_dist_ring_sync", C.c_int, dist)
+    _sig(L, "pt_dist_rendezvous", C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int, C.c_int,
+         C.POINTER(C.c_ubyte))
     # thin C ABI (ptc.h)
     _sig(L, "ptc_device_count", C.c_int)
     _sig(L, "ptc_create", vp, C.c_int, C.c_size_t)
@@ -169,15 +188,21 @@ def ip(a):
 
 
 class Context:
-    """A ``pt_context_t`` initialised from a .bin image (``pt_pi_init``)."""
+    """A ``pt_context_t`` initialised from a .bin image (``pt_pi_init``), or
+    from a SHRD shard (``pt_pi_init_shard``) when ``shard=True``."""
 
-    def __init__(self, blob, max_T=0, device=-1, arena_bytes=0):
+    def __init__(self, blob, max_T=0, device=-1, arena_bytes=0, shard=False):
         from . import lib
         self.L = lib()
         # The context's weight pointers point into this buffer; keep it alive.
         self._blob = C.create_string_buffer(bytes(blob), len(blob))
         self.ctx = pt_context_t()
-        self.L.pt_pi_init(C.byref(self.ctx), C.cast(self._blob, C.c_void_p), device, max_T, arena_bytes)
+        self.shard = pt_shard_info_t()
+        if shard:
+            self.L.pt_pi_init_shard(C.byref(self.ctx), C.byref(self.shard), C.cast(self._blob, C.c_void_p),
+                                    device, max_T, arena_bytes)
+        else:
+            self.L.pt_pi_init(C.byref(self.ctx), C.cast(self._blob, C.c_void_p), device, max_T, arena_bytes)
         self.cfg = self.ctx.cfg
         self._open = True
 
@@ -242,3 +267,77 @@ class Context:
             self.close()
         except Exception:
             pass
+
+
+def make_shard(full_blob, rank, world):
+    """Cut rank's SHRD shard out of a full .bin image (pt_make_shard)."""
+    from . import lib
+    L = lib()
+    src = C.create_string_buffer(bytes(full_blob), len(full_blob))
+    cap = len(full_blob) + 64
+    out = C.create_string_buffer(cap)
+    n = L.pt_make_shard(C.cast(src, C.c_void_p), rank, world, C.cast(out, C.c_void_p), cap)
+    if n == 0:
+        raise ValueError("pt_make_shard failed")
+    return out.raw[:n]
+
+
+class Pipeline:
+    """One rank of the layer pipeline: a shard context plus its ring link."""
+
+    def __init__(self, full_blob, rank, world, device, max_T=0):
+        from . import lib
+        self.L = lib()
+        self.rank, self.world = rank, world
+        self.ctx = Context(make_shard(full_blob, rank, world), max_T=max_T, device=device, shard=True)
+        self.dist = pt_dist_t()
+        rc = self.L.pt_dist_setup_ctx(C.byref(self.dist), C.byref(self.ctx.ctx), C.byref(self.ctx.shard),
+                                      rank, world)
+        if rc != 0:
+            raise RuntimeError(f"rank {rank}: pipeline rendezvous failed")
+
+    @property
+    def is_head(self):
+        return bool(self.dist.has_embed and self.dist.has_head)
+
+    def generate_greedy(self, prompt, n_pos):
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_pos, dtype=np.int32)
+        rc = self.L.pt_dist_generate_greedy(C.byref(self.ctx.ctx), C.byref(self.dist), ip(prompt), len(prompt),
+                                            n_pos, ip(out))
+        if rc != 0:
+            raise RuntimeError("pipeline generate failed")
+        return out
+
+    def forward_step(self, token):
+        return self.L.pt_dist_forward_step(C.byref(self.ctx.ctx), C.byref(self.dist), int(token))
+
+    def decode_greedy(self, prompt, n_pos):
+        """Host-driven pipeline decode through pt_dist_forward_step."""
+        self.ctx.reset_kv()
+        toks = np.zeros(n_pos, dtype=np.int32)
+        tok = int(prompt[0])
+        for p in range(n_pos):
+            nxt = self.forward_step(tok)
+            if nxt < 0:
+                raise RuntimeError("pipeline step failed")
+            if self.is_head:
+                nxt = int(prompt[p + 1]) if p + 1 < len(prompt) else nxt
+                toks[p] = nxt
+                tok = nxt
+        return toks
+
+    def train_step(self, tokens, lr):
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        r = self.L.pt_dist_train_step(C.byref(self.ctx.ctx), C.byref(self.dist), ip(tokens), len(tokens),
+                                      C.c_float(lr))
+        if r.total_ms == 0:
+            raise RuntimeError("pipeline train step failed")
+        return r.loss
+
+    def max_over_ranks(self, v):
+        return float(self.L.pt_dist_max_float(C.byref(self.ctx.ctx), C.byref(self.dist), C.c_float(v)))
+
+    def close(self):
+        self.L.pt_dist_free(C.byref(self.dist))
+        self.ctx.close()

@@ -1,0 +1,403 @@
+/*
+ * pt_dist.c -- the layer pipeline over NVLink (pitorch/dist/pt_dist_pipeline.c
+ * on GPUs instead of a GPIO ring of Pi Zeros).
+ *
+ * One process per GPU. Links are an NCCL communicator: the reference's
+ * blocking send_raw/recv_raw over the GPIO bus (pitorch/dist/transport/
+ * pt_transport.h:15-18) become ncclSend/ncclRecv of device buffers on the
+ * context's stream, so activations never touch the host. The message of a
+ * decode hop keeps the reference's [int32 pos | float x[dim]] layout
+ * (pt_dist_pipeline.c:287, 298-302); training hops carry the [T, dim]
+ * residual stream forward and d_res backward (pt_dist_pipeline.c:134).
+ *
+ * Every wait is bounded by dist->timeout_ms: on expiry the rank prints a
+ * FAIL line, aborts its communicator and returns an error code -- the
+ * reference's recv_raw returns -1 after its 300 s first-byte timeout
+ * (pt_link_gpio.c:134-136) and its callers reboot the board.
+ */
+#include <arpa/inet.h>
+#include <errno.h>
+#include <fcntl.h>
+#include <netdb.h>
+#include <netinet/in.h>
+#include <netinet/tcp.h>
+#include <poll.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/socket.h>
+#include <sys/time.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include "../../../include/pt_dist_pipeline.h"
+#include "pt_device.h"
+
+typedef struct {
+    ncclComm_t comm;
+    int device;
+    float *sbuf, *rbuf;   /* [1 + dim] device message buffers: pos bits, x */
+    float *scal;          /* device scratch scalar */
+    int dim;
+    int verbose;
+    int step;
+} dist_comm_t;
+
+static long now_ms(void) {
+    struct timespec t;
+    clock_gettime(CLOCK_MONOTONIC, &t);
+    return t.tv_sec * 1000L + t.tv_nsec / 1000000L;
+}
+
+static int timeout_of(const pt_dist_t *d) { return d->timeout_ms > 0 ? d->timeout_ms : 300000; }
+
+/* ---- TCP rendezvous for the NCCL unique id -------------------------------- */
+
+static int set_nonblock(int fd, int on) {
+    int fl = fcntl(fd, F_GETFL, 0);
+    return fcntl(fd, F_SETFL, on ? (fl | O_NONBLOCK) : (fl & ~O_NONBLOCK));
+}
+
+static int io_full(int fd, unsigned char *buf, int n, int sending, long deadline) {
+    int done = 0;
+    while (done < n) {
+        long left = deadline - now_ms();
+        if (left <= 0) return -1;
+        struct pollfd p = {fd, (short)(sending ? POLLOUT : POLLIN), 0};
+        int r = poll(&p, 1, (int)(left > 1000 ? 1000 : left));
+        if (r < 0 && errno != EINTR) return -1;
+        if (r <= 0) continue;
+        ssize_t k = sending ? send(fd, buf + done, n - done, MSG_NOSIGNAL) : recv(fd, buf + done, n - done, 0);
+        if (k <= 0) {
+            if (k < 0 && (errno == EAGAIN || errno == EINTR)) continue;
+            return -1;
+        }
+        done += (int)k;
+    }
+    return 0;
+}
+
+int pt_dist_rendezvous(int rank, int world_size, const char *addr, int port, int timeout_ms,
+                       unsigned char blob[128]) {
+    const long deadline = now_ms() + timeout_ms;
+    if (world_size <= 1) return 0;
+    if (rank == 0) {
+        int ls = socket(AF_INET, SOCK_STREAM, 0);
+        if (ls < 0) return -1;
+        int one = 1;
+        setsockopt(ls, SOL_SOCKET, SO_REUSEADDR, &one, sizeof(one));
+        struct sockaddr_in sa;
+        memset(&sa, 0, sizeof(sa));
+        sa.sin_family = AF_INET;
+        sa.sin_port = htons((unsigned short)port);
+        sa.sin_addr.s_addr = htonl(INADDR_ANY);
+        if (bind(ls, (struct sockaddr *)&sa, sizeof(sa)) < 0 || listen(ls, world_size) < 0) {
+            close(ls);
+            return -1;
+        }
+        set_nonblock(ls, 1);
+        int served = 0, rc = 0;
+        while (served < world_size - 1) {
+            long left = deadline - now_ms();
+            if (left <= 0) { rc = -1; break; }
+            struct pollfd p = {ls, POLLIN, 0};
+            int r = poll(&p, 1, (int)(left > 1000 ? 1000 : left));
+            if (r <= 0) continue;
+            int fd = accept(ls, NULL, NULL);
+            if (fd < 0) continue;
+            set_nonblock(fd, 1);
+            if (io_full(fd, blob, 128, 1, deadline) < 0) rc = -1;
+            close(fd);
+            if (rc < 0) break;
+            served++;
+        }
+        close(ls);
+        return rc;
+    }
+    for (;;) {
+        if (now_ms() > deadline) return -1;
+        int fd = socket(AF_INET, SOCK_STREAM, 0);
+        if (fd < 0) return -1;
+        struct sockaddr_in sa;
+        memset(&sa, 0, sizeof(sa));
+        sa.sin_family = AF_INET;
+        sa.sin_port = htons((unsigned short)port);
+        if (inet_pton(AF_INET, addr, &sa.sin_addr) != 1) {
+            struct hostent *he = gethostbyname(addr);
+            if (!he) { close(fd); return -1; }
+            memcpy(&sa.sin_addr, he->h_addr_list[0], sizeof(sa.sin_addr));
+        }
+        if (connect(fd, (struct sockaddr *)&sa, sizeof(sa)) == 0) {
+            set_nonblock(fd, 1);
+            int rc = io_full(fd, blob, 128, 0, deadline);
+            close(fd);
+            return rc;
+        }
+        close(fd);
+        usleep(50000);
+    }
+}
+
+static int rendezvous_port(void) {
+    const char *p = getenv("PT_DIST_PORT");
+    if (p) return atoi(p);
+    const char *m = getenv("MASTER_PORT");
+    return m ? atoi(m) + 17 : 29517;
+}
+
+static const char *rendezvous_addr(void) {
+    const char *a = getenv("MASTER_ADDR");
+    return a ? a : "127.0.0.1";
+}
+
+/* ---- setup ------------------------------------------------------------------ */
+
+static void fail(const pt_dist_t *d, const char *what) {
+    fprintf(stderr, "FAIL: rank %d: %s\n", d->rank, what);
+}
+
+static dist_comm_t *comm_of(pt_dist_t *d) { return (dist_comm_t *)d->comm; }
+
+static int join(pt_dist_t *dist, pt_context_t *ctx) {
+    if (dist->comm) return 0;
+    if (!ctx || !ctx->dev) pt_fatal("pipeline call without an initialised context");
+    unsigned char id[128];
+    memset(id, 0, sizeof(id));
+    ncclUniqueId uid;
+    if (dist->rank == 0) {
+        if (ncclGetUniqueId(&uid) != ncclSuccess) pt_fatal("ncclGetUniqueId failed");
+        memcpy(id, &uid, sizeof(uid) < 128 ? sizeof(uid) : 128);
+    }
+    if (pt_dist_rendezvous(dist->rank, dist->world_size, rendezvous_addr(), rendezvous_port(),
+                           timeout_of(dist), id) < 0) {
+        fail(dist, "ring rendezvous timeout");
+        return -1;
+    }
+    memcpy(&uid, id, sizeof(uid));
+    dist_comm_t *c = (dist_comm_t *)calloc(1, sizeof(dist_comm_t));
+    c->device = ptc_device(ctx->dev->ctx);
+    c->dim = ctx->cfg.dim;
+    if (cudaSetDevice(c->device) != cudaSuccess) pt_fatal("cudaSetDevice(%d) failed", c->device);
+    if (ncclCommInitRank(&c->comm, dist->world_size, uid, dist->rank) != ncclSuccess) {
+        free(c);
+        fail(dist, "ncclCommInitRank failed");
+        return -1;
+    }
+    c->sbuf = (float *)ptc_alloc(ctx->dev->ctx, (size_t)(1 + c->dim) * 4);
+    c->rbuf = (float *)ptc_alloc(ctx->dev->ctx, (size_t)(1 + c->dim) * 4);
+    c->scal = (float *)ptc_alloc(ctx->dev->ctx, 256);
+    dist->comm = c;
+    return 0;
+}
+
+/* pt_dist_pipeline.c:26-33 */
+void pt_dist_setup(pt_dist_t *dist, const pt_shard_info_t *shard, int rank, int world_size) {
+    memset(dist, 0, sizeof(*dist));
+    dist->rank = rank;
+    dist->world_size = world_size;
+    dist->l_start = 0;
+    dist->l_end = shard->n_local;
+    dist->has_embed = shard->has_embed;
+    dist->has_head = shard->has_head;
+    const char *t = getenv("PT_DIST_TIMEOUT_MS");
+    dist->timeout_ms = t ? atoi(t) : 0;
+}
+
+int pt_dist_setup_ctx(pt_dist_t *dist, pt_context_t *ctx, const pt_shard_info_t *shard, int rank,
+                      int world_size) {
+    pt_dist_setup(dist, shard, rank, world_size);
+    return join(dist, ctx);
+}
+
+void pt_dist_free(pt_dist_t *dist) {
+    dist_comm_t *c = comm_of(dist);
+    if (!c) return;
+    ncclCommDestroy(c->comm);
+    free(c);
+    dist->comm = NULL;
+}
+
+void pt_dist_set_verbose(pt_dist_t *dist, int verbose) {
+    if (comm_of(dist)) comm_of(dist)->verbose = verbose;
+}
+
+void pt_dist_reset_links(pt_dist_t *dist) { (void)dist; }
+
+/* Wait for the stream with the dist deadline; abort the communicator on expiry. */
+static int finish(pt_dist_t *dist, pt_context_t *ctx, const char *what) {
+    dist_comm_t *c = comm_of(dist);
+    if (ptc_wait_deadline(ctx->dev->ctx, timeout_of(dist)) == 0) {
+        ncclResult_t ae = ncclSuccess;
+        ncclCommGetAsyncError(c->comm, &ae);
+        if (ae == ncclSuccess) return 0;
+    }
+    fail(dist, what);
+    ncclCommAbort(c->comm);
+    c->comm = NULL;
+    return -1;
+}
+
+static cudaStream_t stream_of(pt_context_t *ctx) { return (cudaStream_t)ptc_stream(ctx->dev->ctx); }
+
+int pt_dist_ring_sync(pt_dist_t *dist) {
+    (void)dist;
+    return 0;
+}
+
+static int ring_sync_ctx(pt_dist_t *dist, pt_context_t *ctx) {
+    dist_comm_t *c = comm_of(dist);
+    if (!c || !c->comm) return -1;
+    ncclAllReduce(c->scal, c->scal, 1, ncclFloat, ncclSum, c->comm, stream_of(ctx));
+    return finish(dist, ctx, "ring handshake timeout");
+}
+
+float pt_dist_max_float(pt_context_t *ctx, pt_dist_t *dist, float v) {
+    if (join(dist, ctx) < 0) return v;
+    dist_comm_t *c = comm_of(dist);
+    cudaStream_t s = stream_of(ctx);
+    cudaMemcpyAsync(c->scal, &v, 4, cudaMemcpyHostToDevice, s);
+    ncclAllReduce(c->scal, c->scal, 1, ncclFloat, ncclMax, c->comm, s);
+    float out = v;
+    cudaMemcpyAsync(&out, c->scal, 4, cudaMemcpyDeviceToHost, s);
+    if (finish(dist, ctx, "max-over-ranks timeout") < 0) return v;
+    return out;
+}
+
+int pt_dist_allreduce_grads_avg(pt_context_t *ctx, pt_dist_t *dist) {
+    if (join(dist, ctx) < 0) return -1;
+    dist_comm_t *c = comm_of(dist);
+    if (!ctx->dev->trainer) pt_fatal("pt_dist_allreduce_grads_avg needs a training context");
+    float *g = ptc_trainer_grads(ctx->dev->trainer);
+    size_t n = ptc_trainer_n_params(ctx->dev->trainer);
+    ncclAllReduce(g, g, n, ncclFloat, ncclAvg, c->comm, stream_of(ctx));
+    return finish(dist, ctx, "gradient allreduce timeout");
+}
+
+/* ---- decode ------------------------------------------------------------------ */
+
+static int next_rank(const pt_dist_t *d) { return (d->rank + 1) % d->world_size; }
+static int prev_rank(const pt_dist_t *d) { return (d->rank + d->world_size - 1) % d->world_size; }
+
+/* Enqueue one position's hop sequence for this rank (no host sync). For the
+ * head rank in device-loop mode the embedding reads the token from the
+ * device and the head advances position/token on the device. */
+static void enqueue_position(pt_dist_t *dist, pt_context_t *ctx, int host_token, int host_pos, int devloop) {
+    dist_comm_t *c = comm_of(dist);
+    ptc_decoder *dec = ctx->dev->dec;
+    cudaStream_t s = stream_of(ctx);
+    const size_t msg = (size_t)(1 + c->dim);
+    float *x = ptc_decoder_x_dev(dec);
+    int *pos_dev = ptc_decoder_pos_dev(dec);
+    if (dist->has_embed && dist->has_head) {
+        if (devloop) {
+            ptc_decoder_enqueue_embed_dev(dec);
+        } else {
+            cudaMemcpyAsync(pos_dev, &host_pos, 4, cudaMemcpyHostToDevice, s);
+            ptc_decoder_enqueue_embed(dec, host_token);
+        }
+        cudaMemcpyAsync(c->sbuf, pos_dev, 4, cudaMemcpyDeviceToDevice, s);
+        cudaMemcpyAsync(c->sbuf + 1, x, (size_t)c->dim * 4, cudaMemcpyDeviceToDevice, s);
+        ncclSend(c->sbuf, msg, ncclFloat, next_rank(dist), c->comm, s);
+        ncclRecv(c->rbuf, msg, ncclFloat, prev_rank(dist), c->comm, s);
+        cudaMemcpyAsync(x, c->rbuf + 1, (size_t)c->dim * 4, cudaMemcpyDeviceToDevice, s);
+        ptc_decoder_enqueue_head(dec);
+    } else {
+        ncclRecv(c->rbuf, msg, ncclFloat, prev_rank(dist), c->comm, s);
+        cudaMemcpyAsync(pos_dev, c->rbuf, 4, cudaMemcpyDeviceToDevice, s);
+        cudaMemcpyAsync(x, c->rbuf + 1, (size_t)c->dim * 4, cudaMemcpyDeviceToDevice, s);
+        ptc_decoder_enqueue_layers_devpos(dec, dist->l_start, dist->l_end);
+        cudaMemcpyAsync(c->sbuf, c->rbuf, 4, cudaMemcpyDeviceToDevice, s);
+        cudaMemcpyAsync(c->sbuf + 1, x, (size_t)c->dim * 4, cudaMemcpyDeviceToDevice, s);
+        ncclSend(c->sbuf, msg, ncclFloat, next_rank(dist), c->comm, s);
+    }
+}
+
+/* pt_dist_pipeline.c:284-372 */
+int pt_dist_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token) {
+    if (join(dist, ctx) < 0) return -1;
+    dist_comm_t *c = comm_of(dist);
+    if (!c->comm) return -1;
+    if (dist->world_size < 2) pt_fatal("pt_dist_forward_step needs world_size >= 2");
+    if (dist->has_embed && dist->has_head && (token < 0 || token >= ctx->cfg.vocab_size))
+        pt_fatal("token %d outside [0, %d)", token, ctx->cfg.vocab_size);
+    long t0 = now_ms();
+    enqueue_position(dist, ctx, token, ctx->pos, 0);
+    int next = 0;
+    if (finish(dist, ctx, "dist forward recv timeout") < 0) return -1;
+    if (dist->has_embed && dist->has_head) {
+        next = ptc_decoder_fetch_next(ctx->dev->dec, ctx->sync_logits ? ctx->state.logits : NULL);
+        ctx->pos++;
+    }
+    if (c->verbose)
+        printf("R%d pos %d -> %d | %ldms\n", dist->rank, c->step, next, now_ms() - t0);
+    c->step++;
+    return next;
+}
+
+int pt_dist_generate_greedy(pt_context_t *ctx, pt_dist_t *dist, const int *prompt, int n_prompt, int n_pos,
+                            int *out_tokens) {
+    if (join(dist, ctx) < 0) return -1;
+    dist_comm_t *c = comm_of(dist);
+    if (!c->comm) return -1;
+    ptc_decoder *dec = ctx->dev->dec;
+    if (n_pos > ctx->cfg.seq_len) n_pos = ctx->cfg.seq_len;
+    ptc_decoder_reset(dec);
+    if (dist->has_embed && dist->has_head) ptc_decoder_generate_begin(dec, prompt, n_prompt);
+    for (int p = 0; p < n_pos; p++) enqueue_position(dist, ctx, 0, 0, 1);
+    if (finish(dist, ctx, "dist generate timeout") < 0) return -1;
+    if (dist->has_embed && dist->has_head) {
+        ptc_decoder_read_tokens(dec, out_tokens, n_pos);
+        ctx->pos = n_pos;
+    }
+    return 0;
+}
+
+/* ---- training (pt_dist_pipeline.c:128-278) ----------------------------------- */
+
+pt_dist_result_t pt_dist_train_step(pt_context_t *ctx, pt_dist_t *dist, const int *tokens, int T, float lr) {
+    pt_dist_result_t res = {0.0f, 0};
+    if (join(dist, ctx) < 0) return res;
+    dist_comm_t *c = comm_of(dist);
+    if (!c->comm) return res;
+    ptc_trainer *tr = ctx->dev->trainer;
+    if (!tr) pt_fatal("pt_dist_train_step needs a context initialised with max_T > 0");
+    cudaStream_t s = stream_of(ctx);
+    const long t0 = now_ms();
+    const int n_local = dist->l_end - dist->l_start;
+    const size_t act = (size_t)T * ctx->cfg.dim;
+    ptc_trainer_set_tokens(tr, tokens, T);
+    ptc_trainer_zero_grads(tr);
+    if (dist->has_embed && dist->has_head) {
+        ptc_trainer_fwd_embed(tr);
+        ncclSend(ptc_trainer_residual(tr, 0), act, ncclFloat, next_rank(dist), c->comm, s);
+        ncclRecv(ptc_trainer_residual(tr, n_local), act, ncclFloat, prev_rank(dist), c->comm, s);
+        if (finish(dist, ctx, "recv fwd act") < 0) return res;
+        const float loss = ptc_trainer_fwd_head(tr);
+        ptc_trainer_bwd_head(tr);
+        ncclSend(ptc_trainer_dres(tr), act, ncclFloat, prev_rank(dist), c->comm, s);
+        ncclRecv(ptc_trainer_dres(tr), act, ncclFloat, next_rank(dist), c->comm, s);
+        ptc_trainer_bwd_embed(tr);
+        ptc_trainer_sgd_head(tr, lr);
+        if (finish(dist, ctx, "recv bwd d_res") < 0) return res;
+        res.loss = loss;
+    } else {
+        ncclRecv(ptc_trainer_residual(tr, 0), act, ncclFloat, prev_rank(dist), c->comm, s);
+        ptc_trainer_fwd_layers(tr, 0, n_local);
+        ncclSend(ptc_trainer_residual(tr, n_local), act, ncclFloat, next_rank(dist), c->comm, s);
+        ncclRecv(ptc_trainer_dres(tr), act, ncclFloat, next_rank(dist), c->comm, s);
+        ptc_trainer_bwd_layers(tr, 0, n_local);
+        ncclSend(ptc_trainer_dres(tr), act, ncclFloat, prev_rank(dist), c->comm, s);
+        ptc_trainer_sgd_layers(tr, lr, 0, n_local);
+        if (finish(dist, ctx, "recv bwd d_res") < 0) return res;
+    }
+    ptc_decoder_weights_updated(ctx->dev->dec);
+    long dt = now_ms() - t0;
+    res.total_ms = (unsigned)(dt > 0 ? dt : 1);
+    if (c->verbose) printf("R%d STEP %d | loss %.4f | %ums\n", dist->rank, c->step, res.loss, res.total_ms);
+    c->step++;
+    (void)ring_sync_ctx;
+    return res;
+}

@@ -272,6 +272,7 @@ extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logit
 }
 
 extern "C" void ptc_decoder_set_x(ptc_decoder *d, const float *x_host) {
+    set_mode(d, 0);
     memcpy(d->stage, x_host, (size_t)d->m.dim * 4);
     PTC_CHECK(cudaMemcpyAsync(d->m.x, d->stage, (size_t)d->m.dim * 4, cudaMemcpyHostToDevice, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
@@ -358,9 +359,10 @@ extern "C" void ptc_decoder_enqueue_layers(ptc_decoder *d, int pos, int l_start,
     for (int l = l_start; l < l_end; l++) ptc::launch_layer(d->m, l, false, d->n_sm, d->stream);
 }
 
+// Mode is the caller's: host-mode callers set it through the functions that
+// take a host token/position; the pipeline's device loop keeps mode 1.
 extern "C" void ptc_decoder_enqueue_head(ptc_decoder *d) {
     if (!d->has_head) PTC_FATAL("decoder has no head");
-    set_mode(d, 0);
     ptc::launch_head(d->m, d->n_sm, d->stream);
 }
 
@@ -372,4 +374,18 @@ extern "C" int ptc_decoder_fetch_next(ptc_decoder *d, float *logits_host) {
     if (logits_host) memcpy(logits_host, d->stage, (size_t)d->m.V * 4);
     check_err(d);
     return d->io->next;
+}
+
+extern "C" int *ptc_decoder_pos_dev(ptc_decoder *d) { return &d->m.step->pos; }
+extern "C" int *ptc_decoder_tok_dev(ptc_decoder *d) { return &d->m.step->tok; }
+
+extern "C" void ptc_decoder_enqueue_layers_devpos(ptc_decoder *d, int l_start, int l_end) {
+    if (l_start < 0 || l_end > d->m.L || l_start > l_end)
+        PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
+    for (int l = l_start; l < l_end; l++) ptc::launch_layer(d->m, l, false, d->n_sm, d->stream);
+}
+
+extern "C" void ptc_decoder_enqueue_embed_dev(ptc_decoder *d) {
+    if (!d->has_embed) PTC_FATAL("decoder has no embedding");
+    ptc::launch_embed(d->m, d->stream);
 }

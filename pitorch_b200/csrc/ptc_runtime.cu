@@ -8,6 +8,7 @@
 // decode/train steps allocate nothing.
 #include <pthread.h>
 #include <string.h>
+#include <time.h>
 
 #include <vector>
 
@@ -227,3 +228,16 @@ extern "C" void ptc_timer_destroy(ptc_timer *t) {
 
 cudaStream_t ptc_ctx_stream(ptc_ctx *c) { return c->stream; }
 int ptc_ctx_device(ptc_ctx *c) { return c->device; }
+
+extern "C" int ptc_wait_deadline(ptc_ctx *c, int timeout_ms) {
+    struct timespec t0, t;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for (;;) {
+        cudaError_t e = cudaStreamQuery(c->stream);
+        if (e == cudaSuccess) return 0;
+        if (e != cudaErrorNotReady) PTC_CHECK(e);
+        clock_gettime(CLOCK_MONOTONIC, &t);
+        const long ms = (t.tv_sec - t0.tv_sec) * 1000L + (t.tv_nsec - t0.tv_nsec) / 1000000L;
+        if (ms > timeout_ms) return 1;
+    }
+}

@@ -1,0 +1,102 @@
+"""The layer pipeline on 2+ GPUs (pt_dist_setup / pt_dist_forward_step /
+pt_dist_train_step), one process per GPU as the reference runs one program
+per Pi (pitorch/dist/pt_dist_pipeline.c).
+
+Parity targets are the reference's host C on the same weights (decode
+fixtures), and -- for training -- the single-context pt_train_step, which is
+the same arithmetic split differently (dev/tests/host/test_shard_train.c
+checks the shard pipeline against the full model the same way).
+Skipped when fewer GPUs are visible than the case needs.
+"""
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def n_gpus():
+    import pitorch_b200
+    return pitorch_b200.lib().ptc_device_count()
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, task, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["PT_DIST_PORT"] = str(port)
+        os.environ["PT_DIST_TIMEOUT_MS"] = "60000"
+        from pitorch_b200 import api, synth
+        name, kind = task
+        cfg = synth.CONFIGS[name]
+        blob = synth.make_blob(cfg)
+        if kind == "decode":
+            g = golden(f"decode_{name}.npz")
+            n = int(g["n_pos"])
+            pipe = api.Pipeline(blob, rank, world, device=rank)
+            dev = pipe.generate_greedy(g["prompt"], n)
+            host = pipe.decode_greedy(g["prompt"], n)
+            q.put((rank, pipe.is_head, dev.tolist(), host.tolist()))
+            pipe.close()
+        else:
+            g = golden(f"train_{name}.npz")
+            T = int(g["T"])
+            pipe = api.Pipeline(blob, rank, world, device=rank, max_T=T)
+            losses = [pipe.train_step(g["tokens"], float(g["lr"])) for _ in range(3)]
+            q.put((rank, pipe.is_head, losses, None))
+            pipe.close()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, None, repr(e), None))
+
+
+def run_ranks(world, task):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, task, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    out = [q.get(timeout=600) for _ in range(world)]
+    for p in ps:
+        p.join(timeout=120)
+    for r, head, a, b in out:
+        assert head is not None, f"rank {r} failed: {a}"
+    return out
+
+
+@pytest.mark.parametrize("name,world", [("tiny", 2), ("stories15M", 2), ("stories15M", 4), ("stories110M", 4)])
+def test_pipeline_decode_matches_reference(ptlib, name, world):
+    if n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = run_ranks(world, (name, "decode"))
+    g = golden(f"decode_{name}.npz")
+    n = int(g["n_pos"])
+    head = [o for o in out if o[1]]
+    assert len(head) == 1
+    _, _, dev, host = head[0]
+    assert np.array_equal(np.array(dev), g["tokens"][:n])
+    assert np.array_equal(np.array(host), g["tokens"][:n])
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_pipeline_training_matches_single_gpu(ptlib, world):
+    if n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = run_ranks(world, ("stories15M", "train"))
+    g = golden("train_stories15M.npz")
+    head = [o for o in out if o[1]]
+    losses = np.array(head[0][2], dtype=np.float64)
+    ref = g["losses"][:3].astype(np.float64)
+    assert np.all(np.abs(losses - ref) <= 1e-4 * np.abs(ref)), (losses, ref)
