@@ -87,6 +87,34 @@ __device__ __forceinline__ void rmsnorm_regs(float4 (&x)[NV], const float *gain,
 }
 
 template <int NV>
+__device__ __forceinline__ void load_gain(float4 (&g)[NV], const float *gain, int c4, int lane) {
+    const float4 *g4 = reinterpret_cast<const float4 *>(gain);
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const int c = lane + 32 * v;
+        g[v] = (c < c4) ? __ldg(g4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// rmsnorm with the gain already in registers (pitorch/ops/core/pt_ops.c:5-12).
+template <int NV>
+__device__ __forceinline__ void rmsnorm_pre(float4 (&x)[NV], const float4 (&g)[NV], int dim) {
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; v++)
+        ss += x[v].x * x[v].x + x[v].y * x[v].y + x[v].z * x[v].z + x[v].w * x[v].w;
+    ss = warp_sum(ss);
+    const float s = rms_scale(ss, dim);
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        x[v].x = __fmul_rn(__fmul_rn(x[v].x, s), g[v].x);
+        x[v].y = __fmul_rn(__fmul_rn(x[v].y, s), g[v].y);
+        x[v].z = __fmul_rn(__fmul_rn(x[v].z, s), g[v].z);
+        x[v].w = __fmul_rn(__fmul_rn(x[v].w, s), g[v].w);
+    }
+}
+
+template <int NV>
 __device__ __forceinline__ void store_vec(float *dst, const float4 (&x)[NV], int c4, int lane) {
     float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
@@ -112,7 +140,6 @@ constexpr int ATT_MAX_CHUNKS = 256;
 
 __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     pdl_trigger();
-    __shared__ __align__(16) float s_q[ATT_MAX_HD];
     __shared__ float s_p[ATT_MAX_CHUNKS];
     __shared__ __align__(16) float s_o[ATT_THREADS * 4];
     __shared__ float s_stat[2];
@@ -124,62 +151,85 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     const int kvh = h / (m.nh / m.nkv);
     const int ngrp = ATT_THREADS / hd4;      // position groups for the value pass
     const int d4 = tid % hd4, grp = tid / hd4;
-    pdl_wait();
+    // The position and every K/V row before it were written by earlier
+    // launches (earlier tokens, or this graph's first node), so they are
+    // read before the wait; only q and the row of `pos` come from the
+    // kernel this one depends on.
     const int pos = min(__ldcg(&m.step->pos), m.seq - 1);
     const int t0 = c * CH;
-    const size_t head_base = ((size_t)l * m.nkv + kvh) * m.seq;
-    const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
-    float *part = m.att_part + ((size_t)h * m.n_chunks + c) * (hd + 2);
-
     const int nc = pos / CH + 1;   // chunks holding positions <= pos
     if (c >= nc) return;           // no positions here: not part of the merge
+    const int n = min(CH, pos + 1 - t0);
+    const int jcur = pos - t0;     // the current position's slot, if < n
+    const size_t head_base = ((size_t)l * m.nkv + kvh) * m.seq;
+    const float4 *kb = reinterpret_cast<const float4 *>(m.kc + (head_base + t0) * hd);
+    const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + t0) * hd);
+    const int js = tid >> 2, sub = tid & 3;
+    constexpr int QK = 4, VP = 4;
+    float4 kv[QK], vpre[VP], qv[QK];
+#pragma unroll
+    for (int i = 0; i < QK; i++) {
+        const int cc = sub + 4 * i;
+        kv[i] = (cc < hd4 && js < n && js != jcur) ? __ldcg(kb + (size_t)js * hd4 + cc)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < VP; k++) {
+        const int j = grp + ngrp * k;
+        vpre[k] = (grp < ngrp && j < n && j != jcur) ? __ldcg(vb + (size_t)j * hd4 + d4)
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    pdl_wait();
+    const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
+    float *part = m.att_part + ((size_t)h * m.n_chunks + c) * (hd + 2);
+    const float4 *q4 = reinterpret_cast<const float4 *>(m.q + h * hd);
+#pragma unroll
+    for (int i = 0; i < QK; i++) {
+        const int cc = sub + 4 * i;
+        qv[i] = (cc < hd4) ? __ldcg(q4 + cc) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (cc < hd4 && js == jcur) kv[i] = __ldcg(kb + (size_t)js * hd4 + cc);
+    }
+#pragma unroll
+    for (int k = 0; k < VP; k++)
+        if (grp < ngrp && grp + ngrp * k == jcur) vpre[k] = __ldcg(vb + (size_t)jcur * hd4 + d4);
     {
-        const int n = min(CH, pos + 1 - t0);
-        for (int d = tid; d < hd; d += ATT_THREADS) s_q[d] = __ldcg(m.q + h * hd + d);
-        __syncthreads();
-        {   // scores: 4 threads per position, float4 loads
-            const int j = tid >> 2, sub = tid & 3;
-            float acc = 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < QK; i++) acc = dot4(kv[i], qv[i], acc);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (js < n && sub == 0) s_p[js] = __fmul_rn(acc, scale);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float mx = -3.4028235e+38f;
+        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_p[j]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int j = lane; j < n; j += 32) {
+            const float e = pt_expf(__fsub_rn(s_p[j], mx));
+            s_p[j] = e;
+            sum += e;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) { s_stat[0] = mx; s_stat[1] = sum; }
+    }
+    __syncthreads();
+    if (grp < ngrp) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < VP; k++) {
+            const int j = grp + ngrp * k;
             if (j < n) {
-                const float4 *kr = reinterpret_cast<const float4 *>(m.kc + (head_base + t0 + j) * hd);
-                const float4 *q4 = reinterpret_cast<const float4 *>(s_q);
-#pragma unroll 16
-                for (int k = sub; k < hd4; k += 4) acc = dot4(__ldcg(kr + k), q4[k], acc);
-            }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            if (j < n && sub == 0) s_p[j] = __fmul_rn(acc, scale);
-        }
-        __syncthreads();
-        if (warp == 0) {
-            float mx = -3.4028235e+38f;
-            for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_p[j]);
-            mx = warp_max(mx);
-            float sum = 0.f;
-            for (int j = lane; j < n; j += 32) {
-                const float e = pt_expf(__fsub_rn(s_p[j], mx));
-                s_p[j] = e;
-                sum += e;
-            }
-            sum = warp_sum(sum);
-            if (lane == 0) { s_stat[0] = mx; s_stat[1] = sum; }
-        }
-        __syncthreads();
-        {   // values: thread (float4 column d4, position group grp)
-            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (grp < ngrp) {
-                const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + t0) * hd);
-#pragma unroll 4
-                for (int j = grp; j < n; j += ngrp) {
-                    const float4 v = __ldcg(vb + (size_t)j * hd4 + d4);
-                    const float e = s_p[j];
-                    o.x = fmaf(e, v.x, o.x); o.y = fmaf(e, v.y, o.y);
-                    o.z = fmaf(e, v.z, o.z); o.w = fmaf(e, v.w, o.w);
-                }
-                reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
+                const float e = s_p[j];
+                o.x = fmaf(e, vpre[k].x, o.x); o.y = fmaf(e, vpre[k].y, o.y);
+                o.z = fmaf(e, vpre[k].z, o.z); o.w = fmaf(e, vpre[k].w, o.w);
             }
         }
-        __syncthreads();
+        reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
+    }
+    __syncthreads();
+    {
         if (nc == 1) {   // one chunk: normalise and finish here
             const float inv = __fdiv_rn(1.0f, s_stat[1]);
             for (int d = tid; d < hd; d += ATT_THREADS) {
@@ -346,25 +396,44 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         for (int k = 0; k < n_chunks && k < MV_STAGES; k++)
             mv_issue<MODE>(m, a, stages + k * stage_floats, &bars[k], it0 + k * ps, min(it1, it0 + (k + 1) * ps));
 
-    pdl_wait();
+    // Everything that does not come from the kernel this one depends on is
+    // loaded before the wait: rmsnorm gains (weights), the position and --
+    // for layer 0 -- the token's embedding row (set by an earlier launch).
+    float4 xr[NV], gr[NV];
     int pos = 0;
-    if (MODE == MV_QKV) pos = __ldcg(&m.step->pos);
-    float4 xr[NV];
+    if (MODE == MV_QKV) {
+        pos = __ldcg(&m.step->pos);
+        load_gain<NV>(gr, m.rms_att + (size_t)a.l * m.dim, c4, lane);
+        if (a.from_embedding) load_act<NV>(xr, m.emb + (size_t)__ldcg(&m.step->tok) * m.dim, c4, lane);
+    } else if (MODE == MV_FFN13) {
+        load_gain<NV>(gr, m.rms_ffn + (size_t)a.l * m.dim, c4, lane);
+    } else if (MODE == MV_CLS) {
+        load_gain<NV>(gr, m.rms_final, c4, lane);
+    }
+    pdl_wait();
+    // residual rows this warp will update (RESID): issued with the input
+    constexpr int XPRE = 4;
+    float xres[XPRE];
+    if (MODE == MV_RESID) {
+#pragma unroll
+        for (int k = 0; k < XPRE; k++) {
+            const int i = it0 + k * ps + warp;
+            xres[k] = (lane == 0 && k < n_chunks && i < min(it1, it0 + (k + 1) * ps)) ? __ldcg(m.x + i) : 0.f;
+        }
+    }
     if (MODE == MV_QKV) {
         if (a.from_embedding) {
-            const int tok = __ldcg(&m.step->tok);
-            load_act<NV>(xr, m.emb + (size_t)tok * m.dim, c4, lane);
             if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.x, xr, c4, lane);
         } else {
             load_act<NV>(xr, m.x, c4, lane);
         }
-        rmsnorm_regs<NV>(xr, m.rms_att + (size_t)a.l * m.dim, m.dim, lane);
+        rmsnorm_pre<NV>(xr, gr, m.dim);
     } else if (MODE == MV_FFN13) {
         load_act<NV>(xr, m.x, c4, lane);
-        rmsnorm_regs<NV>(xr, m.rms_ffn + (size_t)a.l * m.dim, m.dim, lane);
+        rmsnorm_pre<NV>(xr, gr, m.dim);
     } else if (MODE == MV_CLS) {
         load_act<NV>(xr, m.x, c4, lane);
-        rmsnorm_regs<NV>(xr, m.rms_final, m.dim, lane);
+        rmsnorm_pre<NV>(xr, gr, m.dim);
         if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.xn, xr, c4, lane);
     } else {
         load_act<NV>(xr, a.in, c4, lane);
@@ -420,7 +489,13 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
                 if (lane == 0) m.hb[i] = silu_mul(h1, h3);
             } else if (MODE == MV_RESID) {
                 const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
-                if (lane == 0) m.x[i] = __fadd_rn(__ldcg(m.x + i), v);
+                if (lane == 0) {
+                    float xo = 0.f;
+#pragma unroll
+                    for (int q = 0; q < XPRE; q++) if (q == k) xo = xres[q];
+                    if (k >= XPRE) xo = __ldcg(m.x + i);
+                    m.x[i] = __fadd_rn(xo, v);
+                }
             } else {
                 const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
                 if (lane == 0) {
@@ -598,7 +673,10 @@ void launch_embed(const DecodeModel &m, cudaStream_t s) {
 }
 
 int decode_attn_limits_ok(int hd, int chunk, int n_chunks) {
-    return hd <= ATT_MAX_HD && hd % 4 == 0 && chunk * 4 == ATT_THREADS && n_chunks <= ATT_MAX_CHUNKS;
+    // scores: 4 threads per position, <= 4 float4 each (hd <= 64); values:
+    // ATT_THREADS / (hd/4) position groups, <= 4 positions per thread
+    return hd <= 64 && hd % 4 == 0 && chunk * 4 == ATT_THREADS && n_chunks <= ATT_MAX_CHUNKS &&
+           chunk <= 4 * (ATT_THREADS / (hd / 4));
 }
 
 }  // namespace ptc

@@ -121,3 +121,15 @@ def test_matvec_callback_is_gpu(ptlib):
     Wn = np.ctypeslib.as_array(W, shape=(cfg.dim, cfg.dim)).copy()
     assert rel_err(y, oracle.matvec(Wn, x)) <= 1e-5
     ctx.close()
+
+
+def test_persistent_kernel_path_matches_reference(ptlib, monkeypatch):
+    """The opt-in single-kernel decode (PTC_DECODE_PERSIST=1) gives the same
+    stream as the reference, through pt_forward_step and the device loop."""
+    monkeypatch.setenv("PTC_DECODE_PERSIST", "1")
+    g = golden("decode_stories15M.npz")
+    ctx = api.Context(synth.make_blob("stories15M"))
+    assert ptlib.ptc_decoder_is_persistent(ctx.ptc_decoder()) == 1
+    check_stream(ctx, "stories15M")
+    assert np.array_equal(ctx.generate_greedy(g["prompt"], 256), g["tokens"])
+    ctx.close()
