@@ -136,11 +136,13 @@ __device__ __forceinline__ void store_vec(float *dst, const float4 (&x)[NV], int
 // ---------------------------------------------------------------------------
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAX_HD = 256;
-constexpr int ATT_MAX_CHUNKS = 256;
+constexpr int ATT_MAX_CHUNKS = 64;
+constexpr int ATT_MERGE_PER_THREAD = 4;   // chunks per merge thread: needs n_chunks <= 4 * groups
 
 __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     pdl_trigger();
     __shared__ float s_p[ATT_MAX_CHUNKS];
+    __shared__ float s_l[ATT_MAX_CHUNKS];
     __shared__ __align__(16) float s_o[ATT_THREADS * 4];
     __shared__ float s_stat[2];
     __shared__ int s_last;
@@ -255,9 +257,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // Merge the nc chunk partials of this head.
+    // Merge the nc chunk partials of this head: every load (chunk maxima,
+    // sums and this thread's slice of the partial outputs) is issued in one
+    // round, then the max-rescaling runs from shared memory and registers.
     const float *hp = m.att_part + (size_t)h * m.n_chunks * (hd + 2);
-    for (int k = tid; k < nc; k += ATT_THREADS) s_p[k] = __ldcg(hp + (size_t)k * (hd + 2) + hd);
+    constexpr int MK = ATT_MERGE_PER_THREAD;
+    float4 po[MK];
+#pragma unroll
+    for (int q = 0; q < MK; q++) {
+        const int k = grp + ngrp * q;
+        const float *pk = hp + (size_t)k * (hd + 2) + 4 * d4;
+        po[q] = (grp < ngrp && k < nc) ? make_float4(__ldcg(pk), __ldcg(pk + 1), __ldcg(pk + 2), __ldcg(pk + 3))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int k = tid; k < nc; k += ATT_THREADS) {
+        s_p[k] = __ldcg(hp + (size_t)k * (hd + 2) + hd);
+        s_l[k] = __ldcg(hp + (size_t)k * (hd + 2) + hd + 1);
+    }
     __syncthreads();
     if (warp == 0) {
         float M = -3.4028235e+38f;
@@ -271,20 +287,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     __syncthreads();
     if (tid == 0) {
         float L = 0.f;
-        for (int k = 0; k < nc; k++) L = fmaf(s_p[k], __ldcg(hp + (size_t)k * (hd + 2) + hd + 1), L);
+        for (int k = 0; k < nc; k++) L = fmaf(s_p[k], s_l[k], L);
         s_stat[1] = __fdiv_rn(1.0f, L);
     }
-    {
+    if (grp < ngrp) {
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (grp < ngrp) {
-            for (int k = grp; k < nc; k += ngrp) {
-                const float *pk = hp + (size_t)k * (hd + 2) + 4 * d4;
+#pragma unroll
+        for (int q = 0; q < MK; q++) {
+            const int k = grp + ngrp * q;
+            if (k < nc) {
                 const float w = s_p[k];
-                o.x = fmaf(w, __ldcg(pk + 0), o.x); o.y = fmaf(w, __ldcg(pk + 1), o.y);
-                o.z = fmaf(w, __ldcg(pk + 2), o.z); o.w = fmaf(w, __ldcg(pk + 3), o.w);
+                o.x = fmaf(w, po[q].x, o.x); o.y = fmaf(w, po[q].y, o.y);
+                o.z = fmaf(w, po[q].z, o.z); o.w = fmaf(w, po[q].w, o.w);
             }
-            reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
         }
+        reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
     }
     __syncthreads();
     const float invL = s_stat[1];
@@ -416,9 +433,9 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     float xres[XPRE];
     if (MODE == MV_RESID) {
 #pragma unroll
-        for (int k = 0; k < XPRE; k++) {
-            const int i = it0 + k * ps + warp;
-            xres[k] = (lane == 0 && k < n_chunks && i < min(it1, it0 + (k + 1) * ps)) ? __ldcg(m.x + i) : 0.f;
+        for (int q = 0; q < XPRE; q++) {
+            const int i = it0 + warp + q * NW;   // this warp's q-th item (direct mode)
+            xres[q] = (lane == 0 && n_chunks <= MV_STAGES && i < it1) ? __ldcg(m.x + i) : 0.f;
         }
     }
     if (MODE == MV_QKV) {
@@ -442,74 +459,93 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
 
     unsigned long long best = 0ull;
     bool ok = true;
-    for (int k = 0; k < n_chunks; k++) {
-        const int s = k % MV_STAGES;
-        const float *stage = stages + s * stage_floats;
-        const bool got = mbar_wait_bounded(&bars[s], (unsigned)((k / MV_STAGES) & 1), m.err, ERR_MBAR_TIMEOUT);
-        if (__syncthreads_or(!got)) {   // block-uniform give-up
-            ok = false;
-            if (tid == 0)   // let copies still in flight land before the CTA exits
-                for (int kk = k + 1; kk < n_chunks && kk < k + MV_STAGES; kk++)
-                    mbar_wait_bounded(&bars[kk % MV_STAGES], (unsigned)((kk / MV_STAGES) & 1), nullptr, 0);
-            break;
-        }
-        const int c0 = it0 + k * ps, c1 = min(it1, c0 + ps);
-        for (int i = c0 + warp; i < c1; i += NW) {
-            const int li = i - c0;
-            if (MODE == MV_QKV) {
-                const float a0 = smem_row_dot<NV>(stage + (size_t)(2 * li) * a.cols, xr, c4, lane);
-                const float a1 = smem_row_dot<NV>(stage + (size_t)(2 * li + 1) * a.cols, xr, c4, lane);
-                if (lane == 0 && pos_ok) {
-                    const int r0 = 2 * i, hd = m.hd;
-                    if (r0 < m.dim + m.kvd) {
-                        const bool is_q = r0 < m.dim;
-                        const int j = is_q ? r0 : r0 - m.dim;
-                        const float th = rope_theta(j, hd, pos);
-                        const float cs = pt_cosf(th), sn = pt_sinf(th);
-                        const float o0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
-                        const float o1 = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
-                        if (is_q) {
-                            m.q[j] = o0;
-                            m.q[j + 1] = o1;
-                        } else {
-                            float *dst = m.kc + (((size_t)a.l * m.nkv + j / hd) * m.seq + pos) * hd + (j % hd);
-                            dst[0] = o0;
-                            dst[1] = o1;
-                        }
+    // One item (row or row pair) from a filled stage: dot products + epilogue.
+    auto do_item = [&](const float *stage, int li, int i, float xo) {
+        if (MODE == MV_QKV) {
+            const float a0 = smem_row_dot<NV>(stage + (size_t)(2 * li) * a.cols, xr, c4, lane);
+            const float a1 = smem_row_dot<NV>(stage + (size_t)(2 * li + 1) * a.cols, xr, c4, lane);
+            if (lane == 0 && pos_ok) {
+                const int r0 = 2 * i, hd = m.hd;
+                if (r0 < m.dim + m.kvd) {
+                    const bool is_q = r0 < m.dim;
+                    const int j = is_q ? r0 : r0 - m.dim;
+                    const float th = rope_theta(j, hd, pos);
+                    const float cs = pt_cosf(th), sn = pt_sinf(th);
+                    const float o0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+                    const float o1 = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+                    if (is_q) {
+                        m.q[j] = o0;
+                        m.q[j + 1] = o1;
                     } else {
-                        const int j = r0 - m.dim - m.kvd;
-                        float *dst = m.vc + (((size_t)a.l * m.nkv + j / hd) * m.seq + pos) * hd + (j % hd);
-                        dst[0] = a0;
-                        dst[1] = a1;
+                        float *dst = m.kc + (((size_t)a.l * m.nkv + j / hd) * m.seq + pos) * hd + (j % hd);
+                        dst[0] = o0;
+                        dst[1] = o1;
                     }
-                }
-            } else if (MODE == MV_FFN13) {
-                const float h1 = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
-                const float h3 = smem_row_dot<NV>(stage + (size_t)(ps + li) * a.cols, xr, c4, lane);
-                if (lane == 0) m.hb[i] = silu_mul(h1, h3);
-            } else if (MODE == MV_RESID) {
-                const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
-                if (lane == 0) {
-                    float xo = 0.f;
-#pragma unroll
-                    for (int q = 0; q < XPRE; q++) if (q == k) xo = xres[q];
-                    if (k >= XPRE) xo = __ldcg(m.x + i);
-                    m.x[i] = __fadd_rn(xo, v);
-                }
-            } else {
-                const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
-                if (lane == 0) {
-                    m.logits[i] = v;
-                    const unsigned long long key = argmax_key(v, i);
-                    if (key > best) best = key;
+                } else {
+                    const int j = r0 - m.dim - m.kvd;
+                    float *dst = m.vc + (((size_t)a.l * m.nkv + j / hd) * m.seq + pos) * hd + (j % hd);
+                    dst[0] = a0;
+                    dst[1] = a1;
                 }
             }
+        } else if (MODE == MV_FFN13) {
+            const float h1 = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
+            const float h3 = smem_row_dot<NV>(stage + (size_t)(ps + li) * a.cols, xr, c4, lane);
+            if (lane == 0) m.hb[i] = silu_mul(h1, h3);
+        } else if (MODE == MV_RESID) {
+            const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
+            if (lane == 0) m.x[i] = __fadd_rn(xo, v);
+        } else {
+            const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
+            if (lane == 0) {
+                m.logits[i] = v;
+                const unsigned long long key = argmax_key(v, i);
+                if (key > best) best = key;
+            }
         }
-        __syncthreads();
-        if (tid == 0 && k + MV_STAGES < n_chunks) {
-            fence_proxy_async_smem();
-            const int kk = k + MV_STAGES;
-            mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps));
+    };
+    if (n_chunks <= MV_STAGES) {
+        // The whole block is in flight at once: each warp takes its items
+        // directly, waiting only for the stage that holds each one.
+        int q = 0;
+        for (int i = it0 + warp; i < it1; i += NW, q++) {
+            const int k = (i - it0) / ps;
+            if (!mbar_wait_bounded(&bars[k], 0u, m.err, ERR_MBAR_TIMEOUT)) {
+                ok = false;
+                break;
+            }
+            float xo = 0.f;
+            if (MODE == MV_RESID && lane == 0) {
+#pragma unroll
+                for (int t = 0; t < XPRE; t++) if (t == q) xo = xres[t];
+                if (q >= XPRE) xo = __ldcg(m.x + i);
+            }
+            do_item(stages + k * stage_floats, (i - it0) % ps, i, xo);
+        }
+        // a warp that gave up leaves copies in flight: let them land
+        if (!ok && lane == 0)
+            for (int k = 0; k < n_chunks; k++) mbar_wait_bounded(&bars[k], 0u, nullptr, 0);
+    } else {
+        for (int k = 0; k < n_chunks; k++) {
+            const int s = k % MV_STAGES;
+            const float *stage = stages + s * stage_floats;
+            const bool got = mbar_wait_bounded(&bars[s], (unsigned)((k / MV_STAGES) & 1), m.err, ERR_MBAR_TIMEOUT);
+            if (__syncthreads_or(!got)) {   // block-uniform give-up
+                ok = false;
+                if (tid == 0)   // let copies still in flight land before the CTA exits
+                    for (int kk = k + 1; kk < n_chunks && kk < k + MV_STAGES; kk++)
+                        mbar_wait_bounded(&bars[kk % MV_STAGES], (unsigned)((kk / MV_STAGES) & 1), nullptr, 0);
+                break;
+            }
+            const int c0 = it0 + k * ps, c1 = min(it1, c0 + ps);
+            for (int i = c0 + warp; i < c1; i += NW)
+                do_item(stage, i - c0, i, (MODE == MV_RESID && lane == 0) ? __ldcg(m.x + i) : 0.f);
+            __syncthreads();
+            if (tid == 0 && k + MV_STAGES < n_chunks) {
+                fence_proxy_async_smem();
+                const int kk = k + MV_STAGES;
+                mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps));
+            }
         }
     }
     (void)ok;
@@ -676,7 +712,7 @@ int decode_attn_limits_ok(int hd, int chunk, int n_chunks) {
     // scores: 4 threads per position, <= 4 float4 each (hd <= 64); values:
     // ATT_THREADS / (hd/4) position groups, <= 4 positions per thread
     return hd <= 64 && hd % 4 == 0 && chunk * 4 == ATT_THREADS && n_chunks <= ATT_MAX_CHUNKS &&
-           chunk <= 4 * (ATT_THREADS / (hd / 4));
+           chunk <= 4 * (ATT_THREADS / (hd / 4)) && n_chunks <= ATT_MERGE_PER_THREAD * (ATT_THREADS / (hd / 4));
 }
 
 }  // namespace ptc

@@ -131,7 +131,7 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     m.att_chunk = 64;
     m.n_chunks = (m.seq + m.att_chunk - 1) / m.att_chunk;
     if (!ptc::decode_attn_limits_ok(m.hd, m.att_chunk, m.n_chunks))
-        PTC_FATAL("attention limits: head_dim %d (multiple of 4, <= 256), seq_len %d (<= 16384)", m.hd, m.seq);
+        PTC_FATAL("attention limits: head_dim %d (multiple of 4, <= 64), seq_len %d (<= 64 chunks of 64)", m.hd, m.seq);
     m.att_part = (float *)ptc_alloc(c, (size_t)m.nh * m.n_chunks * (m.hd + 2) * 4);
     m.att_ticket = (unsigned *)ptc_alloc(c, (size_t)m.nh * 4);
     m.step = (StepState *)ptc_alloc(c, sizeof(StepState));
