@@ -78,6 +78,37 @@ class pt_dist_t(C.Structure):
                 ("timeout_ms", C.c_int)]
 
 
+class pt_token_index_t(C.Structure):
+    _fields_ = [("str", C.c_char_p), ("id", C.c_int)]
+
+
+class pt_tokenizer_t(C.Structure):
+    _fields_ = [("vocab", C.c_void_p), ("vocab_scores", f32p), ("vocab_size", C.c_int),
+                ("max_token_length", C.c_int), ("sorted_ready", C.c_int),
+                ("sorted_vocab", C.POINTER(pt_token_index_t))]
+
+
+class pt_sampler_t(C.Structure):
+    _fields_ = [("vocab_size", C.c_int), ("temperature", C.c_float), ("topp", C.c_float),
+                ("rng_state", C.c_uint64)]
+
+
+def declare_text(L):
+    """Signatures of the text layer (include/pt_text.h). Separate from
+    declare() because the reference's own build exports the same names."""
+    P = C.POINTER
+    _sig(L, "pt_tokenizer_init", None, P(pt_tokenizer_t), C.c_void_p, C.c_int)
+    _sig(L, "pt_load_tokenizer", None, P(pt_tokenizer_t), C.c_void_p, C.c_int)
+    _sig(L, "pt_tokenizer_free", None, P(pt_tokenizer_t))
+    _sig(L, "pt_decode", C.c_char_p, P(pt_tokenizer_t), C.c_int, C.c_int)
+    _sig(L, "pt_encode", None, P(pt_tokenizer_t), C.c_char_p, C.c_int, C.c_int, i32p, i32p)
+    _sig(L, "pt_sampler_init", None, P(pt_sampler_t), C.c_int, C.c_float, C.c_float, C.c_uint64)
+    _sig(L, "pt_sample", C.c_int, P(pt_sampler_t), f32p)
+    _sig(L, "pt_generate", None, P(pt_config_t), P(pt_weights_t), P(pt_state_t), P(pt_tokenizer_t),
+         P(pt_sampler_t), C.c_char_p, C.c_int, vp)
+    return L
+
+
 def _sig(L, name, res, *args):
     f = getattr(L, name, None)
     if f is None:

@@ -158,7 +158,7 @@ void pt_free_state(pt_state_t *s) {
 
 /* The device twin of a host state; created on first use for states from
  * pt_alloc_state, from the image that `w` points into. */
-static struct pt_device *state_device(const pt_config_t *cfg, const pt_weights_t *w, pt_state_t *s) {
+struct pt_device *pt_state_device(const pt_config_t *cfg, const pt_weights_t *w, pt_state_t *s) {
     int i = find_state(s);
     if (i < 0) pt_fatal("pt_state_t %p was not created by pt_alloc_state / pt_*_init", (void *)s);
     if (g_states[i].dev) return g_states[i].dev;
@@ -315,12 +315,9 @@ void pt_matvec_gpu(const float *W, const float *x, float *y, int out_dim, int in
 void pt_forward(const pt_config_t *cfg, const pt_weights_t *w, pt_state_t *s, int token, int pos,
                 pt_matvec_fn matvec) {
     (void)matvec;
-    struct pt_device *d = state_device(cfg, w, s);
+    struct pt_device *d = pt_state_device(cfg, w, s);
     if (!d->has_embed || !d->has_head) pt_fatal("pt_forward needs a full model; use the staged calls");
-    int syncl = 1;
-    for (int i = 0; i < PT_MAX_STATES; i++)
-        if (g_states[i].s == s && !g_states[i].owned) syncl = 1;
-    (void)ptc_decoder_step(d->dec, token, pos, syncl ? s->logits : NULL);
+    (void)ptc_decoder_step(d->dec, token, pos, s->logits);
     ptc_decoder_get_xnorm(d->dec, s->x);
 }
 
@@ -332,7 +329,7 @@ void pt_forward_embed(const pt_weights_t *w, float *x, int dim, int token) {
 void pt_forward_layers_range(const pt_config_t *cfg, const pt_weights_t *w, pt_state_t *s, int pos,
                              int l_start, int l_end, pt_matvec_fn matvec) {
     (void)matvec;
-    struct pt_device *d = state_device(cfg, w, s);
+    struct pt_device *d = pt_state_device(cfg, w, s);
     ptc_decoder_set_x(d->dec, s->x);
     ptc_decoder_enqueue_layers(d->dec, pos, l_start, l_end);
     ptc_decoder_get_x(d->dec, s->x);
@@ -340,7 +337,7 @@ void pt_forward_layers_range(const pt_config_t *cfg, const pt_weights_t *w, pt_s
 
 void pt_forward_head(const pt_config_t *cfg, const pt_weights_t *w, pt_state_t *s, pt_matvec_fn matvec) {
     (void)matvec;
-    struct pt_device *d = state_device(cfg, w, s);
+    struct pt_device *d = pt_state_device(cfg, w, s);
     if (!d->has_head) pt_fatal("pt_forward_head on a state without the classifier");
     ptc_decoder_set_x(d->dec, s->x);
     ptc_decoder_enqueue_head(d->dec);

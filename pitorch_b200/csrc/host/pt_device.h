@@ -39,4 +39,7 @@ int pt_pick_device(int requested);
 
 void pt_fatal(const char *fmt, ...);
 
+/* The device twin of a host decode state (created on first use). */
+struct pt_device *pt_state_device(const pt_config_t *cfg, const pt_weights_t *w, pt_state_t *s);
+
 #endif

@@ -135,7 +135,6 @@ __device__ __forceinline__ void store_vec(float *dst, const float4 (&x)[NV], int
 // values and the merge), so a phase costs one memory round trip.
 // ---------------------------------------------------------------------------
 constexpr int ATT_THREADS = 256;
-constexpr int ATT_MAX_HD = 256;
 constexpr int ATT_MAX_CHUNKS = 64;
 constexpr int ATT_MERGE_PER_THREAD = 4;   // chunks per merge thread: needs n_chunks <= 4 * groups
 
