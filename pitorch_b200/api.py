@@ -208,6 +208,7 @@ def declare(L):
     _sig(L, "ptc_timer_stop", None, vp)
     _sig(L, "ptc_timer_ms", C.c_float, vp)
     _sig(L, "ptc_timer_destroy", None, vp)
+    return declare_text(L)
 
 
 def fp(a):
