@@ -170,6 +170,13 @@ __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
     return acc;
 }
 
+// Vector reduction into global memory (performed at L2): dst 16-byte aligned.
+__device__ __forceinline__ void red_add_v4(float *dst, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+
 // Programmatic dependent launch (sm_90+): wait for the producer grid's
 // memory, and let the next grid in the stream start its prologue early.
 __device__ __forceinline__ void pdl_wait() {

@@ -35,6 +35,14 @@ struct DecodeModel {
     float *att;      // [dim] attention output (input of wo)
     float *hb;       // [hidden] silu(w1 x) * (w3 x)
     float *logits;   // [V]
+    // Fused-FFN path: xm is the post-attention residual (FFN input), xo the
+    // per-layer outputs [L][dim] that the next layer consumes, w2t the
+    // transposed w2 [L][hidden][dim]. The FFN kernel accumulates into a
+    // zeroed buffer; whoever reads a layer input last zeroes it again.
+    float *xm, *xo;
+    const float *w2t;
+    int fused_ffn;   // 1: k_ffn replaces k_mv<FFN13> + k_mv<RESID>(w2)
+    int ffn_rows;    // hidden units per k_ffn CTA (capacity of its shared memory)
     // KV cache, head-major: [L][nkv][seq][hd]
     float *kc, *vc;
     // attention split-K partials: [nh][n_chunks][hd + 2] and per-head tickets
@@ -51,7 +59,12 @@ struct DecodeModel {
 constexpr int MV_THREADS = 256;
 constexpr int MV_STAGES = 4;
 constexpr int MV_STAGE_BYTES = 24 * 1024;
-constexpr int MV_SMEM_BYTES = MV_STAGES * MV_STAGE_BYTES + MV_STAGES * 8;
+constexpr int MV_BAR_BYTES = 128;   // mbarriers at the front, stages 128-byte aligned after
+constexpr int MV_SMEM_BYTES = MV_BAR_BYTES + MV_STAGES * MV_STAGE_BYTES;
+
+// Fused FFN (k_ffn): one CTA per SM, whole w1/w3/w2t row blocks resident.
+constexpr int FF_THREADS = 256;
+constexpr int FF_MAX_SMEM = 200 * 1024;
 
 // Error codes written to DecodeModel::err.
 constexpr int ERR_MBAR_TIMEOUT = 1;

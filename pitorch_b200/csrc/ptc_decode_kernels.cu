@@ -335,7 +335,10 @@ enum MvMode { MV_QKV = 0, MV_FFN13 = 1, MV_RESID = 2, MV_CLS = 3 };
 
 struct MvArgs {
     const float *W;    // MV_RESID: the matrix; MV_CLS: wcls
-    const float *in;   // MV_RESID input vector
+    const float *in;   // MV_RESID: input vector; MV_QKV: the layer input x
+    float *res_in;        // MV_RESID: residual source, row r read once
+    float *res_out;       // MV_RESID: receives res_in[r] + W[r] . in
+    int zero_res_in;      // MV_RESID: clear res_in[r] after reading it
     int n_items;       // items over the whole grid
     int cols;          // row length in floats
     int slots;         // rows per item
@@ -390,8 +393,8 @@ template <int NV, int MODE>
 __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     pdl_trigger();
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    float *stages = reinterpret_cast<float *>(smem_raw);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw + MV_STAGES * MV_STAGE_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
+    float *stages = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES);
     __shared__ unsigned long long s_best[MV_THREADS / 32];
     __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -434,14 +437,14 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
 #pragma unroll
         for (int q = 0; q < XPRE; q++) {
             const int i = it0 + warp + q * NW;   // this warp's q-th item (direct mode)
-            xres[q] = (lane == 0 && n_chunks <= MV_STAGES && i < it1) ? __ldcg(m.x + i) : 0.f;
+            xres[q] = (lane == 0 && n_chunks <= MV_STAGES && i < it1) ? __ldcg(a.res_in + i) : 0.f;
         }
     }
     if (MODE == MV_QKV) {
         if (a.from_embedding) {
             if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.x, xr, c4, lane);
         } else {
-            load_act<NV>(xr, m.x, c4, lane);
+            load_act<NV>(xr, a.in, c4, lane);
         }
         rmsnorm_pre<NV>(xr, gr, m.dim);
     } else if (MODE == MV_FFN13) {
@@ -493,7 +496,10 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             if (lane == 0) m.hb[i] = silu_mul(h1, h3);
         } else if (MODE == MV_RESID) {
             const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
-            if (lane == 0) m.x[i] = __fadd_rn(xo, v);
+            if (lane == 0) {
+                a.res_out[i] = __fadd_rn(xo, v);
+                if (a.zero_res_in) a.res_in[i] = 0.f;
+            }
         } else {
             const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
             if (lane == 0) {
@@ -517,7 +523,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             if (MODE == MV_RESID && lane == 0) {
 #pragma unroll
                 for (int t = 0; t < XPRE; t++) if (t == q) xo = xres[t];
-                if (q >= XPRE) xo = __ldcg(m.x + i);
+                if (q >= XPRE) xo = __ldcg(a.res_in + i);
             }
             do_item(stages + k * stage_floats, (i - it0) % ps, i, xo);
         }
@@ -538,7 +544,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             }
             const int c0 = it0 + k * ps, c1 = min(it1, c0 + ps);
             for (int i = c0 + warp; i < c1; i += NW)
-                do_item(stage, i - c0, i, (MODE == MV_RESID && lane == 0) ? __ldcg(m.x + i) : 0.f);
+                do_item(stage, i - c0, i, (MODE == MV_RESID && lane == 0) ? __ldcg(a.res_in + i) : 0.f);
             __syncthreads();
             if (tid == 0 && k + MV_STAGES < n_chunks) {
                 fence_proxy_async_smem();
@@ -578,6 +584,108 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         st->pos = p + 1;
     }
     __threadfence();
+}
+
+// ---------------------------------------------------------------------------
+// k_ffn: the whole feed-forward block of one layer in one kernel
+// (llama2.c:279-287): rmsnorm(x) -> h1 = w1 x, h3 = w3 x -> hb = silu(h1)*h3
+// -> x_out = x + w2 hb. CTA b owns hidden units [j0, j1): it holds their
+// w1 and w3 rows and the matching rows of the transposed w2 (w2t[j] = column
+// j of w2) in shared memory, all fetched by bulk copies before
+// griddepcontrol.wait. After the wait it normalises x, produces its hb
+// values, and adds its partial w2 product -- a full dim-vector -- into the
+// zeroed output with vector reductions at L2 (CTA 0 also adds the residual).
+// The split over hidden units makes w2 a split-K product summed by L2
+// atomics, so no other kernel has to wait for hb.
+// ---------------------------------------------------------------------------
+constexpr int FF_MAX_ROWS = 64;
+
+struct FfnArgs {
+    const float *xin;  // FFN input and residual (post-attention x)
+    float *xout;       // zero on entry; receives x + w2 . hb
+    int l;
+};
+
+template <int NV>
+__global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a) {
+    pdl_trigger();
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
+    const int dim = m.dim, c4 = dim >> 2, R = m.ffn_rows;
+    float *w1s = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES);   // [R][dim]
+    float *w3s = w1s + (size_t)R * dim;                                 // [R][dim]
+    float *w2s = w3s + (size_t)R * dim;                                 // [R][dim]
+    __shared__ float s_hb[FF_MAX_ROWS];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = FF_THREADS / 32;
+    const int j0 = (int)((long)m.hidden * blockIdx.x / gridDim.x);
+    const int j1 = (int)((long)m.hidden * (blockIdx.x + 1) / gridDim.x);
+    const int nj = j1 - j0;
+    const unsigned bytes = (unsigned)nj * (unsigned)dim * 4u;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const size_t off = ((size_t)a.l * m.hidden + j0) * dim;
+        mbar_expect_tx(&bars[0], 2u * bytes);
+        bulk_g2s(w1s, m.w1 + off, bytes, &bars[0]);
+        bulk_g2s(w3s, m.w3 + off, bytes, &bars[0]);
+        mbar_expect_tx(&bars[1], bytes);
+        bulk_g2s(w2s, m.w2t + off, bytes, &bars[1]);
+    }
+    float4 xr[NV], gr[NV];
+    load_gain<NV>(gr, m.rms_ffn + (size_t)a.l * dim, c4, lane);
+    pdl_wait();
+    load_act<NV>(xr, a.xin, c4, lane);
+    // the residual this thread adds (CTA 0): issued with the input
+    constexpr int RV = 2;   // float4 columns per thread: dim <= 4 * RV * FF_THREADS
+    float4 res[RV];
+#pragma unroll
+    for (int r = 0; r < RV; r++) {
+        const int c = tid + r * FF_THREADS;
+        res[r] = (blockIdx.x == 0 && c < c4) ? __ldcg(reinterpret_cast<const float4 *>(a.xin) + c)
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    rmsnorm_pre<NV>(xr, gr, dim);
+
+    bool ok = mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT);
+    if (__syncthreads_or(!ok)) {
+        if (tid == 0) {   // let the copies still in flight land before exiting
+            mbar_wait_bounded(&bars[0], 0u, nullptr, 0);
+            mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
+        }
+        return;
+    }
+    for (int j = warp; j < nj; j += NW) {
+        const float h1 = smem_row_dot<NV>(w1s + (size_t)j * dim, xr, c4, lane);
+        const float h3 = smem_row_dot<NV>(w3s + (size_t)j * dim, xr, c4, lane);
+        if (lane == 0) s_hb[j] = silu_mul(h1, h3);
+    }
+    ok = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
+    if (__syncthreads_or(!ok)) {   // also publishes s_hb
+        if (tid == 0) mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
+        return;
+    }
+    const float4 *w2s4 = reinterpret_cast<const float4 *>(w2s);
+#pragma unroll
+    for (int r = 0; r < RV; r++) {
+        const int c = tid + r * FF_THREADS;
+        if (c < c4) {
+            float4 acc = res[r];
+            for (int j = 0; j < nj; j++) {
+                const float h = s_hb[j];
+                const float4 w = w2s4[(size_t)j * c4 + c];
+                acc.x = fmaf(h, w.x, acc.x);
+                acc.y = fmaf(h, w.y, acc.y);
+                acc.z = fmaf(h, w.z, acc.z);
+                acc.w = fmaf(h, w.w, acc.w);
+            }
+            red_add_v4(a.xout + 4 * c, acc);
+        }
+    }
 }
 
 // Host-side launchers --------------------------------------------------------
@@ -650,7 +758,14 @@ static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) 
     a.per_stage = MV_STAGE_BYTES / item_bytes;
     if (a.per_stage < 1) PTC_FATAL("decode row of %d floats does not fit a staging buffer", a.cols);
     const int grid = a.n_items < n_sm ? a.n_items : n_sm;
-    launch_pdl(k_mv<NV, MODE>, dim3(grid), dim3(MV_THREADS), (size_t)MV_SMEM_BYTES, s, m, a);
+    // Only the stages a CTA can fill are reserved, so that the next kernels
+    // of the chain fit beside this one on an SM and start their weight
+    // streams early.
+    const int items_max = (a.n_items + grid - 1) / grid;
+    int stages = (items_max + a.per_stage - 1) / a.per_stage;
+    if (stages > MV_STAGES) stages = MV_STAGES;
+    const size_t smem = (size_t)MV_BAR_BYTES + (size_t)stages * MV_STAGE_BYTES;
+    launch_pdl(k_mv<NV, MODE>, dim3(grid), dim3(MV_THREADS), smem, s, m, a);
 }
 
 static MvArgs mv_args(int n_items, int cols, int slots, int l) {
@@ -663,10 +778,40 @@ static MvArgs mv_args(int n_items, int cols, int slots, int l) {
     return a;
 }
 
-void launch_layer(const DecodeModel &m, int l, bool from_embedding, int n_sm, cudaStream_t s) {
+template <int NV>
+static void launch_ffn(const DecodeModel &m, FfnArgs a, int n_sm, cudaStream_t s) {
+    static bool configured = false;  // per instantiation
+    if (!configured) {
+        PTC_CHECK(cudaFuncSetAttribute(k_ffn<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       MV_BAR_BYTES + FF_MAX_SMEM));
+        PTC_CHECK(cudaFuncSetAttribute(k_ffn<NV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        configured = true;
+    }
+    const int grid = m.hidden < n_sm ? m.hidden : n_sm;
+    const size_t smem = (size_t)MV_BAR_BYTES + 3 * (size_t)m.ffn_rows * m.dim * 4;
+    launch_pdl(k_ffn<NV>, dim3(grid), dim3(FF_THREADS), smem, s, m, a);
+}
+
+// Hidden units per k_ffn CTA for this model and grid, or 0 when the fused
+// FFN does not fit (rows in shared memory, output columns per thread).
+int decode_ffn_rows(int dim, int hidden, int n_sm) {
+    const int grid = hidden < n_sm ? hidden : n_sm;
+    const int rows = (hidden + grid - 1) / grid;
+    if (rows > FF_MAX_ROWS || dim / 4 > 2 * FF_THREADS) return 0;
+    if (3 * (size_t)rows * dim * 4 > (size_t)FF_MAX_SMEM) return 0;
+    return rows;
+}
+
+// One layer with explicit residual-stream buffers: the layer reads x_in
+// (rmsnorm input and attention residual) and leaves its output in x_out.
+// Fused FFN: wo writes xm = x_in + wo.att and clears x_in behind it, k_ffn
+// accumulates xm + w2.hb into x_out, which is zero on entry.
+static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float *x_in, float *x_out, int n_sm,
+                         cudaStream_t s) {
     const int nvd = nv_of(m.dim), nvh = nv_of(m.hidden);
     MvArgs a = mv_args((m.dim + 2 * m.kvd) / 2, m.dim, 2, l);
     a.from_embedding = from_embedding ? 1 : 0;
+    a.in = x_in;
     PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_QKV>(m, a, n_sm, s)));
     static bool attn_configured = false;
     if (!attn_configured) {
@@ -678,13 +823,46 @@ void launch_layer(const DecodeModel &m, int l, bool from_embedding, int n_sm, cu
     a = mv_args(m.dim, m.dim, 1, l);
     a.W = m.wo + (size_t)l * m.dim * m.dim;
     a.in = m.att;
+    if (m.fused_ffn) {
+        a.res_in = x_in;
+        a.res_out = m.xm;
+        a.zero_res_in = 1;
+        PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_RESID>(m, a, n_sm, s)));
+        FfnArgs f;
+        f.xin = m.xm;
+        f.xout = x_out;
+        f.l = l;
+        PTC_NV_SWITCH(nvd, (launch_ffn<NV>(m, f, n_sm, s)));
+        return;
+    }
+    // unfused: x_in == x_out, updated in place
+    a.res_in = x_in;
+    a.res_out = x_in;
     PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_RESID>(m, a, n_sm, s)));
     a = mv_args(m.hidden, m.dim, 2, l);
+    a.in = x_in;
     PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_FFN13>(m, a, n_sm, s)));
     a = mv_args(m.dim, m.hidden, 1, l);
     a.W = m.w2 + (size_t)l * m.dim * m.hidden;
     a.in = m.hb;
+    a.res_in = x_in;
+    a.res_out = x_in;
     PTC_NV_SWITCH(nvh, (launch_mv<NV, MV_RESID>(m, a, n_sm, s)));
+}
+
+// Layers [l0, l1): the range reads m.x and leaves its output in m.x. With
+// the fused FFN, layer l < l1-1 hands over through xo[l] (zeroed again by
+// the next layer's wo once read); the last layer accumulates into m.x,
+// which the first layer's wo cleared.
+void launch_layers(const DecodeModel &m, int l0, int l1, bool from_embedding, int n_sm, cudaStream_t s) {
+    for (int l = l0; l < l1; l++) {
+        float *x_in = m.x, *x_out = m.x;
+        if (m.fused_ffn) {
+            x_in = (l == l0) ? m.x : m.xo + (size_t)(l - 1) * m.dim;
+            x_out = (l == l1 - 1) ? m.x : m.xo + (size_t)l * m.dim;
+        }
+        launch_layer(m, l, from_embedding && l == 0, x_in, x_out, n_sm, s);
+    }
 }
 
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s) {

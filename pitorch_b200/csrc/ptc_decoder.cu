@@ -44,7 +44,7 @@ struct ptc_decoder {
 static void enqueue_kernels(ptc_decoder *d, cudaStream_t s) {
     const DecodeModel &m = d->m;
     if (d->has_embed && m.L == 0) ptc::launch_embed(m, s);
-    for (int l = 0; l < m.L; l++) ptc::launch_layer(m, l, d->has_embed && l == 0, d->n_sm, s);
+    ptc::launch_layers(m, 0, m.L, d->has_embed != 0, d->n_sm, s);
     if (d->has_head) ptc::launch_head(m, d->n_sm, s);
 }
 
@@ -139,6 +139,22 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     d->d_tokens = (int *)ptc_alloc(c, (size_t)(m.seq + 1) * 4);
 
     cudaStream_t s = d->stream;
+    // Fused FFN (default where it fits; PTC_DECODE_FUSED=0 selects the
+    // five-kernel layer): needs the transposed w2 and the hand-over buffers.
+    const char *want_fused = getenv("PTC_DECODE_FUSED");
+    m.ffn_rows = ptc::decode_ffn_rows(m.dim, m.hidden, d->n_sm);
+    m.fused_ffn = m.L > 0 && m.ffn_rows > 0 && !(want_fused && want_fused[0] == '0');
+    if (m.fused_ffn || (m.L > 0 && ptc::persist_supported(m, d->n_sm))) {
+        float *w2t = (float *)ptc_alloc(c, (size_t)m.L * m.hidden * m.dim * 4);
+        ptc::persist_transpose_w2(m, w2t, s);
+        m.w2t = w2t;
+    }
+    if (m.fused_ffn) {
+        m.xm = (float *)ptc_alloc(c, (size_t)m.dim * 4);
+        m.xo = (float *)ptc_alloc(c, (size_t)m.L * m.dim * 4);
+        PTC_CHECK(cudaMemsetAsync(m.xm, 0, (size_t)m.dim * 4, s));
+        PTC_CHECK(cudaMemsetAsync(m.xo, 0, (size_t)m.L * m.dim * 4, s));
+    }
     PTC_CHECK(cudaMemsetAsync(m.x, 0, m.dim * 4, s));
     PTC_CHECK(cudaMemsetAsync(m.kc, 0, kv ? kv : 4, s));
     PTC_CHECK(cudaMemsetAsync(m.vc, 0, kv ? kv : 4, s));
@@ -175,13 +191,11 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
         pa.m = m;
         pa.has_embed = has_embed;
         pa.has_head = has_head;
-        float *w2t = (float *)ptc_alloc(c, (size_t)m.L * m.hidden * m.dim * 4);
-        pa.w2t = w2t;
+        pa.w2t = m.w2t;
         pa.x1 = (float *)ptc_alloc(c, (size_t)m.dim * 4);
         pa.max_chunks = d->n_sm / m.nh > 0 ? d->n_sm / m.nh : 1;
         pa.att_part = (float *)ptc_alloc(c, (size_t)m.nh * pa.max_chunks * (m.hd + 2) * 4);
         pa.bar = (unsigned *)ptc_alloc(c, 256);
-        ptc::persist_transpose_w2(m, w2t, s);
         PTC_CHECK(cudaStreamSynchronize(s));
     }
     d->loop_pos = 0;
@@ -189,10 +203,10 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
 }
 
 // Re-derive device-side copies that depend on the weights (the transposed
-// w2 of the persistent path) after the weights were updated in place.
+// w2 of the fused FFN and the persistent path) after an in-place update.
 extern "C" void ptc_decoder_weights_updated(ptc_decoder *d) {
-    if (!d->persist) return;
-    ptc::persist_transpose_w2(d->m, (float *)d->pa.w2t, d->stream);
+    if (!d->m.w2t) return;
+    ptc::persist_transpose_w2(d->m, (float *)d->m.w2t, d->stream);
 }
 
 extern "C" int ptc_decoder_is_persistent(ptc_decoder *d) { return d->persist ? 1 : 0; }
@@ -356,7 +370,7 @@ extern "C" void ptc_decoder_enqueue_layers(ptc_decoder *d, int pos, int l_start,
         PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
     set_mode(d, 0);
     put_step_int(d, &d->m.step->pos, pos);
-    for (int l = l_start; l < l_end; l++) ptc::launch_layer(d->m, l, false, d->n_sm, d->stream);
+    ptc::launch_layers(d->m, l_start, l_end, false, d->n_sm, d->stream);
 }
 
 // Mode is the caller's: host-mode callers set it through the functions that
@@ -382,7 +396,7 @@ extern "C" int *ptc_decoder_tok_dev(ptc_decoder *d) { return &d->m.step->tok; }
 extern "C" void ptc_decoder_enqueue_layers_devpos(ptc_decoder *d, int l_start, int l_end) {
     if (l_start < 0 || l_end > d->m.L || l_start > l_end)
         PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
-    for (int l = l_start; l < l_end; l++) ptc::launch_layer(d->m, l, false, d->n_sm, d->stream);
+    ptc::launch_layers(d->m, l_start, l_end, false, d->n_sm, d->stream);
 }
 
 extern "C" void ptc_decoder_enqueue_embed_dev(ptc_decoder *d) {

@@ -133,3 +133,15 @@ def test_persistent_kernel_path_matches_reference(ptlib, monkeypatch):
     check_stream(ctx, "stories15M")
     assert np.array_equal(ctx.generate_greedy(g["prompt"], 256), g["tokens"])
     ctx.close()
+
+
+def test_unfused_layer_path_matches_reference(ptlib, monkeypatch):
+    """PTC_DECODE_FUSED=0 selects the five-kernel layer (separate w1/w3 and
+    w2 matvecs); it gives the same stream as the default fused FFN."""
+    monkeypatch.setenv("PTC_DECODE_FUSED", "0")
+    ctx = api.Context(synth.make_blob("stories15M"))
+    check_stream(ctx, "stories15M")
+    ctx.close()
+    ctx = api.Context(synth.make_blob("tiny"))
+    check_stream(ctx, "tiny")
+    ctx.close()
