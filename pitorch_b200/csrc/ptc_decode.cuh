@@ -43,6 +43,10 @@ struct DecodeModel {
     const float *w2t;
     int fused_ffn;   // 1: k_ffn replaces k_mv<FFN13> + k_mv<RESID>(w2)
     int ffn_rows;    // hidden units per k_ffn CTA (capacity of its shared memory)
+    int fused_attn;  // 1: k_attn_fused replaces k_mv<QKV> + k_attn + k_mv<RESID>(wo)
+    int attn_stage;  // floats of k_attn_fused's shared staging region
+    unsigned *tickets;  // [0] k_attn_fused, [1] k_ffn: CTAs done reading their input
+    const float2 *rope;  // [seq][hd/2] (cos, sin) of the RoPE angle (k_attn_fused)
     // KV cache, head-major: [L][nkv][seq][hd]
     float *kc, *vc;
     // attention split-K partials: [nh][n_chunks][hd + 2] and per-head tickets

@@ -21,9 +21,12 @@
 #include "ptc_decode.cuh"
 #include "ptc_internal.h"
 
+#include <cooperative_groups.h>
 #include <string.h>
 
 #include <utility>
+
+namespace cg = cooperative_groups;
 
 namespace ptc {
 
@@ -603,6 +606,7 @@ constexpr int FF_MAX_ROWS = 64;
 struct FfnArgs {
     const float *xin;  // FFN input and residual (post-attention x)
     float *xout;       // zero on entry; receives x + w2 . hb
+    float *xclear;     // cleared once every CTA has read the input (null: none)
     int l;
 };
 
@@ -616,6 +620,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
     float *w3s = w1s + (size_t)R * dim;                                 // [R][dim]
     float *w2s = w3s + (size_t)R * dim;                                 // [R][dim]
     __shared__ float s_hb[FF_MAX_ROWS];
+    __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = FF_THREADS / 32;
     const int j0 = (int)((long)m.hidden * blockIdx.x / gridDim.x);
@@ -650,42 +655,377 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     rmsnorm_pre<NV>(xr, gr, dim);
-
-    bool ok = mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT);
-    if (__syncthreads_or(!ok)) {
-        if (tid == 0) {   // let the copies still in flight land before exiting
-            mbar_wait_bounded(&bars[0], 0u, nullptr, 0);
-            mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
-        }
-        return;
-    }
-    for (int j = warp; j < nj; j += NW) {
-        const float h1 = smem_row_dot<NV>(w1s + (size_t)j * dim, xr, c4, lane);
-        const float h3 = smem_row_dot<NV>(w3s + (size_t)j * dim, xr, c4, lane);
-        if (lane == 0) s_hb[j] = silu_mul(h1, h3);
-    }
-    ok = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
-    if (__syncthreads_or(!ok)) {   // also publishes s_hb
-        if (tid == 0) mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
-        return;
-    }
-    const float4 *w2s4 = reinterpret_cast<const float4 *>(w2s);
+    // The input is consumed (rmsnorm; the residual registers are forced
+    // below): take the ticket now, look at it when the CTA ends.
 #pragma unroll
-    for (int r = 0; r < RV; r++) {
-        const int c = tid + r * FF_THREADS;
-        if (c < c4) {
-            float4 acc = res[r];
-            for (int j = 0; j < nj; j++) {
-                const float h = s_hb[j];
-                const float4 w = w2s4[(size_t)j * c4 + c];
-                acc.x = fmaf(h, w.x, acc.x);
-                acc.y = fmaf(h, w.y, acc.y);
-                acc.z = fmaf(h, w.z, acc.z);
-                acc.w = fmaf(h, w.w, acc.w);
+    for (int r = 0; r < RV; r++) asm volatile("" ::"f"(res[r].x), "f"(res[r].y), "f"(res[r].z), "f"(res[r].w));
+    __syncthreads();
+    unsigned ticket = 0u;
+    if (a.xclear && tid == FF_THREADS - 1) ticket = atomicAdd(&m.tickets[1], 1u);
+
+    // A failed wait is recorded in m.err; the CTA then skips its products
+    // but still takes part in the ticket.
+    bool ok = __syncthreads_and(mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT));
+    if (ok)
+        for (int j = warp; j < nj; j += NW) {
+            const float h1 = smem_row_dot<NV>(w1s + (size_t)j * dim, xr, c4, lane);
+            const float h3 = smem_row_dot<NV>(w3s + (size_t)j * dim, xr, c4, lane);
+            if (lane == 0) s_hb[j] = silu_mul(h1, h3);
+        }
+    if (ok) ok = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
+    ok = __syncthreads_and(ok);   // also publishes s_hb
+    if (ok) {
+        const float4 *w2s4 = reinterpret_cast<const float4 *>(w2s);
+#pragma unroll
+        for (int r = 0; r < RV; r++) {
+            const int c = tid + r * FF_THREADS;
+            if (c < c4) {
+                float4 acc = res[r];
+                for (int j = 0; j < nj; j++) {
+                    const float h = s_hb[j];
+                    const float4 w = w2s4[(size_t)j * c4 + c];
+                    acc.x = fmaf(h, w.x, acc.x);
+                    acc.y = fmaf(h, w.y, acc.y);
+                    acc.z = fmaf(h, w.z, acc.z);
+                    acc.w = fmaf(h, w.w, acc.w);
+                }
+                red_add_v4(a.xout + 4 * c, acc);
             }
-            red_add_v4(a.xout + 4 * c, acc);
+        }
+    } else if (tid == 0) {   // let the copies still in flight land before exiting
+        mbar_wait_bounded(&bars[0], 0u, nullptr, 0);
+        mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
+    }
+    if (a.xclear) {
+        if (tid == FF_THREADS - 1) s_last = (ticket == gridDim.x - 1);
+        __syncthreads();
+        if (s_last) {
+            for (int i = tid; i < c4; i += FF_THREADS)
+                reinterpret_cast<float4 *>(a.xclear)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (tid == 0) m.tickets[1] = 0u;
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// k_attn_fused: the attention half of one layer (llama2.c:229-277) as one
+// kernel of n_heads clusters of AC CTAs. Cluster h does, for head h:
+//   1. rmsnorm(x) and its share of the head's 3*hd q/k/v rows (held in shared
+//      memory, bulk-copied before griddepcontrol.wait); every CTA sends its
+//      raw results to all CTAs of the cluster through distributed shared
+//      memory; cluster barrier;
+//   2. RoPE on q and k (every CTA, same arithmetic); CTA 0 writes the new
+//      K/V row of `pos` into the cache;
+//   3. attention over its chunk of positions [0, pos] (K/V rows of earlier
+//      positions were loaded into registers before the wait), kept as an
+//      online-softmax partial (max, sum, unnormalised output); partials are
+//      exchanged through distributed shared memory; cluster barrier;
+//   4. every CTA merges the AC partials into the head's attention output and
+//      multiplies it by its slice of wo (rows [o0, o1), columns of head h),
+//      adding the result into the zeroed output with vector reductions; the
+//      cluster of head 0 also adds the residual x.
+// The only grid-wide dependency is the output sum at L2, so the layer's
+// attention costs one kernel boundary instead of three.
+// ---------------------------------------------------------------------------
+constexpr int AC = 8;                 // CTAs per head (cluster size, portable)
+constexpr int AT_THREADS = 256;
+constexpr int AT_MAX_HD = 64;
+constexpr int AT_ROUND = 64;          // positions per attention round (4 threads each)
+constexpr int AT_MAX_OUT = 256;       // wo rows per CTA (dim <= 2048)
+
+struct AttnArgs {
+    const float *xin;  // layer input; null: the embedding row of step->tok (layer 0)
+    float *xout;       // zero on entry; receives x + wo . attention
+    float *xclear;     // cleared once every CTA has read the input
+    int l;
+    int stage_floats;  // shared staging region (q/k/v rows, then wo slice + value sums)
+};
+
+template <int NV>
+__global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, AttnArgs a) {
+    // The next kernel (k_ffn) may start at once: its 18.9 MB (110M) weight
+    // stream must be resident by its wait. Releasing it later, after this
+    // kernel's input read, measured slower (its stream then lands on this
+    // kernel's cluster exchange instead).
+    pdl_trigger();
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);   // [0] q/k/v rows
+    float *stage = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES);
+    __shared__ __align__(16) float s_qkv[3 * AT_MAX_HD];        // this head's q, k, v (all CTAs' rows)
+    __shared__ __align__(16) float s_part[AC][AT_MAX_HD + 4];   // per-CTA o[hd], max, sum
+    __shared__ __align__(16) float s_att[AT_MAX_HD];
+    __shared__ __align__(16) float s_res[AT_MAX_OUT];
+    __shared__ float s_sc[AT_ROUND];
+    __shared__ float s_stat[2];
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = AT_THREADS / 32;
+    const int r = (int)cluster.block_rank();
+    const int h = blockIdx.x / AC;
+    const int dim = m.dim, hd = m.hd, hd4 = hd >> 2, c4 = dim >> 2, l = a.l;
+    const int q0 = 3 * hd * r / AC, q1 = 3 * hd * (r + 1) / AC;   // q/k/v rows of this CTA
+    const int o0 = dim * r / AC, o1 = dim * (r + 1) / AC;         // wo rows of this CTA
+    const int pos_raw = __ldcg(&m.step->pos);
+    const bool pos_ok = pos_raw >= 0 && pos_raw < m.seq;
+    const int pos = pos_ok ? pos_raw : 0;
+    // positions of this CTA: [t0, t1) of [0, pos]
+    const int ppc = (pos + AC) / AC;
+    const int t0 = min(r * ppc, pos + 1), t1 = min(t0 + ppc, pos + 1);
+    const size_t head_base = ((size_t)l * m.nkv + h) * m.seq;
+
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const size_t D = dim, K = m.kvd;
+        const float *mats[3] = {m.wq + (size_t)l * D * D, m.wk + (size_t)l * K * D, m.wv + (size_t)l * K * D};
+        mbar_expect_tx(&bars[0], (unsigned)((q1 - q0) * dim * 4));
+        for (int sgm = 0; sgm < 3; sgm++) {
+            const int lo = max(q0, sgm * hd), hi = min(q1, (sgm + 1) * hd);
+            if (lo < hi)
+                bulk_g2s(stage + (size_t)(lo - q0) * dim, mats[sgm] + (size_t)(h * hd + lo - sgm * hd) * dim,
+                         (unsigned)((hi - lo) * dim * 4), &bars[0]);
+        }
+    }
+    if (tid == 32 && t1 - t0 > AT_ROUND) {
+        // positions past the first round are read after the wait: warm L2
+        const int tp = t0 + AT_ROUND, te = min(t1, pos);
+        if (te > tp) {
+            prefetch_l2(m.kc + (head_base + tp) * hd, (unsigned)((te - tp) * hd * 4));
+            prefetch_l2(m.vc + (head_base + tp) * hd, (unsigned)((te - tp) * hd * 4));
+        }
+    }
+    // K/V rows of the first round's earlier positions: written by earlier
+    // tokens, so read before the wait (the row of pos comes from step 2).
+    const int js = tid >> 2, sub = tid & 3;
+    const int ngrp = AT_THREADS / hd4, d4 = tid % hd4, grp = tid / hd4;
+    constexpr int QK = 4, VP = 4;
+    float4 kv[QK], vpre[VP];
+    {
+        const float4 *kb = reinterpret_cast<const float4 *>(m.kc + (head_base + t0) * hd);
+        const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + t0) * hd);
+        const int n0 = min(AT_ROUND, t1 - t0);
+#pragma unroll
+        for (int i = 0; i < QK; i++) {
+            const int cc = sub + 4 * i;
+            kv[i] = (cc < hd4 && js < n0 && t0 + js != pos) ? __ldcg(kb + (size_t)js * hd4 + cc)
+                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < VP; k++) {
+            const int j = grp + ngrp * k;
+            vpre[k] = (grp < ngrp && j < n0 && t0 + j != pos) ? __ldcg(vb + (size_t)j * hd4 + d4)
+                                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    float4 xr[NV], gr[NV];
+    load_gain<NV>(gr, m.rms_att + (size_t)l * dim, c4, lane);
+    // RoPE factors of pos for the pair this thread rotates (tid < hd)
+    float2 rcs = make_float2(1.f, 0.f);
+    if (tid < hd) rcs = __ldg(m.rope + (size_t)pos * (hd / 2) + (tid % (hd / 2)));
+    const float *xsrc = a.xin ? a.xin : m.emb + (size_t)__ldcg(&m.step->tok) * dim;
+    if (!a.xin) load_act<NV>(xr, xsrc, c4, lane);
+    cluster.sync();   // every CTA of the cluster runs before any remote store
+    pdl_wait();
+    if (a.xin) load_act<NV>(xr, xsrc, c4, lane);
+    if (h == 0)
+        for (int i = tid; i < (o1 - o0) / 4; i += AT_THREADS)
+            reinterpret_cast<float4 *>(s_res)[i] = __ldcg(reinterpret_cast<const float4 *>(xsrc + o0) + i);
+    rmsnorm_pre<NV>(xr, gr, dim);
+
+    // 1. q/k/v rows -> every CTA's s_qkv
+    bool bad = !mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT);
+    for (int j = q0 + warp; j < q1; j += NW) {
+        const float v = smem_row_dot<NV>(stage + (size_t)(j - q0) * dim, xr, c4, lane);
+        if (lane < AC) cluster.map_shared_rank(s_qkv, lane)[j] = v;
+    }
+    cluster.sync();
+    // Every thread of this CTA has consumed the layer input (rmsnorm, the
+    // residual copy), so the CTA takes its ticket now; the result is only
+    // looked at when the CTA ends, where the last one clears the buffer.
+    unsigned ticket = 0u;
+    if (tid == AT_THREADS - 1) ticket = atomicAdd(&m.tickets[0], 1u);
+    // The staging rows are consumed: the wo slice (rows [o0, o1), the hd
+    // columns of head h) takes their place, 16 bytes per thread and copy.
+    {
+        const float *wo_base = m.wo + (size_t)l * dim * dim + (size_t)h * hd;
+        for (int f = tid; f < (o1 - o0) * hd4; f += AT_THREADS) {
+            const int row = f / hd4, c = f - row * hd4;
+            cp_async16(stage + (size_t)row * hd + 4 * c, wo_base + (size_t)(o0 + row) * dim + 4 * c);
+        }
+        cp_async_commit();
+    }
+    // 2. RoPE (llama2.c:238-245) in place on q and k
+    if (tid < hd) {
+        const int is_k = tid >= hd / 2;
+        const int i = 2 * (tid - (is_k ? hd / 2 : 0));
+        float *v = s_qkv + (is_k ? hd : 0) + i;
+        const float cs = rcs.x, sn = rcs.y;
+        const float a0 = v[0], a1 = v[1];
+        v[0] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+        v[1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+    }
+    __syncthreads();
+    if (r == 0 && pos_ok && tid < 2 * hd) {
+        const int d = tid % hd;
+        float *dst = (tid < hd ? m.kc : m.vc) + (head_base + pos) * hd + d;
+        *dst = s_qkv[(tid < hd ? hd : 2 * hd) + d];
+    }
+
+    // 3. attention over [t0, t1): online softmax in rounds of AT_ROUND
+    const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
+    float4 qv[QK];
+#pragma unroll
+    for (int i = 0; i < QK; i++) {
+        const int cc = sub + 4 * i;
+        qv[i] = (cc < hd4) ? reinterpret_cast<const float4 *>(s_qkv)[cc] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float *s_o = stage + (size_t)(dim / AC) * hd;   // value sums [ngrp][hd], after the wo slice
+    float m_run = -3.4028235e+38f, l_run = 0.f, o_run = 0.f;   // o_run: element tid of the output (tid < hd)
+    for (int rt0 = t0; rt0 < t1; rt0 += AT_ROUND) {
+        const int n = min(AT_ROUND, t1 - rt0);
+        if (rt0 != t0) {   // later rounds: load after the wait (L2 was warmed)
+            const float4 *kb = reinterpret_cast<const float4 *>(m.kc + (head_base + rt0) * hd);
+            const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + rt0) * hd);
+#pragma unroll
+            for (int i = 0; i < QK; i++) {
+                const int cc = sub + 4 * i;
+                kv[i] = (cc < hd4 && js < n && rt0 + js != pos) ? __ldcg(kb + (size_t)js * hd4 + cc)
+                                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < VP; k++) {
+                const int j = grp + ngrp * k;
+                vpre[k] = (grp < ngrp && j < n && rt0 + j != pos) ? __ldcg(vb + (size_t)j * hd4 + d4)
+                                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        // the current position's row is this kernel's own (post-RoPE) k and v
+        if (js < n && rt0 + js == pos) {
+#pragma unroll
+            for (int i = 0; i < QK; i++) {
+                const int cc = sub + 4 * i;
+                if (cc < hd4) kv[i] = reinterpret_cast<const float4 *>(s_qkv + hd)[cc];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < VP; k++) {
+            const int j = grp + ngrp * k;
+            if (grp < ngrp && j < n && rt0 + j == pos) vpre[k] = reinterpret_cast<const float4 *>(s_qkv + 2 * hd)[d4];
+        }
+        {
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < QK; i++) acc = dot4(kv[i], qv[i], acc);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            if (js < n && sub == 0) s_sc[js] = __fmul_rn(acc, scale);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            float mx = -3.4028235e+38f;
+            for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_sc[j]);
+            mx = warp_max(mx);
+            const float m_new = fmaxf(m_run, mx);
+            float sum = 0.f;
+            for (int j = lane; j < n; j += 32) {
+                const float e = pt_expf(__fsub_rn(s_sc[j], m_new));
+                s_sc[j] = e;
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                const float alpha = pt_expf(__fsub_rn(m_run, m_new));
+                s_stat[0] = m_new;
+                s_stat[1] = alpha;
+                l_run = fmaf(l_run, alpha, sum);
+            }
+        }
+        __syncthreads();
+        if (grp < ngrp) {
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < VP; k++) {
+                const int j = grp + ngrp * k;
+                if (j < n) {
+                    const float e = s_sc[j];
+                    o.x = fmaf(e, vpre[k].x, o.x); o.y = fmaf(e, vpre[k].y, o.y);
+                    o.z = fmaf(e, vpre[k].z, o.z); o.w = fmaf(e, vpre[k].w, o.w);
+                }
+            }
+            reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
+        }
+        __syncthreads();
+        m_run = s_stat[0];
+        if (tid < hd) {
+            float o = 0.f;
+            for (int g = 0; g < ngrp; g++) o += s_o[g * hd + tid];
+            o_run = fmaf(o_run, s_stat[1], o);
+        }
+        __syncthreads();   // s_sc, s_o, s_stat reused by the next round
+    }
+    // partial of this CTA -> slot r of every CTA
+    if (tid < hd)
+        for (int k = 0; k < AC; k++) cluster.map_shared_rank(&s_part[0][0], k)[r * (AT_MAX_HD + 4) + tid] = o_run;
+    if (tid == 0)
+        for (int k = 0; k < AC; k++) {
+            float *p = cluster.map_shared_rank(&s_part[0][0], k) + r * (AT_MAX_HD + 4);
+            p[AT_MAX_HD] = m_run;
+            p[AT_MAX_HD + 1] = l_run;
+        }
+    cluster.sync();
+
+    // 4. merge the AC partials (every output thread, same order in every
+    // CTA), then wo
+    if (tid < hd) {
+        float M = -3.4028235e+38f;
+        for (int k = 0; k < AC; k++) M = fmaxf(M, s_part[k][AT_MAX_HD]);
+        float L = 0.f, o = 0.f;
+        for (int k = 0; k < AC; k++) {
+            const float w = pt_expf(__fsub_rn(s_part[k][AT_MAX_HD], M));
+            L = fmaf(w, s_part[k][AT_MAX_HD + 1], L);
+            o = fmaf(w, s_part[k][tid], o);
+        }
+        s_att[tid] = o * __fdiv_rn(1.0f, L);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // wo rows in quads: lane 8e + k reduces row 4qd + e over float4 columns
+    // k, k + 8, ...; lane 0 gathers the quad and adds it at L2.
+    const int e8 = lane >> 3, k8 = lane & 7;
+    const float4 *att4 = reinterpret_cast<const float4 *>(s_att);
+    for (int qd = warp; qd < (o1 - o0) / 4; qd += NW) {
+        const float4 *w4 = reinterpret_cast<const float4 *>(stage + (size_t)(4 * qd + e8) * hd);
+        float acc = 0.f;
+        for (int c = k8; c < hd4; c += 8) acc = dot4(w4[c], att4[c], acc);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+        const float y1 = __shfl_sync(0xffffffffu, acc, 8);
+        const float y2 = __shfl_sync(0xffffffffu, acc, 16);
+        const float y3 = __shfl_sync(0xffffffffu, acc, 24);
+        if (lane == 0) {
+            float4 out = make_float4(acc, y1, y2, y3);
+            if (h == 0) {
+                const float4 rr = reinterpret_cast<const float4 *>(s_res)[qd];
+                out.x = __fadd_rn(rr.x, out.x); out.y = __fadd_rn(rr.y, out.y);
+                out.z = __fadd_rn(rr.z, out.z); out.w = __fadd_rn(rr.w, out.w);
+            }
+            red_add_v4(a.xout + o0 + 4 * qd, out);
+        }
+    }
+    if (tid == AT_THREADS - 1) s_last = (ticket == gridDim.x - 1);
+    __syncthreads();
+    if (s_last) {
+        for (int i = tid; i < c4; i += AT_THREADS)
+            reinterpret_cast<float4 *>(a.xclear)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tid == 0) m.tickets[0] = 0u;
+    }
+    if (bad && tid == 0) mbar_wait_bounded(&bars[0], 0u, nullptr, 0);   // let the copy land before exiting
 }
 
 // Host-side launchers --------------------------------------------------------
@@ -741,6 +1081,27 @@ static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     PTC_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
+// The same, for a kernel launched in clusters of `cluster` CTAs.
+template <typename... KArgs, typename... Args>
+static void launch_cluster_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster,
+                               cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_on() ? 2 : 1;
+    PTC_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 __global__ void k_embed(DecodeModel m);
 
 template <int NV, int MODE>
@@ -792,6 +1153,36 @@ static void launch_ffn(const DecodeModel &m, FfnArgs a, int n_sm, cudaStream_t s
     launch_pdl(k_ffn<NV>, dim3(grid), dim3(FF_THREADS), smem, s, m, a);
 }
 
+template <int NV>
+static void launch_attn_fused(const DecodeModel &m, AttnArgs a, cudaStream_t s) {
+    const size_t smem = (size_t)MV_BAR_BYTES + (size_t)m.attn_stage * 4;
+    static size_t configured = 0;  // per instantiation: largest size set so far
+    if (smem > configured) {
+        PTC_CHECK(cudaFuncSetAttribute(k_attn_fused<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        PTC_CHECK(cudaFuncSetAttribute(k_attn_fused<NV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        configured = smem;
+    }
+    a.stage_floats = m.attn_stage;
+    launch_cluster_pdl(k_attn_fused<NV>, dim3(m.nh * AC), dim3(AT_THREADS), smem, AC, s, m, a);
+}
+
+// Staging floats of k_attn_fused for this model, or 0 when the fused
+// attention does not apply: one K/V head per query head, head_dim <= 64 and
+// a multiple of 4, dim a multiple of 4 * AC (whole wo row quads per CTA).
+int decode_attn_stage(int dim, int nh, int nkv, int seq) {
+    if (nh != nkv || dim % nh) return 0;
+    const int hd = dim / nh;
+    if (hd > AT_MAX_HD || hd % 4 || dim % (4 * AC) || dim / AC > AT_MAX_OUT || dim > 2048) return 0;
+    (void)seq;   // positions are processed in rounds: no limit from seq_len
+    const int qkv_rows = (3 * hd + AC - 1) / AC;
+    const int ngrp = AT_THREADS / (hd / 4);
+    const int stage_a = qkv_rows * dim;                  // q/k/v rows
+    const int stage_b = (dim / AC) * hd + ngrp * hd;      // wo slice + value sums
+    const int stage = stage_a > stage_b ? stage_a : stage_b;
+    if ((size_t)stage * 4 > 160 * 1024) return 0;
+    return stage;
+}
+
 // Hidden units per k_ffn CTA for this model and grid, or 0 when the fused
 // FFN does not fit (rows in shared memory, output columns per thread).
 int decode_ffn_rows(int dim, int hidden, int n_sm) {
@@ -809,6 +1200,24 @@ int decode_ffn_rows(int dim, int hidden, int n_sm) {
 static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float *x_in, float *x_out, int n_sm,
                          cudaStream_t s) {
     const int nvd = nv_of(m.dim), nvh = nv_of(m.hidden);
+    if (m.fused_attn) {
+        // two kernels: attention block -> xm, FFN block -> x_out; each clears
+        // the input it consumed once all its CTAs have read it
+        AttnArgs at;
+        memset(&at, 0, sizeof(at));
+        at.xin = from_embedding ? nullptr : x_in;
+        at.xout = m.xm;
+        at.xclear = x_in;
+        at.l = l;
+        PTC_NV_SWITCH(nvd, (launch_attn_fused<NV>(m, at, s)));
+        FfnArgs f;
+        f.xin = m.xm;
+        f.xout = x_out;
+        f.xclear = m.xm;
+        f.l = l;
+        PTC_NV_SWITCH(nvd, (launch_ffn<NV>(m, f, n_sm, s)));
+        return;
+    }
     MvArgs a = mv_args((m.dim + 2 * m.kvd) / 2, m.dim, 2, l);
     a.from_embedding = from_embedding ? 1 : 0;
     a.in = x_in;
@@ -831,6 +1240,7 @@ static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float
         FfnArgs f;
         f.xin = m.xm;
         f.xout = x_out;
+        f.xclear = nullptr;   // wo overwrites xm whole
         f.l = l;
         PTC_NV_SWITCH(nvd, (launch_ffn<NV>(m, f, n_sm, s)));
         return;
@@ -883,6 +1293,23 @@ __global__ void k_embed(DecodeModel m) {
 
 void launch_embed(const DecodeModel &m, cudaStream_t s) {
     launch_pdl(k_embed, dim3((m.dim + 255) / 256), dim3(256), 0, s, m);
+}
+
+// RoPE factors (cos, sin) of every (position, pair) with pitorch's angle and
+// trigonometry (pt_ops.c:33-49), computed once per decoder.
+__global__ void k_rope_table(float2 *t, int seq, int hd) {
+    const int half = hd / 2;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < seq * half; i += gridDim.x * blockDim.x) {
+        const int p = i / half, j = 2 * (i % half);
+        const float th = rope_theta(j, hd, p);
+        t[i] = make_float2(pt_cosf(th), pt_sinf(th));
+    }
+}
+
+void build_rope_table(float2 *t, int seq, int hd, cudaStream_t s) {
+    const int n = seq * (hd / 2);
+    k_rope_table<<<(n + 255) / 256, 256, 0, s>>>(t, seq, hd);
+    PTC_CHECK(cudaGetLastError());
 }
 
 int decode_attn_limits_ok(int hd, int chunk, int n_chunks) {

@@ -141,9 +141,22 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     cudaStream_t s = d->stream;
     // Fused FFN (default where it fits; PTC_DECODE_FUSED=0 selects the
     // five-kernel layer): needs the transposed w2 and the hand-over buffers.
+    // PTC_DECODE_FUSED=0: five kernels per layer; =ffn: fused FFN only;
+    // default: fused attention block + fused FFN (two kernels per layer).
     const char *want_fused = getenv("PTC_DECODE_FUSED");
+    const bool no_fuse = want_fused && want_fused[0] == '0';
+    const bool ffn_only = want_fused && strcmp(want_fused, "ffn") == 0;
     m.ffn_rows = ptc::decode_ffn_rows(m.dim, m.hidden, d->n_sm);
-    m.fused_ffn = m.L > 0 && m.ffn_rows > 0 && !(want_fused && want_fused[0] == '0');
+    m.fused_ffn = m.L > 0 && m.ffn_rows > 0 && !no_fuse;
+    m.attn_stage = ptc::decode_attn_stage(m.dim, m.nh, m.nkv, m.seq);
+    m.fused_attn = m.fused_ffn && m.attn_stage > 0 && !ffn_only;
+    m.tickets = (unsigned *)ptc_alloc(c, 64);
+    PTC_CHECK(cudaMemsetAsync(m.tickets, 0, 64, s));
+    if (m.fused_attn) {
+        float2 *rope = (float2 *)ptc_alloc(c, (size_t)m.seq * (m.hd / 2) * sizeof(float2));
+        ptc::build_rope_table(rope, m.seq, m.hd, s);
+        m.rope = rope;
+    }
     if (m.fused_ffn || (m.L > 0 && ptc::persist_supported(m, d->n_sm))) {
         float *w2t = (float *)ptc_alloc(c, (size_t)m.L * m.hidden * m.dim * 4);
         ptc::persist_transpose_w2(m, w2t, s);

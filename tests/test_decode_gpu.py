@@ -135,13 +135,13 @@ def test_persistent_kernel_path_matches_reference(ptlib, monkeypatch):
     ctx.close()
 
 
-def test_unfused_layer_path_matches_reference(ptlib, monkeypatch):
-    """PTC_DECODE_FUSED=0 selects the five-kernel layer (separate w1/w3 and
-    w2 matvecs); it gives the same stream as the default fused FFN."""
-    monkeypatch.setenv("PTC_DECODE_FUSED", "0")
-    ctx = api.Context(synth.make_blob("stories15M"))
-    check_stream(ctx, "stories15M")
-    ctx.close()
-    ctx = api.Context(synth.make_blob("tiny"))
-    check_stream(ctx, "tiny")
-    ctx.close()
+@pytest.mark.parametrize("mode", ["0", "ffn"])
+def test_unfused_layer_paths_match_reference(ptlib, monkeypatch, mode):
+    """PTC_DECODE_FUSED=0 selects the five-kernel layer, =ffn the fused FFN
+    with separate q/k/v, attention and wo kernels; both give the reference's
+    stream, as the default two-kernel layer does."""
+    monkeypatch.setenv("PTC_DECODE_FUSED", mode)
+    for name in ("stories15M", "tiny"):
+        ctx = api.Context(synth.make_blob(name))
+        check_stream(ctx, name)
+        ctx.close()
