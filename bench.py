@@ -264,6 +264,103 @@ def run_single(args):
     return 0
 
 
+SWEEP_SHAPES = [(288, 288), (768, 288), (288, 768), (512, 512), (1376, 512), (2048, 768), (768, 2048),
+                (32000, 288), (32000, 768)]
+L2_BYTES = 126 * 1024 * 1024
+
+
+def run_sweep(args):
+    """The isolated fp32 matvec sweep y = W.x (W rows x cols, W ~ N(0,0.02),
+    x ~ N(0,1), seeded) through the C ABI's ptc_matvec. Per shape, one JSON
+    line:
+      cold  back-to-back calls, each on a different copy of W, the copies
+            together >= 2x L2 so every call streams W from HBM; the calls are
+            one CUDA graph, timed with CUDA events (launches overlap through
+            programmatic dependent launch, as in a decode step);
+      hot   the same, always the same W (L2-resident when it fits);
+      cpu_baseline  the reference's own smatvec_cpu (oracle/_ref), 1 thread.
+    Algorithmic bytes per call: 4*(rows*cols + rows + cols)."""
+    import ctypes as C
+    import oracle
+    import pitorch_b200
+    from pitorch_b200 import api
+    L = pitorch_b200.lib()
+    pc = L.ptc_create(0, 0)
+    stream = L.ptc_stream(pc)
+    timer = L.ptc_timer_create(pc)
+    hbm, src = peaks()
+    shapes = SWEEP_SHAPES
+    if args.sweep_shapes:
+        shapes = [tuple(int(v) for v in s.split("x")) for s in args.sweep_shapes.split(",")]
+    impl = "reference" if oracle.ref_available() else "port"
+    for rows, cols in shapes:
+        rng = np.random.default_rng(1000 + rows + cols)
+        W = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+        x = rng.standard_normal(cols).astype(np.float32)
+        wbytes = W.nbytes
+        n_copies = max(2, -(-2 * L2_BYTES // wbytes))
+        dW = L.ptc_alloc(pc, wbytes * n_copies)
+        dx = L.ptc_alloc(pc, cols * 4)
+        dy = L.ptc_alloc(pc, rows * 4)
+        L.ptc_h2d(pc, dW, W.ctypes.data, wbytes)
+        for k in range(1, n_copies):
+            L.ptc_d2d(pc, dW + k * wbytes, dW, wbytes)
+        L.ptc_h2d(pc, dx, x.ctypes.data, cols * 4)
+        L.ptc_sync(pc)
+        # parity against the oracle (smatvec_cpu order), tolerance 1e-5
+        L.ptc_matvec(dW, dx, dy, rows, cols, stream)
+        y = np.zeros(rows, np.float32)
+        L.ptc_d2h(pc, y.ctypes.data, dy, rows * 4)
+        ref = oracle.matvec(W, x)
+        err = float(np.abs(y - ref).max() / np.abs(ref).max())
+        bytes_call = 4 * (rows * cols + rows + cols)
+        res = {}
+        for mode in ("cold", "hot"):
+            n_calls = n_copies if mode == "cold" else max(64, n_copies)
+            while n_calls * bytes_call < 1.5e9 and n_calls < 4096:   # >= ~0.25 ms of work per replay
+                n_calls *= 2
+            L.ptc_capture_begin(pc)
+            for i in range(n_calls):
+                Wi = dW + (i % n_copies) * wbytes if mode == "cold" else dW
+                L.ptc_matvec(Wi, dx, dy, rows, cols, stream)
+            g = L.ptc_capture_end(pc)
+            for _ in range(max(3, args.warmup)):
+                L.ptc_graph_launch(g)
+            L.ptc_sync(pc)
+            reps = max(3, args.steps)
+            L.ptc_timer_start(timer)
+            for _ in range(reps):
+                L.ptc_graph_launch(g)
+            L.ptc_timer_stop(timer)
+            ms = L.ptc_timer_ms(timer)
+            L.ptc_graph_destroy(g)
+            us_call = 1000 * ms / (reps * n_calls)
+            gbs = bytes_call / (us_call * 1e-6) / 1e9
+            res[mode] = {"GB/s": gbs, "us_per_call": us_call, "calls_per_graph": n_calls,
+                         "frac_of_hbm": gbs / hbm}
+        # CPU: the reference's smatvec_cpu on a bounded sample
+        n_cpu, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 0.3 or n_cpu < 2:
+            oracle.matvec(W, x, impl=impl)
+            n_cpu += 1
+        cpu_us = 1e6 * (time.perf_counter() - t0) / n_cpu
+        line = {
+            "metric": "fp32 matvec GB/s", "shape": f"{rows}x{cols}", "unit": "GB/s", "n_gpus": 1,
+            "value": res["cold"]["GB/s"], "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+            "bytes_per_call": bytes_call, "cold": res["cold"], "hot": res["hot"],
+            "cold_copies": n_copies, "l2_policy": f"cold: {n_copies} copies of W = "
+                                                  f"{n_copies * wbytes / 2**20:.0f} MiB >= 2x L2",
+            "peak": hbm, "peak_source": f"{src} hbm_gbs", "parity_rel_err": err,
+            "cpu_baseline": {"value": bytes_call / (cpu_us * 1e-6) / 1e9, "unit": "GB/s", "cores": 1,
+                             "kind": impl, "us_per_call": cpu_us,
+                             "sample": f"{n_cpu} calls of smatvec_cpu on the same W, x"},
+        }
+        print(json.dumps(line), flush=True)
+    L.ptc_timer_destroy(timer)
+    L.ptc_destroy(pc)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -273,7 +370,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--positions", type=int, default=0,
                     help="decode positions per step (default: the model's seq_len, 1024)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="isolated fp32 matvec sweep (one JSON line per W shape) instead of the decode")
+    ap.add_argument("--sweep-shapes", default="", help="e.g. 32000x768,2048x768 (default: the 9 shapes)")
     args = ap.parse_args()
+    if args.sweep:
+        return run_sweep(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":

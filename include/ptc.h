@@ -258,6 +258,17 @@ void ptc_timer_stop(ptc_timer *t);
 float ptc_timer_ms(ptc_timer *t);     /* synchronises on the stop event */
 void ptc_timer_destroy(ptc_timer *t);
 
+/* ---- CUDA graphs of work enqueued on a context's stream ------------------
+ * No reference counterpart (the Pi runtime has no command graphs). Between
+ * ptc_capture_begin and ptc_capture_end, calls that enqueue on the context's
+ * stream (ptc_matvec with ptc_stream(c), the decoder's enqueue calls) are
+ * recorded instead of run; ptc_graph_launch replays them with one launch. */
+typedef struct ptc_graph ptc_graph;
+void ptc_capture_begin(ptc_ctx *c);
+ptc_graph *ptc_capture_end(ptc_ctx *c);
+void ptc_graph_launch(ptc_graph *g);
+void ptc_graph_destroy(ptc_graph *g);
+
 #ifdef __cplusplus
 }
 #endif

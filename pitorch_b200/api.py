@@ -208,6 +208,11 @@ def declare(L):
     _sig(L, "ptc_timer_stop", None, vp)
     _sig(L, "ptc_timer_ms", C.c_float, vp)
     _sig(L, "ptc_timer_destroy", None, vp)
+    _sig(L, "ptc_capture_begin", None, vp)
+    _sig(L, "ptc_capture_end", vp, vp)
+    _sig(L, "ptc_graph_launch", None, vp)
+    _sig(L, "ptc_graph_destroy", None, vp)
+    _sig(L, "ptc_d2d", None, vp, vp, vp, C.c_size_t)
     return declare_text(L)
 
 

@@ -25,19 +25,17 @@ namespace ptc {
 template <int NV, int R>
 __global__ void __launch_bounds__(256) k_matvec(const float *__restrict__ W, const float *__restrict__ x,
                                                 float *__restrict__ y, int rows, int cols) {
+    // Programmatic dependent launch: W never comes from the previous kernel
+    // of the stream, so the first rows are requested before
+    // griddepcontrol.wait and consecutive matvecs overlap; x (possibly the
+    // previous kernel's output) is read after it.
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
     const int c4 = cols >> 2;
-    float4 xr[NV];
-    const float4 *x4 = reinterpret_cast<const float4 *>(x);
-#pragma unroll
-    for (int v = 0; v < NV; v++) {
-        int c = lane + 32 * v;
-        xr[v] = (c < c4) ? __ldg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    for (int r0 = gw * R; r0 < rows; r0 += nw * R) {
-        float4 w[R][NV];
+    float4 w[R][NV];
+    auto load_rows = [&](int r0) {
 #pragma unroll
         for (int k = 0; k < R; k++) {
             const float4 *row = reinterpret_cast<const float4 *>(W + (size_t)(r0 + k) * cols);
@@ -47,6 +45,19 @@ __global__ void __launch_bounds__(256) k_matvec(const float *__restrict__ W, con
                 w[k][v] = (r0 + k < rows && c < c4) ? ldg_stream(row + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
+    };
+    int r0 = gw * R;
+    if (r0 < rows) load_rows(r0);
+    pdl_wait();
+    float4 xr[NV];
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        int c = lane + 32 * v;
+        xr[v] = (c < c4) ? __ldcg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (; r0 < rows; r0 += nw * R) {
+        if (r0 != gw * R) load_rows(r0);
 #pragma unroll
         for (int k = 0; k < R; k++) {
             float acc = 0.f;
@@ -81,12 +92,27 @@ __global__ void __launch_bounds__(256) k_matvec_any(const float *__restrict__ W,
     if (r < rows && lane == 0) y[r] = acc;
 }
 
+template <int NV, int R>
+static void launch_k_matvec(int grid, const float *W, const float *x, float *y, int rows, int cols,
+                            cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PTC_CHECK(cudaLaunchKernelEx(&cfg, k_matvec<NV, R>, W, x, y, rows, cols));
+}
+
 #define MV_CASE(NVV)                                                                        \
     case NVV:                                                                               \
         if (rows >= 4096)                                                                   \
-            k_matvec<NVV, 2><<<grid2, 256, 0, s>>>(W, x, y, rows, cols);                    \
+            launch_k_matvec<NVV, 2>(grid2, W, x, y, rows, cols, s);                         \
         else                                                                                \
-            k_matvec<NVV, 1><<<grid1, 256, 0, s>>>(W, x, y, rows, cols);                    \
+            launch_k_matvec<NVV, 1>(grid1, W, x, y, rows, cols, s);                         \
         break;
 
 void launch_matvec(const float *W, const float *x, float *y, int rows, int cols, cudaStream_t s) {

@@ -226,6 +226,34 @@ extern "C" void ptc_timer_destroy(ptc_timer *t) {
     delete t;
 }
 
+// ---------------------------------------------------------------------------
+// Graphs of stream work
+// ---------------------------------------------------------------------------
+struct ptc_graph {
+    ptc_ctx *c;
+    cudaGraphExec_t exec;
+};
+
+extern "C" void ptc_capture_begin(ptc_ctx *c) {
+    PTC_CHECK(cudaSetDevice(c->device));
+    PTC_CHECK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+}
+extern "C" ptc_graph *ptc_capture_end(ptc_ctx *c) {
+    cudaGraph_t g;
+    PTC_CHECK(cudaStreamEndCapture(c->stream, &g));
+    ptc_graph *pg = new ptc_graph();
+    pg->c = c;
+    PTC_CHECK(cudaGraphInstantiate(&pg->exec, g, 0));
+    PTC_CHECK(cudaGraphDestroy(g));
+    return pg;
+}
+extern "C" void ptc_graph_launch(ptc_graph *g) { PTC_CHECK(cudaGraphLaunch(g->exec, g->c->stream)); }
+extern "C" void ptc_graph_destroy(ptc_graph *g) {
+    if (!g) return;
+    cudaGraphExecDestroy(g->exec);
+    delete g;
+}
+
 cudaStream_t ptc_ctx_stream(ptc_ctx *c) { return c->stream; }
 int ptc_ctx_device(ptc_ctx *c) { return c->device; }
 
