@@ -361,6 +361,69 @@ def run_sweep(args):
     return 0
 
 
+def train_flops(cfg, T):
+    """Algorithmic FLOPs of one pt_train_step: forward 2*T*P_lin, backward dX
+    and dW 2*(T-1)*P_lin each (P_lin = the linear layers' parameters: per
+    layer 2*dim^2 + 2*kvd*dim + 3*hidden*dim, plus the V*dim classifier), plus
+    attention forward and backward (~4x the forward score/value products)."""
+    dim, hidden, L, nh, nkv, V, seq = cfg
+    kvd = nkv * (dim // nh)
+    p_lin = L * (2 * dim * dim + 2 * kvd * dim + 3 * hidden * dim) + V * dim
+    attn_fwd = L * 2 * 2 * dim * T * (T + 1) / 2     # q.k and p.v over the causal triangle
+    return 2 * T * p_lin + 2 * 2 * (T - 1) * p_lin + attn_fwd * 3
+
+
+def run_train(args):
+    """Training throughput: pt_train_step on the stories15M shape, T = 256
+    seeded tokens, lr 1e-3 (the BASELINE training config), timed with CUDA
+    events around K whole steps (each returns its loss to the host)."""
+    import oracle
+    import pitorch_b200
+    from pitorch_b200 import api
+    L = pitorch_b200.lib()
+    model, T, lr = "stories15M", 256, 1e-3
+    cfg = synth.CONFIGS[model]
+    blob = synth.make_blob(cfg)
+    tokens = synth.make_tokens(cfg[5], T)
+    ctx = api.Context(blob, max_T=T)
+    pc = ctx.ptc_ctx()
+    timer = L.ptc_timer_create(pc)
+    losses = []
+    for _ in range(args.warmup):
+        losses.append(ctx.train_step(tokens, lr))
+    L.ptc_sync(pc)
+    with ClockSampler(0) as clk:
+        L.ptc_timer_start(timer)
+        for _ in range(args.steps):
+            losses.append(ctx.train_step(tokens, lr))
+        L.ptc_timer_stop(timer)
+        ms = L.ptc_timer_ms(timer) / args.steps
+    L.ptc_timer_destroy(timer)
+    ctx.close()
+    flops = train_flops(cfg, T)
+    line = {
+        "metric": "stories15M train step tokens/s (T=256)", "value": T / (ms / 1000.0), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02) weights, seeded uniform tokens)",
+        "config": {"workload": "pt_train_step: forward, cross-entropy, backward, SGD", "model": model,
+                   "global_batch": 1, "seq_len": T, "lr": lr, "parallelism": "none"},
+        "achieved_gflops": flops / (ms / 1000.0) / 1e9, "flops_per_step": flops,
+        "losses_first": losses[:3], "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        impl = "reference" if oracle.ref_available() else "port"
+        m = oracle.Model(blob, max_T=T, impl=impl)
+        t0 = time.perf_counter()
+        ref_loss = m.train_step(tokens, lr)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": T / dt, "unit": "tokens/s", "cores": 1, "kind": impl,
+                                "s_per_step": dt, "sample": "one pt_train_step at T=256 on the same weights"}
+        line["loss_rel_err_step0"] = abs(losses[0] - ref_loss) / abs(ref_loss) if args.warmup else None
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -373,9 +436,12 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="isolated fp32 matvec sweep (one JSON line per W shape) instead of the decode")
     ap.add_argument("--sweep-shapes", default="", help="e.g. 32000x768,2048x768 (default: the 9 shapes)")
+    ap.add_argument("--train", action="store_true", help="stories15M training step (T=256) instead of the decode")
     args = ap.parse_args()
     if args.sweep:
         return run_sweep(args)
+    if args.train and args.impl != "reference" and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        return run_train(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":

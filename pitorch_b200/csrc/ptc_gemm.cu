@@ -25,6 +25,54 @@
 
 namespace ptc {
 
+// Store a thread's TM x TN block (rows mb.., columns nb..) with the
+// product's epilogue, or into the split-K partial buffer.
+template <int TM, int TN>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs &g, const float (&acc)[TM][TN], int mb, int nb,
+                                              int split) {
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        const int m = mb + i;
+        if (m >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const int n = nb + j;
+            if (n >= g.N) continue;
+            const float v = acc[i][j];
+            if (g.splits > 1) {
+                g.partial[((size_t)split * g.M + m) * g.N + n] = v;
+                continue;
+            }
+            float *c = g.C + (size_t)m * g.ldc + n;
+            switch (g.epi) {
+                case EPI_STORE: *c = v; break;
+                case EPI_ACCUM: *c = *c + v; break;
+                case EPI_RESID: *c = __fadd_rn(g.R[(size_t)m * g.ldr + n], v); break;
+            }
+        }
+    }
+    // RoPE epilogue (q/k projections): pairs (n, n+1) are held by the same
+    // thread since TN is even and tiles start at even n.
+    if (g.epi == EPI_ROPE && g.splits == 1) {
+#pragma unroll
+        for (int i = 0; i < TM; i++) {
+            const int m = mb + i;
+            if (m >= g.M) continue;
+#pragma unroll
+            for (int j = 0; j < TN; j += 2) {
+                const int n = nb + j;
+                if (n + 1 >= g.N) continue;
+                const float th = rope_theta(n, g.rope_hd, m);
+                const float cs = pt_cosf(th), sn = pt_sinf(th);
+                const float a0 = acc[i][j], a1 = acc[i][j + 1];
+                float *c = g.C + (size_t)m * g.ldc + n;
+                c[0] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+                c[1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+            }
+        }
+    }
+}
+
 template <int BM, int BN, int BK, int TM, int TN, bool A_KC, bool B_KC>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     k_gemm(GemmArgs g) {
@@ -108,53 +156,150 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
         buf ^= 1;
     }
 
-    // Epilogue
-#pragma unroll
-    for (int i = 0; i < TM; i++) {
-        const int m = m0 + ty * TM + i;
-        if (m >= g.M) continue;
-#pragma unroll
-        for (int j = 0; j < TN; j++) {
-            const int n = n0 + tx * TN + j;
-            if (n >= g.N) continue;
-            const float v = acc[i][j];
-            if (g.splits > 1) {
-                g.partial[((size_t)split * g.M + m) * g.N + n] = v;
-                continue;
-            }
-            float *c = g.C + (size_t)m * g.ldc + n;
-            switch (g.epi) {
-                case EPI_STORE: *c = v; break;
-                case EPI_ACCUM: *c = *c + v; break;
-                case EPI_RESID: *c = __fadd_rn(g.R[(size_t)m * g.ldr + n], v); break;
-            }
-        }
-    }
-    // RoPE epilogue (q/k projections): pairs (n, n+1) are held by the same
-    // thread since TN is even and tiles start at even n.
-    if (g.epi == EPI_ROPE && g.splits == 1) {
-#pragma unroll
-        for (int i = 0; i < TM; i++) {
-            const int m = m0 + ty * TM + i;
-            if (m >= g.M) continue;
-#pragma unroll
-            for (int j = 0; j < TN; j += 2) {
-                const int n = n0 + tx * TN + j;
-                if (n + 1 >= g.N) continue;
-                const float th = rope_theta(n, g.rope_hd, m);
-                const float cs = pt_cosf(th), sn = pt_sinf(th);
-                const float a0 = acc[i][j], a1 = acc[i][j + 1];
-                float *c = g.C + (size_t)m * g.ldc + n;
-                c[0] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
-                c[1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
-            }
-        }
-    }
+    gemm_epilogue<TM, TN>(g, acc, m0 + ty * TM, n0 + tx * TN, split);
 }
 
-// Fixed-order reduction of split-K partials into C with the epilogue.
+// Vectorised variant for operands whose contiguous dimension and leading
+// dimensions are multiples of 4 floats (every product of the training step):
+// 128-bit global loads along the contiguous dimension, staged through
+// registers into the next shared-memory buffer while the current one is
+// used; 128-bit shared reads of the TM x TN operand fragments. K is split
+// into chunks of kper (a multiple of BK) by blockIdx.z.
+template <int BM, int BN, int BK, int TM, int TN, bool A_KC, bool B_KC>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_gemm_v(GemmArgs g, int kper) {
+    constexpr int NT = (BM / TM) * (BN / TN);
+    constexpr int A4 = BM * BK / 4 / NT, B4 = BN * BK / 4 / NT;
+    static_assert(A4 >= 1 && B4 >= 1 && A4 * 4 * NT == BM * BK && B4 * 4 * NT == BN * BK, "tile / threads");
+    __shared__ __align__(16) float As[2][BK][BM + 4];
+    __shared__ __align__(16) float Bs[2][BK][BN + 4];
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int split = blockIdx.z;
+    const int kbeg = split * kper, kend = min(g.K, kbeg + kper);
+    const int tx = tid % (BN / TN), ty = tid / (BN / TN);
+    float4 ra[A4], rb[B4];
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    auto gload = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < A4; i++) {
+            const int e = tid + i * NT;
+            if (A_KC) {   // BM rows of BK/4 float4 along k
+                const int r = e / (BK / 4), c = e % (BK / 4), m = m0 + r, k = k0 + 4 * c;
+                ra[i] = (m < g.M && k < kend) ? __ldg(reinterpret_cast<const float4 *>(g.A + (size_t)m * g.lda + k))
+                                              : zero;
+            } else {      // BK rows (k) of BM/4 float4 along m
+                const int r = e / (BM / 4), c = e % (BM / 4), k = k0 + r, m = m0 + 4 * c;
+                ra[i] = (k < kend && m < g.M) ? __ldg(reinterpret_cast<const float4 *>(g.A + (size_t)k * g.lda + m))
+                                              : zero;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < B4; i++) {
+            const int e = tid + i * NT;
+            if (B_KC) {
+                const int r = e / (BK / 4), c = e % (BK / 4), n = n0 + r, k = k0 + 4 * c;
+                rb[i] = (n < g.N && k < kend) ? __ldg(reinterpret_cast<const float4 *>(g.B + (size_t)n * g.ldb + k))
+                                              : zero;
+            } else {
+                const int r = e / (BN / 4), c = e % (BN / 4), k = k0 + r, n = n0 + 4 * c;
+                rb[i] = (k < kend && n < g.N) ? __ldg(reinterpret_cast<const float4 *>(g.B + (size_t)k * g.ldb + n))
+                                              : zero;
+            }
+        }
+    };
+    auto sstore = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < A4; i++) {
+            const int e = tid + i * NT;
+            if (A_KC) {
+                const int r = e / (BK / 4), c = e % (BK / 4);
+                As[buf][4 * c + 0][r] = ra[i].x;
+                As[buf][4 * c + 1][r] = ra[i].y;
+                As[buf][4 * c + 2][r] = ra[i].z;
+                As[buf][4 * c + 3][r] = ra[i].w;
+            } else {
+                const int r = e / (BM / 4), c = e % (BM / 4);
+                *reinterpret_cast<float4 *>(&As[buf][r][4 * c]) = ra[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < B4; i++) {
+            const int e = tid + i * NT;
+            if (B_KC) {
+                const int r = e / (BK / 4), c = e % (BK / 4);
+                Bs[buf][4 * c + 0][r] = rb[i].x;
+                Bs[buf][4 * c + 1][r] = rb[i].y;
+                Bs[buf][4 * c + 2][r] = rb[i].z;
+                Bs[buf][4 * c + 3][r] = rb[i].w;
+            } else {
+                const int r = e / (BN / 4), c = e % (BN / 4);
+                *reinterpret_cast<float4 *>(&Bs[buf][r][4 * c]) = rb[i];
+            }
+        }
+    };
+
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) acc[i][j] = 0.f;
+    if (kbeg < kend) {
+        gload(kbeg);
+        sstore(0);
+    }
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = kbeg; k0 < kend; k0 += BK) {
+        const bool more = k0 + BK < kend;
+        if (more) gload(k0 + BK);
+#pragma unroll
+        for (int kk = 0; kk < BK; kk++) {
+            float a[TM], b[TN];
+#pragma unroll
+            for (int q = 0; q < TM / 4; q++) {
+                const float4 v = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * TM + 4 * q]);
+                a[4 * q] = v.x; a[4 * q + 1] = v.y; a[4 * q + 2] = v.z; a[4 * q + 3] = v.w;
+            }
+#pragma unroll
+            for (int q = 0; q < TN / 4; q++) {
+                const float4 v = *reinterpret_cast<const float4 *>(&Bs[buf][kk][tx * TN + 4 * q]);
+                b[4 * q] = v.x; b[4 * q + 1] = v.y; b[4 * q + 2] = v.z; b[4 * q + 3] = v.w;
+            }
+#pragma unroll
+            for (int i = 0; i < TM; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        if (more) sstore(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+    }
+    gemm_epilogue<TM, TN>(g, acc, m0 + ty * TM, n0 + tx * TN, split);
+}
+
+// Fixed-order reduction of split-K partials into C with the epilogue
+// (RoPE rows rotate pairs (n, n+1), so that case walks pairs).
 __global__ void k_splitk_reduce(GemmArgs g) {
     const size_t total = (size_t)g.M * g.N;
+    if (g.epi == EPI_ROPE) {
+        // N is even (a head dimension multiple), so pairs never straddle rows
+        for (size_t e = 2 * (blockIdx.x * (size_t)blockDim.x + threadIdx.x); e < total;
+             e += 2 * (size_t)gridDim.x * blockDim.x) {
+            float v0 = 0.f, v1 = 0.f;
+            for (int s = 0; s < g.splits; s++) {
+                v0 += g.partial[(size_t)s * total + e];
+                v1 += g.partial[(size_t)s * total + e + 1];
+            }
+            const int m = (int)(e / g.N), n = (int)(e % g.N);
+            const float th = rope_theta(n, g.rope_hd, m);
+            const float cs = pt_cosf(th), sn = pt_sinf(th);
+            float *c = g.C + (size_t)m * g.ldc + n;
+            c[0] = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
+            c[1] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
+        }
+        return;
+    }
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total;
          e += (size_t)gridDim.x * blockDim.x) {
         float v = 0.f;
@@ -181,12 +326,61 @@ static void launch_tile(const GemmArgs &g, cudaStream_t s) {
     PTC_CHECK(cudaGetLastError());
 }
 
+template <int BM, int BN, int BK, int TM, int TN>
+static void launch_tile_v(const GemmArgs &g, int kper, cudaStream_t s) {
+    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
+    dim3 block((BM / TM) * (BN / TN));
+    if (g.a_kcontig && g.b_kcontig) k_gemm_v<BM, BN, BK, TM, TN, true, true><<<grid, block, 0, s>>>(g, kper);
+    else if (g.a_kcontig) k_gemm_v<BM, BN, BK, TM, TN, true, false><<<grid, block, 0, s>>>(g, kper);
+    else if (g.b_kcontig) k_gemm_v<BM, BN, BK, TM, TN, false, true><<<grid, block, 0, s>>>(g, kper);
+    else k_gemm_v<BM, BN, BK, TM, TN, false, false><<<grid, block, 0, s>>>(g, kper);
+    PTC_CHECK(cudaGetLastError());
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+// The vectorised kernel reads float4s along each operand's contiguous
+// dimension: that dimension (K for a k-contiguous operand, else M or N) and
+// the leading dimensions must be multiples of 4, the bases 16-byte aligned.
+static bool vec_ok(const GemmArgs &g) {
+    if (g.lda % 4 || g.ldb % 4) return false;
+    if (g.a_kcontig ? g.K % 4 : g.M % 4) return false;
+    if (g.b_kcontig ? g.K % 4 : g.N % 4) return false;
+    return aligned16(g.A) && aligned16(g.B);
+}
+
 void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
     if (g.M <= 0 || g.N <= 0) return;
     if (g.K <= 0) {
         if (g.epi == EPI_STORE) {
             for (int m = 0; m < g.M; m++)
                 PTC_CHECK(cudaMemsetAsync(g.C + (size_t)m * g.ldc, 0, (size_t)g.N * 4, s));
+        }
+        return;
+    }
+    if (vec_ok(g)) {
+        // Tile: 128x128 when the product alone fills the GPU, else 64x64;
+        // then split K (chunks of at least 64, a multiple of the k-tile)
+        // until about one wave of CTAs covers the SMs.
+        const bool big = (long)((g.M + 127) / 128) * ((g.N + 127) / 128) >= n_sm;
+        const int BK = big ? 8 : 16;
+        const long tiles = big ? (long)((g.M + 127) / 128) * ((g.N + 127) / 128)
+                               : (long)((g.M + 63) / 64) * ((g.N + 63) / 64);
+        int splits = 1;
+        if (g.partial)
+            while (tiles * splits * 2 <= 2L * n_sm && g.K / (splits * 2) >= 64 &&
+                   (size_t)(splits * 2) * g.M * g.N <= g.partial_cap)
+                splits *= 2;
+        int kper = (g.K + splits - 1) / splits;
+        kper = (kper + BK - 1) / BK * BK;
+        g.splits = (g.K + kper - 1) / kper;
+        if (big) launch_tile_v<128, 128, 8, 8, 8>(g, kper, s);
+        else launch_tile_v<64, 64, 16, 4, 4>(g, kper, s);
+        if (g.splits > 1) {
+            int blocks = (int)(((size_t)g.M * g.N + 255) / 256);
+            if (blocks > 8 * n_sm) blocks = 8 * n_sm;
+            k_splitk_reduce<<<blocks, 256, 0, s>>>(g);
+            PTC_CHECK(cudaGetLastError());
         }
         return;
     }

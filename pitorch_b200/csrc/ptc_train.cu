@@ -67,12 +67,13 @@ __global__ void __launch_bounds__(128) k_tr_attn_fwd(const float *q, const float
     const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
     for (int d = threadIdx.x; d < hd; d += blockDim.x) s_q[d] = q[(size_t)t * D + h * hd + d];
     __syncthreads();
-    for (int s = warp; s <= t; s += nwarp) {
-        const float *kr = k + (size_t)s * K + koff;
+    // one thread per position: independent 128-bit loads of k_s
+    for (int s = threadIdx.x; s <= t; s += blockDim.x) {
+        const float4 *kr = reinterpret_cast<const float4 *>(k + (size_t)s * K + koff);
+        const float4 *q4 = reinterpret_cast<const float4 *>(s_q);
         float acc = 0.f;
-        for (int d = lane; d < hd; d += 32) acc = fmaf(s_q[d], kr[d], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) s_p[s] = __fmul_rn(acc, scale);
+        for (int d4 = 0; d4 < hd / 4; d4++) acc = dot4(__ldg(kr + d4), q4[d4], acc);
+        s_p[s] = __fmul_rn(acc, scale);
     }
     __syncthreads();
     if (warp == 0) {
@@ -97,9 +98,22 @@ __global__ void __launch_bounds__(128) k_tr_attn_fwd(const float *q, const float
         arow[s] = p;
     }
     __syncthreads();
+    // weighted values: warp w sums positions s = w (mod 4) for columns
+    // lane and lane + 32; the four partial sums are added in warp order
+    __shared__ float s_part[4][64];
+    float o0 = 0.f, o1 = 0.f;
+    for (int s = warp; s <= t; s += nwarp) {
+        const float p = s_p[s];
+        const float *vr = v + (size_t)s * K + koff;
+        if (lane < hd) o0 = fmaf(p, vr[lane], o0);
+        if (lane + 32 < hd) o1 = fmaf(p, vr[lane + 32], o1);
+    }
+    s_part[warp][lane] = o0;
+    s_part[warp][lane + 32] = o1;
+    __syncthreads();
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.f;
-        for (int s = 0; s <= t; s++) o = fmaf(s_p[s], v[(size_t)s * K + koff + d], o);
+        for (int w = 0; w < nwarp; w++) o += s_part[w][d];
         out[(size_t)t * D + h * hd + d] = o;
     }
 }
@@ -222,14 +236,22 @@ __global__ void k_tr_rmsnorm_bwd(float *dx, float *dw_rows, const float *d_o, co
     }
 }
 
-// g[i] += sum over rows of dw_rows[t][i], accumulated in row order like the
-// reference's position loop.
-__global__ void k_tr_colsum_accum(float *g, const float *rows_, int n_rows, int D) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= D) return;
-    float acc = g[i];
-    for (int t = 0; t < n_rows; t++) acc = __fadd_rn(acc, rows_[(size_t)t * D + i]);
-    g[i] = acc;
+// g[i] += sum over rows of dw_rows[t][i]: CTA = 32 columns, warp w sums
+// rows w, w + 8, ... (lane = column), the 8 partials are added in warp order.
+__global__ void __launch_bounds__(256) k_tr_colsum_accum(float *g, const float *rows_, int n_rows, int D) {
+    __shared__ float s_part[8][33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x * 32 + lane;
+    float acc = 0.f;
+    if (i < D)
+        for (int t = warp; t < n_rows; t += 8) acc = __fadd_rn(acc, rows_[(size_t)t * D + i]);
+    s_part[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0 && i < D) {
+        float sum = g[i];
+        for (int w = 0; w < 8; w++) sum = __fadd_rn(sum, s_part[w][lane]);
+        g[i] = sum;
+    }
 }
 
 // silu*gate backward (pt_train.c:715-721).
@@ -262,12 +284,12 @@ __global__ void __launch_bounds__(128) k_tr_attn_bwd_q(const float *d_ao, const 
     const float *P = att + ((size_t)h * T + t) * T;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) s_do[d] = d_ao[(size_t)t * D + h * hd + d];
     __syncthreads();
-    for (int s = warp; s <= t; s += nwarp) {
-        const float *vr = v + (size_t)s * K + koff;
+    for (int s = threadIdx.x; s <= t; s += blockDim.x) {
+        const float4 *vr = reinterpret_cast<const float4 *>(v + (size_t)s * K + koff);
+        const float4 *d4p = reinterpret_cast<const float4 *>(s_do);
         float acc = 0.f;
-        for (int d = lane; d < hd; d += 32) acc = fmaf(s_do[d], vr[d], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) s_dp[s] = acc;
+        for (int d4 = 0; d4 < hd / 4; d4++) acc = dot4(__ldg(vr + d4), d4p[d4], acc);
+        s_dp[s] = acc;
     }
     __syncthreads();
     if (warp == 0) {
@@ -285,9 +307,20 @@ __global__ void __launch_bounds__(128) k_tr_attn_bwd_q(const float *d_ao, const 
         if (s <= t) s_dp[s] = x;
     }
     __syncthreads();
+    __shared__ float s_part[4][64];
+    float a0 = 0.f, a1 = 0.f;
+    for (int s = warp; s <= t; s += nwarp) {
+        const float x = s_dp[s];
+        const float *kr = k + (size_t)s * K + koff;
+        if (lane < hd) a0 = fmaf(x, kr[lane], a0);
+        if (lane + 32 < hd) a1 = fmaf(x, kr[lane + 32], a1);
+    }
+    s_part[warp][lane] = a0;
+    s_part[warp][lane + 32] = a1;
+    __syncthreads();
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float acc = 0.f;
-        for (int s = 0; s <= t; s++) acc = fmaf(s_dp[s], k[(size_t)s * K + koff + d], acc);
+        for (int w = 0; w < nwarp; w++) acc += s_part[w][d];
         d_q[(size_t)t * D + h * hd + d] = acc;
     }
 }
@@ -298,17 +331,39 @@ __global__ void __launch_bounds__(128) k_tr_attn_bwd_q(const float *d_ao, const 
 __global__ void __launch_bounds__(128) k_tr_attn_bwd_kv(const float *d_ao, const float *att, const float *q,
                                                         const float *dS, float *d_k, float *d_v, int T,
                                                         int n_rows, int nh, int nkv, int hd) {
+    // warp w takes rows t = s + w (mod warps); lanes own columns lane and
+    // lane + 32 (hd <= 64); partial sums are added in warp order
     const int kh = blockIdx.x, s = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
     const int D = nh * hd, K = nkv * hd, group = nh / nkv;
+    __shared__ float s_k[4][64], s_v[4][64];
+    float ak0 = 0.f, ak1 = 0.f, av0 = 0.f, av1 = 0.f;
+    for (int hh = 0; hh < group; hh++) {
+        const int h = kh * group + hh;
+        for (int t = s + warp; t < n_rows; t += nwarp) {
+            const size_t rowoff = ((size_t)h * T + t) * T + s;
+            const float ds = dS[rowoff], p = att[rowoff];
+            const float *qr = q + (size_t)t * D + h * hd, *dr = d_ao + (size_t)t * D + h * hd;
+            if (lane < hd) {
+                ak0 = fmaf(ds, qr[lane], ak0);
+                av0 = fmaf(p, dr[lane], av0);
+            }
+            if (lane + 32 < hd) {
+                ak1 = fmaf(ds, qr[lane + 32], ak1);
+                av1 = fmaf(p, dr[lane + 32], av1);
+            }
+        }
+    }
+    s_k[warp][lane] = ak0;
+    s_k[warp][lane + 32] = ak1;
+    s_v[warp][lane] = av0;
+    s_v[warp][lane + 32] = av1;
+    __syncthreads();
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float ak = 0.f, av = 0.f;
-        for (int hh = 0; hh < group; hh++) {
-            const int h = kh * group + hh;
-            for (int t = s; t < n_rows; t++) {
-                const size_t rowoff = ((size_t)h * T + t) * T + s;
-                ak = fmaf(dS[rowoff], q[(size_t)t * D + h * hd + d], ak);
-                av = fmaf(att[rowoff], d_ao[(size_t)t * D + h * hd + d], av);
-            }
+        for (int w = 0; w < nwarp; w++) {
+            ak += s_k[w][d];
+            av += s_v[w][d];
         }
         d_k[(size_t)s * K + kh * hd + d] = ak;
         d_v[(size_t)s * K + kh * hd + d] = av;
@@ -407,6 +462,7 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
     tr->w = *w;
     if (max_T < 2) PTC_FATAL("training needs max_T >= 2 (got %d)", max_T);
     if (tr->D % 2 || tr->hd % 2) PTC_FATAL("training needs even dim and head_dim");
+    if (tr->hd > 64 || tr->hd % 4) PTC_FATAL("training attention supports head_dim <= 64, a multiple of 4 (got %d)", tr->hd);
 
     const size_t T = max_T, D = tr->D, H = tr->H, L = tr->L, K = tr->K, V = tr->V, nh = tr->nh;
     auto A = [&](size_t n) { return (float *)ptc_alloc(c, (n ? n : 1) * 4); };
@@ -590,7 +646,7 @@ extern "C" void ptc_trainer_bwd_head(ptc_trainer *tr) {
     const float *rfin = tr->res + (size_t)tr->L * T * D;
     ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, rfin,
                                                       tr->w.rms_final_weight, n, D);
-    ptc::k_tr_colsum_accum<<<(D + 127) / 128, 128, 0, s>>>(tr->g_rms_final, tr->dw_rows, n, D);
+    ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_final, tr->dw_rows, n, D);
     // dWcls += d_logit^T . x_final   [V x D], K = n
     run_gemm(tr, G(V, D, n, tr->d_logit, V, false, tr->x_final, D, false, tr->g_wcls, D, ptc::EPI_ACCUM));
     PTC_CHECK(cudaGetLastError());
@@ -622,7 +678,7 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
                        ptc::EPI_ACCUM));
         ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res_att + LD,
                                                           tr->w.rms_ffn_weight + (size_t)l * D, n, D);
-        ptc::k_tr_colsum_accum<<<(D + 127) / 128, 128, 0, s>>>(tr->g_rms_ffn + (size_t)l * D, tr->dw_rows, n, D);
+        ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_ffn + (size_t)l * D, tr->dw_rows, n, D);
         // wo
         run_gemm(tr, G(n, D, D, tr->d_res, D, true, Wo, D, false, tr->d_aout, D, ptc::EPI_STORE));
         run_gemm(tr, G(D, D, n, tr->d_res, D, false, tr->att_out + LD, D, false, tr->g_wo + (size_t)l * D * D, D,
@@ -632,7 +688,7 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         const float *att_l = tr->att + (size_t)l * nh * T * T;
         ptc::k_tr_attn_bwd_q<<<dim3(nh, n), 128, smem, s>>>(tr->d_aout, att_l, tr->q + LD, tr->k + LK, tr->v + LK,
                                                             tr->dS, tr->d_q, T, nh, tr->nkv, tr->hd);
-        ptc::k_tr_attn_bwd_kv<<<dim3(tr->nkv, n), 64, 0, s>>>(tr->d_aout, att_l, tr->q + LD, tr->dS, tr->d_k,
+        ptc::k_tr_attn_bwd_kv<<<dim3(tr->nkv, n), 128, 0, s>>>(tr->d_aout, att_l, tr->q + LD, tr->dS, tr->d_k,
                                                               tr->d_v, T, n, nh, tr->nkv, tr->hd);
         ptc::k_tr_rope_bwd<<<blocks_for((size_t)n * D / 2, 256, tr->n_sm), 256, 0, s>>>(
             tr->d_qpre, tr->d_kpre, tr->d_q, tr->d_k, n, D, K, tr->hd);
@@ -645,7 +701,7 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         run_gemm(tr, G(K, D, n, tr->d_v, K, false, xa, D, false, tr->g_wv + (size_t)l * K * D, D, ptc::EPI_ACCUM));
         ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res + LD,
                                                           tr->w.rms_att_weight + (size_t)l * D, n, D);
-        ptc::k_tr_colsum_accum<<<(D + 127) / 128, 128, 0, s>>>(tr->g_rms_att + (size_t)l * D, tr->dw_rows, n, D);
+        ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_att + (size_t)l * D, tr->dw_rows, n, D);
     }
     PTC_CHECK(cudaGetLastError());
 }
