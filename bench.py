@@ -103,6 +103,15 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# DRAM bytes (read + write) per launch of each decode kernel from one ncu
+# capture of the 16-position bench case (positions 0-15, so the attention
+# block's KV share is that of those positions, not of the mean position):
+# dram__bytes_read.sum + dram__bytes_write.sum.
+TRAFFIC = {"attention block": 9502208, "ffn block": 18909696, "classifier": 102196000}
+TRAFFIC_SOURCE = ("ncu --set full, one launch each, python bench.py --positions 16 --steps 1 --warmup 1 "
+                  "--no-cpu-baseline (attention block at a position < 16: its KV bytes are those of that position)")
+
+
 def decode_bytes_per_token(cfg, pos):
     """Algorithmic HBM bytes of one decode position: all weights read once
     (tied classifier = embedding table, read once by the classifier, plus one
@@ -218,22 +227,48 @@ def run_single(args):
     e2e_value = seq / (e2e_ms / 1000.0)
     streams_match = bool(np.array_equal(toks_host, toks_dev))
 
-    # ---- roofline of the dominant kernel: the classifier (k_cls) ------------
-    n_cls = 50
-    L.ptc_sync(pctx)
-    L.ptc_timer_start(timer)
-    for _ in range(n_cls):
-        L.ptc_decoder_enqueue_head(dec)
-    L.ptc_timer_stop(timer)
-    cls_ms = L.ptc_timer_ms(timer) / n_cls
-    cls_bytes = 4 * (V * dim + V + 2 * dim)
+    # ---- per-kernel rooflines: each decode kernel alone, 50 back-to-back
+    # launches at the mean position (CUDA events on the decoder's stream) ----
     hbm, src = peaks()
-    cls_gbs = cls_bytes / (cls_ms / 1000.0) / 1e9
+    launches_per_step = L.ptc_decoder_launches_per_step(dec)
+    kvd = nkv * (dim // nh)
+    pos_mid = seq // 2
+    n_rep = 50
+
+    def time_kernel(kind, layer):
+        L.ptc_sync(pctx)
+        L.ptc_timer_start(timer)
+        for _ in range(n_rep):
+            L.ptc_decoder_enqueue_kernel(dec, kind, layer, pos_mid)
+        L.ptc_timer_stop(timer)
+        return L.ptc_timer_ms(timer) / n_rep
+
+    fused = launches_per_step == 2 * nl + 1
+    kern = {
+        # attention block: q/k/v and wo rows, the rms gain, K/V rows of
+        # positions <= pos read, one K/V row written, x read
+        "attention block": (0, 4 * (dim * (dim + 2 * kvd) + dim * dim + dim + 2 * (pos_mid + 1) * kvd + 2 * kvd + dim),
+                            "k_attn_fused: per-head clusters; q/k/v rows, RoPE, KV attention, wo" if fused
+                            else "q/k/v, attention and wo kernels"),
+        "ffn block": (1, 4 * (3 * hidden * dim + dim + dim),
+                      "k_ffn: rmsnorm, w1/w3 rows, silu, transposed-w2 split-K"),
+        "classifier": (2, 4 * (V * dim + V + 2 * dim), "k_mv<CLS>: final rmsnorm, 32000 rows, argmax"),
+    }
+    kernels = {}
+    for name, (kind, nbytes, what) in kern.items():
+        ms_k = time_kernel(kind, nl // 2)
+        gbs = nbytes / (ms_k / 1000.0) / 1e9
+        kernels[name] = {"kernel": what, "bytes_per_launch": nbytes, "ms_per_launch": ms_k,
+                         "achieved": gbs, "frac": gbs / hbm,
+                         "launches_per_step": (nl if kind < 2 else 1) * seq}
+    L.ptc_decoder_reset(dec)
+    # dominant kernel: the largest share of the step's kernel time
+    dom = max(kernels, key=lambda k: kernels[k]["ms_per_launch"] * kernels[k]["launches_per_step"])
+    dk = kernels[dom]
 
     # whole-step roofline (bytes per token over the decode)
     mean_bytes = np.mean([decode_bytes_per_token(cfg, p) for p in range(seq)])
     step_gbs = mean_bytes * seq / (ms_per_step / 1000.0) / 1e9
-
     L.ptc_timer_destroy(timer)
     ctx.close()
     clocks = clk.summary()
@@ -248,14 +283,16 @@ def run_single(args):
         "e2e": {"value": e2e_value, "unit": "tokens/s", "api": "pt_forward_step per position",
                 "h2d_bytes_per_step": 8 * seq, "d2h_bytes_per_step": 4 * seq,
                 "wall_ms_per_step": e2e_wall_ms, "token_stream_equals_device_loop": streams_match},
-        "roofline": {"kernel": "k_cls (final rmsnorm + 32000x768 classifier matvec + argmax)",
-                     "bound": "hbm", "achieved": cls_gbs, "peak": hbm, "unit": "GB/s",
-                     "frac": cls_gbs / hbm, "peak_source": f"{src} hbm_gbs",
-                     "traffic": None, "bytes_per_launch": cls_bytes, "ms_per_launch": cls_ms},
+        "roofline": {"kernel": f"{dom}: {dk['kernel']}", "bound": "hbm", "achieved": dk["achieved"],
+                     "peak": hbm, "unit": "GB/s", "frac": dk["frac"], "peak_source": f"{src} hbm_gbs (burst copy)",
+                     "traffic": TRAFFIC.get(dom), "traffic_source": TRAFFIC_SOURCE,
+                     "bytes_per_launch": dk["bytes_per_launch"], "ms_per_launch": dk["ms_per_launch"],
+                     "position": pos_mid, "timing": f"{n_rep} back-to-back launches, CUDA events"},
+        "kernels": kernels,
         "step_roofline": {"bytes_per_token": float(mean_bytes), "achieved": step_gbs, "peak": hbm,
                           "unit": "GB/s", "frac": step_gbs / hbm,
                           "roofline_tokens_per_s": hbm * 1e9 / mean_bytes},
-        "gpu_launches": args.steps * seq * (5 * nl + 1),
+        "gpu_launches": args.steps * seq * launches_per_step,
         "clocks": clocks,
     }
     if not args.no_cpu_baseline:

@@ -158,6 +158,15 @@ int *ptc_decoder_pos_dev(ptc_decoder *d);
 int *ptc_decoder_tok_dev(ptc_decoder *d);
 void ptc_decoder_enqueue_layers_devpos(ptc_decoder *d, int l_start, int l_end);
 void ptc_decoder_enqueue_embed_dev(ptc_decoder *d);
+/* Timing hook (no reference counterpart): enqueue ONE kernel of the decode
+ * step at position pos -- kind 0: layer l's attention block, 1: layer l's
+ * FFN block, 2: the classifier head -- on the residual buffers of a full
+ * decode. The decode state it leaves is not meaningful: call
+ * ptc_decoder_reset before decoding again. */
+void ptc_decoder_enqueue_kernel(ptc_decoder *d, int kind, int l, int pos);
+/* Kernels one decode position launches (2 per layer + head when the layer
+ * blocks are fused, 5 per layer + head otherwise). */
+int ptc_decoder_launches_per_step(ptc_decoder *d);
 /* Stream helpers for the pipeline's bounded waits: 0 = all queued work on
  * the context stream finished, 1 = still running after timeout_ms. */
 int ptc_wait_deadline(ptc_ctx *c, int timeout_ms);

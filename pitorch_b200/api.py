@@ -201,6 +201,8 @@ def declare(L):
     _sig(L, "ptc_decoder_enqueue_embed", None, vp, C.c_int)
     _sig(L, "ptc_decoder_enqueue_layers", None, vp, C.c_int, C.c_int, C.c_int)
     _sig(L, "ptc_decoder_enqueue_head", None, vp)
+    _sig(L, "ptc_decoder_enqueue_kernel", None, vp, C.c_int, C.c_int, C.c_int)
+    _sig(L, "ptc_decoder_launches_per_step", C.c_int, vp)
     _sig(L, "ptc_decoder_fetch_next", C.c_int, vp, f32p)
     _sig(L, "ptc_decoder_step", C.c_int, vp, C.c_int, C.c_int, f32p)
     _sig(L, "ptc_timer_create", vp, vp)

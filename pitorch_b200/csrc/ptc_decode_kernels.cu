@@ -1260,6 +1260,35 @@ static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float
     PTC_NV_SWITCH(nvh, (launch_mv<NV, MV_RESID>(m, a, n_sm, s)));
 }
 
+// One block of layer l (kind 0: attention, 1: FFN) on the buffers a full
+// [0, L) decode uses -- for timing single kernels.
+void launch_block(const DecodeModel &m, int kind, int l, int n_sm, cudaStream_t s) {
+    float *x_in = m.x, *x_out = m.x;
+    if (m.fused_ffn) {
+        x_in = (l == 0) ? m.x : m.xo + (size_t)(l - 1) * m.dim;
+        x_out = (l == m.L - 1) ? m.x : m.xo + (size_t)l * m.dim;
+    }
+    const int nvd = nv_of(m.dim);
+    if (kind == 0 && m.fused_attn) {
+        AttnArgs at;
+        memset(&at, 0, sizeof(at));
+        at.xin = x_in;
+        at.xout = m.xm;
+        at.xclear = x_in;
+        at.l = l;
+        PTC_NV_SWITCH(nvd, (launch_attn_fused<NV>(m, at, s)));
+    } else if (kind == 1 && m.fused_ffn) {
+        FfnArgs f;
+        f.xin = m.xm;
+        f.xout = x_out;
+        f.xclear = m.fused_attn ? m.xm : nullptr;
+        f.l = l;
+        PTC_NV_SWITCH(nvd, (launch_ffn<NV>(m, f, n_sm, s)));
+    } else {
+        launch_layer(m, l, false, x_in, x_out, n_sm, s);   // unfused layouts: the whole layer
+    }
+}
+
 // Layers [l0, l1): the range reads m.x and leaves its output in m.x. With
 // the fused FFN, layer l < l1-1 hands over through xo[l] (zeroed again by
 // the next layer's wo once read); the last layer accumulates into m.x,

@@ -267,6 +267,13 @@ extern "C" void ptc_decoder_reset(ptc_decoder *d) {
         PTC_CHECK(cudaMemsetAsync(d->m.kc, 0, kv, d->stream));
         PTC_CHECK(cudaMemsetAsync(d->m.vc, 0, kv, d->stream));
     }
+    // the fused layers' accumulation buffers start from zero (a completed
+    // step leaves them so; a timing hook may not)
+    if (d->m.fused_ffn) {
+        PTC_CHECK(cudaMemsetAsync(d->m.xm, 0, (size_t)d->m.dim * 4, d->stream));
+        PTC_CHECK(cudaMemsetAsync(d->m.xo, 0, (size_t)d->m.L * d->m.dim * 4, d->stream));
+        PTC_CHECK(cudaMemsetAsync(d->m.tickets, 0, 64, d->stream));
+    }
     PTC_CHECK(cudaStreamSynchronize(d->stream));
 }
 
@@ -410,6 +417,26 @@ extern "C" void ptc_decoder_enqueue_layers_devpos(ptc_decoder *d, int l_start, i
     if (l_start < 0 || l_end > d->m.L || l_start > l_end)
         PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
     ptc::launch_layers(d->m, l_start, l_end, false, d->n_sm, d->stream);
+}
+
+extern "C" void ptc_decoder_enqueue_kernel(ptc_decoder *d, int kind, int l, int pos) {
+    if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
+    set_mode(d, 0);
+    put_step_int(d, &d->m.step->pos, pos);
+    if (kind == 2) {
+        if (!d->has_head) PTC_FATAL("decoder has no head");
+        ptc::launch_head(d->m, d->n_sm, d->stream);
+        return;
+    }
+    if (l < 0 || l >= d->m.L) PTC_FATAL("layer %d outside [0, %d)", l, d->m.L);
+    ptc::launch_block(d->m, kind, l, d->n_sm, d->stream);
+}
+
+extern "C" int ptc_decoder_launches_per_step(ptc_decoder *d) {
+    if (d->persist) return 1;
+    const ptc::DecodeModel &m = d->m;
+    const int per_layer = m.fused_attn ? 2 : m.fused_ffn ? 4 : 5;
+    return per_layer * m.L + (d->has_head ? 1 : 0) + (d->has_embed && m.L == 0 ? 1 : 0);
 }
 
 extern "C" void ptc_decoder_enqueue_embed_dev(ptc_decoder *d) {

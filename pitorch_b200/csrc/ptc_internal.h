@@ -22,6 +22,7 @@ struct DecodeModel;
 // Layers [l0, l1) of one decode position; the range reads and leaves x in m.x.
 void launch_layers(const DecodeModel &m, int l0, int l1, bool from_embedding, int n_sm, cudaStream_t s);
 int decode_ffn_rows(int dim, int hidden, int n_sm);
+void launch_block(const DecodeModel &m, int kind, int l, int n_sm, cudaStream_t s);
 int decode_attn_stage(int dim, int nh, int nkv, int seq);
 void build_rope_table(float2 *t, int seq, int hd, cudaStream_t s);
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s);

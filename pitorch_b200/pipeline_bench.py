@@ -14,8 +14,9 @@ the others split the 12 layers), joins the ring (NCCL over NVLink) and runs
 
 Batch-1 decode cannot overlap positions (each token depends on the previous
 argmax), so the pipeline splits weights across GPUs without adding
-throughput; the scaling is reported as measured ("weak": every N runs the
-same full decode).
+throughput; every N runs the same full decode (fixed total work: "strong"
+scaling), reported as measured against the serial roofline (each token's
+bytes stream once, stage after stage).
 """
 import json
 import os
@@ -37,6 +38,7 @@ def run(args, rank, world):
     seq = cfg[6] if not args.positions else min(args.positions, cfg[6])
     blob = synth.make_blob(cfg)
     prompt = synth.make_prompt(cfg[5], 8)
+    import bench as _bench   # the single-GPU bench's clock sampler and byte model
     pipe = api.Pipeline(blob, rank, world, device=local)
     del blob
     pc = pipe.ctx.ptc_ctx()
@@ -46,12 +48,13 @@ def run(args, rank, world):
         pipe.generate_greedy(prompt, seq)
     ms = 0.0
     toks = None
-    for _ in range(args.steps):
-        L.ptc_sync(pc)
-        L.ptc_timer_start(timer)
-        toks = pipe.generate_greedy(prompt, seq)
-        L.ptc_timer_stop(timer)
-        ms += L.ptc_timer_ms(timer)
+    with _bench.ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            L.ptc_sync(pc)
+            L.ptc_timer_start(timer)
+            toks = pipe.generate_greedy(prompt, seq)
+            L.ptc_timer_stop(timer)
+            ms += L.ptc_timer_ms(timer)
     ms_step = pipe.max_over_ranks(ms / args.steps)
     value = seq / (ms_step / 1000.0)
 
@@ -68,13 +71,22 @@ def run(args, rank, world):
     same = pipe.max_over_ranks(0.0 if same else 1.0) == 0.0
 
     dim, hidden, nl, nh, nkv, V, _ = cfg
-    n_layer_ranks = world - 1
-    launches = seq * (5 * nl + 2 + 2 * n_layer_ranks)
+    # kernels per position over all ranks: the layer kernels of every layer
+    # (the same count per layer on every rank), the head rank's embedding and
+    # classifier; NCCL's own send/recv kernels are not counted
+    dec = pipe.ctx.ptc_decoder()
+    n_local = int(pipe.ctx.cfg.n_layers)
+    per_layer = (L.ptc_decoder_launches_per_step(dec) - (1 if pipe.is_head else 0)) // n_local if n_local else 0
+    per_layer = int(pipe.max_over_ranks(float(per_layer)))
+    launches = seq * (per_layer * nl + 2)
+    hbm, src = _bench.peaks()
+    mean_bytes = float(np.mean([_bench.decode_bytes_per_token(cfg, p) for p in range(seq)]))
+    step_gbs = mean_bytes * seq / (ms_step / 1000.0) / 1e9
     if rank == 0:
         line = {
             "metric": "batch-1 decode tokens/s (stories110M shape)", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) fp32 weights, seeded 8-token prompt)",
             "config": {"workload": f"{model} batch-1 greedy decode, {seq} positions per step, "
                                    f"layer pipeline over {world} GPUs",
@@ -86,6 +98,10 @@ def run(args, rank, world):
                     "h2d_bytes_per_step": 8 * seq, "d2h_bytes_per_step": 4 * seq,
                     "wall_ms_per_step": e2e_wall, "token_stream_equals_device_loop": same},
             "gpu_launches": args.steps * launches,
+            "step_roofline": {"bytes_per_token": mean_bytes, "achieved": step_gbs, "peak": hbm, "unit": "GB/s",
+                              "frac": step_gbs / hbm, "peak_source": f"{src} hbm_gbs",
+                              "basis": "serial: each token's weights and KV stream once, stage after stage"},
+            "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
     L.ptc_timer_destroy(timer)
