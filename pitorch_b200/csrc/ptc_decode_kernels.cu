@@ -829,7 +829,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     if (tid < hd) rcs = __ldg(m.rope + (size_t)pos * (hd / 2) + (tid % (hd / 2)));
     const float *xsrc = a.xin ? a.xin : m.emb + (size_t)__ldcg(&m.step->tok) * dim;
     if (!a.xin) load_act<NV>(xr, xsrc, c4, lane);
-    cluster.sync();   // every CTA of the cluster runs before any remote store
+    // every CTA of the cluster runs before any remote store (no memory
+    // ordering needed here, so the relaxed form)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
     pdl_wait();
     if (a.xin) load_act<NV>(xr, xsrc, c4, lane);
     if (h == 0)
@@ -857,8 +859,24 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             const int row = f / hd4, c = f - row * hd4;
             cp_async16(stage + (size_t)row * hd + 4 * c, wo_base + (size_t)(o0 + row) * dim + 4 * c);
         }
-        cp_async_commit();
     }
+    // K/V rows of the earlier positions past the first round: copied now
+    // into the free part of the staging region (after the wo slice and the
+    // value sums), so later rounds read shared memory; positions beyond its
+    // capacity are read from global memory in their round.
+    float *s_o = stage + (size_t)(dim / AC) * hd;   // value sums [ngrp][hd], after the wo slice
+    float *kv2 = s_o + (size_t)ngrp * hd;           // K rows [n2][hd], then V rows [n2][hd]
+    const int p2 = t0 + AT_ROUND;
+    const int kv2_cap = (a.stage_floats - (dim / AC) * hd - ngrp * hd) / (2 * hd);
+    const int n2 = max(0, min(min(t1, pos), p2 + kv2_cap) - p2);
+    if (n2 > 0) {
+        const float *kb = m.kc + (head_base + p2) * hd, *vb = m.vc + (head_base + p2) * hd;
+        for (int f = tid; f < n2 * hd4; f += AT_THREADS) {
+            cp_async16(kv2 + 4 * f, kb + 4 * f);
+            cp_async16(kv2 + (size_t)n2 * hd + 4 * f, vb + 4 * f);
+        }
+    }
+    cp_async_commit();
     // 2. RoPE (llama2.c:238-245) in place on q and k
     if (tid < hd) {
         const int is_k = tid >= hd / 2;
@@ -870,11 +888,6 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         v[1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
     }
     __syncthreads();
-    if (r == 0 && pos_ok && tid < 2 * hd) {
-        const int d = tid % hd;
-        float *dst = (tid < hd ? m.kc : m.vc) + (head_base + pos) * hd + d;
-        *dst = s_qkv[(tid < hd ? hd : 2 * hd) + d];
-    }
 
     // 3. attention over [t0, t1): online softmax in rounds of AT_ROUND
     const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
@@ -884,24 +897,31 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         const int cc = sub + 4 * i;
         qv[i] = (cc < hd4) ? reinterpret_cast<const float4 *>(s_qkv)[cc] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    float *s_o = stage + (size_t)(dim / AC) * hd;   // value sums [ngrp][hd], after the wo slice
     float m_run = -3.4028235e+38f, l_run = 0.f, o_run = 0.f;   // o_run: element tid of the output (tid < hd)
     for (int rt0 = t0; rt0 < t1; rt0 += AT_ROUND) {
         const int n = min(AT_ROUND, t1 - rt0);
-        if (rt0 != t0) {   // later rounds: load after the wait (L2 was warmed)
+        if (rt0 != t0) {   // later rounds: staged rows from shared memory, the rest from L2 (warmed)
+            cp_async_wait_all();
+            __syncthreads();
             const float4 *kb = reinterpret_cast<const float4 *>(m.kc + (head_base + rt0) * hd);
             const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + rt0) * hd);
+            const float4 *ks = reinterpret_cast<const float4 *>(kv2);
+            const float4 *vs = reinterpret_cast<const float4 *>(kv2 + (size_t)n2 * hd);
 #pragma unroll
             for (int i = 0; i < QK; i++) {
-                const int cc = sub + 4 * i;
-                kv[i] = (cc < hd4 && js < n && rt0 + js != pos) ? __ldcg(kb + (size_t)js * hd4 + cc)
-                                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                const int cc = sub + 4 * i, p = rt0 + js;
+                float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (cc < hd4 && js < n && p != pos)
+                    val = (p - p2 < n2) ? ks[(size_t)(p - p2) * hd4 + cc] : __ldcg(kb + (size_t)js * hd4 + cc);
+                kv[i] = val;
             }
 #pragma unroll
             for (int k = 0; k < VP; k++) {
-                const int j = grp + ngrp * k;
-                vpre[k] = (grp < ngrp && j < n && rt0 + j != pos) ? __ldcg(vb + (size_t)j * hd4 + d4)
-                                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                const int j = grp + ngrp * k, p = rt0 + j;
+                float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (grp < ngrp && j < n && p != pos)
+                    val = (p - p2 < n2) ? vs[(size_t)(p - p2) * hd4 + d4] : __ldcg(vb + (size_t)j * hd4 + d4);
+                vpre[k] = val;
             }
         }
         // the current position's row is this kernel's own (post-RoPE) k and v
@@ -1017,6 +1037,13 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             }
             red_add_v4(a.xout + o0 + 4 * qd, out);
         }
+    }
+    // the new K/V row, needed only by later tokens (written after the
+    // cluster barriers, whose release would otherwise wait for it)
+    if (r == 0 && pos_ok && tid < 2 * hd) {
+        const int d = tid % hd;
+        float *dst = (tid < hd ? m.kc : m.vc) + (head_base + pos) * hd + d;
+        *dst = s_qkv[(tid < hd ? hd : 2 * hd) + d];
     }
     if (tid == AT_THREADS - 1) s_last = (ticket == gridDim.x - 1);
     __syncthreads();

@@ -122,7 +122,7 @@ def make_matvec_kat():
                    "cases": entries}, f, indent=1)
 
 
-def make_decode(name, n_pos, keep_rows):
+def make_decode(name, n_pos, keep_rows, suffix=""):
     cfg = synth.CONFIGS[name]
     blob = synth.make_blob(cfg)
     prompt = synth.make_prompt(cfg[5])
@@ -132,7 +132,7 @@ def make_decode(name, n_pos, keep_rows):
     dt = time.time() - t0
     srt = np.sort(logits, axis=1)
     np.savez_compressed(
-        os.path.join(HERE, f"decode_{name}.npz"),
+        os.path.join(HERE, f"decode_{name}{suffix}.npz"),
         prompt=prompt, tokens=toks, n_pos=np.int32(n_pos), seed=np.int32(synth.DEFAULT_SEED),
         logit_absmax=np.abs(logits).max(axis=1), logit_sum=logits.astype(np.float64).sum(axis=1),
         top2_gap=srt[:, -1] - srt[:, -2], rows=np.array(keep_rows, dtype=np.int32),
@@ -176,6 +176,8 @@ def main():
     if not args.skip_slow:
         make_decode("stories42M", 64, [63])
         make_decode("stories110M", 64, [63])
+        # the whole 1024-position cache: attention over more than 512 positions
+        make_decode("stories42M", 1024, [511, 700, 1023], suffix="_long")
         make_train("stories15M", 256, 20)
 
 

@@ -19,8 +19,8 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-4
 
 
-def check_stream(ctx, name, n_pos=None):
-    g = golden(f"decode_{name}.npz")
+def check_stream(ctx, name, n_pos=None, fixture=None):
+    g = golden(fixture or f"decode_{name}.npz")
     n = int(g["n_pos"]) if n_pos is None else n_pos
     toks, logits = ctx.decode_greedy(g["prompt"], n, want_logits=True)
     assert np.array_equal(toks, g["tokens"][:n]), f"token stream diverged at {np.argmax(toks != g['tokens'][:n])}"
@@ -145,3 +145,43 @@ def test_unfused_layer_paths_match_reference(ptlib, monkeypatch, mode):
         ctx = api.Context(synth.make_blob(name))
         check_stream(ctx, name)
         ctx.close()
+
+
+NEAR_TIE = 1e-5   # top-2 logit gap / max|logit| below which fp32 order may flip the argmax
+
+
+@pytest.mark.parametrize("mode", ["default", "ffn"])
+def test_42M_full_cache_decode(ptlib, monkeypatch, mode):
+    """All 1024 positions of the 42M decode (attention over more than 512
+    positions: a second round of K/V per cluster CTA in the fused kernel).
+
+    The seeded model's logits are small and flat, so the reference's own
+    stream has near-ties (top-2 gap down to 0 at position 571) that any other
+    fp32 summation order may resolve differently. Hence:
+      teacher-forced  -- the reference's tokens as inputs at every position:
+        logits at 511, 700, 1023 within TOL; our argmax equals the reference's
+        token wherever its top-2 gap is at least NEAR_TIE of max|logit|;
+      free-running    -- the device loop equals the reference's stream up to
+        its first near-tie."""
+    if mode != "default":
+        monkeypatch.setenv("PTC_DECODE_FUSED", mode)
+    g = golden("decode_stories42M_long.npz")
+    ref_toks = g["tokens"]
+    forced = np.concatenate([g["prompt"][:1], ref_toks[:-1]]).astype(np.int32)
+    ctx = api.Context(synth.make_blob("stories42M"))
+    _, logits = ctx.decode_greedy(forced, 1024, want_logits=True)
+    for r, row in zip(g["rows"], g["logits_rows"]):
+        assert rel_err(logits[r], row) <= TOL, int(r)
+    am = np.abs(logits).max(axis=1)
+    assert np.all(np.abs(am - g["logit_absmax"]) <= TOL * g["logit_absmax"] + 1e-7)
+    clear = g["top2_gap"] >= NEAR_TIE * g["logit_absmax"]
+    clear[: len(g["prompt"]) - 1] = False   # prompt positions: the next token is forced, not an argmax
+    mine = logits.argmax(axis=1)
+    assert clear.sum() > 0.95 * len(clear)
+    assert np.array_equal(mine[clear], ref_toks[clear]), np.nonzero((mine != ref_toks) & clear)[0][:5]
+    free = ctx.generate_greedy(g["prompt"], 1024)
+    tie = ~clear
+    tie[: len(g["prompt"]) - 1] = False
+    first_tie = int(np.argmax(tie)) if tie.any() else 1024
+    assert np.array_equal(free[:first_tie + 1], ref_toks[:first_tie + 1]), first_tie
+    ctx.close()
