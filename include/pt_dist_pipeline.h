@@ -30,6 +30,11 @@ void pt_dist_setup(pt_dist_t *dist, const pt_shard_info_t *shard, int rank, int 
  * once all ranks joined). Returns 0 or -1 on timeout. */
 int pt_dist_ring_sync(pt_dist_t *dist);
 
+/* Decode hop transport in use once joined (no reference counterpart):
+ * 1 = stores into the successor's memory over NVLink (ptc_hop_*),
+ * 0 = NCCL send/recv, -1 = not joined. */
+int pt_dist_transport(const pt_dist_t *dist);
+
 /* pitorch/dist/pt_dist_pipeline.h:88 -- nothing to reset on NVLink; kept. */
 void pt_dist_reset_links(pt_dist_t *dist);
 

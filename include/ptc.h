@@ -267,6 +267,26 @@ void ptc_timer_stop(ptc_timer *t);
 float ptc_timer_ms(ptc_timer *t);     /* synchronises on the stop event */
 void ptc_timer_destroy(ptc_timer *t);
 
+/* ---- Pipeline hop over NVLink peer memory ----------------------------------
+ * The decode hop of pitorch/dist/pt_dist_pipeline.c:287-333 ([pos | x] from
+ * one stage to the next, there over GPIO). Each rank allocates a mailbox in
+ * its own memory and exports it (CUDA IPC handle of
+ * PTC_MAILBOX_HANDLE_BYTES) to the rank that sends to it. ptc_hop_send
+ * writes pos and x into the successor's mailbox with peer stores and then
+ * publishes ++*sent; ptc_hop_recv waits (at most timeout_ns on the GPU; on
+ * expiry *err = 1 and nothing is copied) until its mailbox holds message
+ * ++*recvd, then copies x (and pos, when pos is not NULL) out. The counters
+ * are device ints of the caller, zero at the start. */
+#define PTC_MAILBOX_HANDLE_BYTES 64
+void *ptc_mailbox_alloc(ptc_ctx *c, int dim);
+void ptc_mailbox_free(void *box);
+int ptc_mailbox_handle(void *box, void *handle_out);
+void *ptc_mailbox_open(ptc_ctx *c, const void *handle);  /* NULL when the peer cannot be mapped */
+void ptc_mailbox_close(void *peer);
+void ptc_hop_send(ptc_ctx *c, const float *x, const int *pos, void *peer_box, unsigned *sent, int dim);
+void ptc_hop_recv(ptc_ctx *c, const void *box, float *x, int *pos, unsigned *recvd, int dim, int *err,
+                  long long timeout_ns);
+
 /* ---- CUDA graphs of work enqueued on a context's stream ------------------
  * No reference counterpart (the Pi runtime has no command graphs). Between
  * ptc_capture_begin and ptc_capture_end, calls that enqueue on the context's

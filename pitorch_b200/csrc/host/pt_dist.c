@@ -44,6 +44,13 @@ typedef struct {
     int dim;
     int verbose;
     int step;
+    /* decode hops over NVLink peer memory (ptc_hop_*), when every rank could
+     * map its successor's mailbox; otherwise NCCL send/recv */
+    int p2p;
+    void *box;            /* this rank's mailbox (the predecessor writes it) */
+    void *peer_box;       /* the successor's mailbox, mapped */
+    unsigned *ctr;        /* device [0] messages sent, [1] messages received */
+    int *hop_err;         /* device: a hop wait ran out */
 } dist_comm_t;
 
 static long now_ms(void) {
@@ -160,6 +167,64 @@ static void fail(const pt_dist_t *d, const char *what) {
 }
 
 static dist_comm_t *comm_of(pt_dist_t *d) { return (dist_comm_t *)d->comm; }
+static int finish(pt_dist_t *dist, pt_context_t *ctx, const char *what);
+static int next_rank(const pt_dist_t *d) { return (d->rank + 1) % d->world_size; }
+static int prev_rank(const pt_dist_t *d) { return (d->rank + d->world_size - 1) % d->world_size; }
+
+/* Decode hops over NVLink: allocate this rank's mailbox, all-gather the IPC
+ * handles, map the successor's mailbox, and agree on the transport (every
+ * rank must use the same one). PT_DIST_P2P=0 keeps NCCL send/recv. Returns
+ * -1 only when a collective of the agreement times out. */
+static int setup_p2p(pt_dist_t *dist, pt_context_t *ctx) {
+    dist_comm_t *c = comm_of(dist);
+    const char *e = getenv("PT_DIST_P2P");
+    if (e && e[0] == '0') return 0;
+    ptc_ctx *pc = ctx->dev->ctx;
+    cudaStream_t s = (cudaStream_t)ptc_stream(pc);
+    const int W = dist->world_size, H = PTC_MAILBOX_HANDLE_BYTES;
+    unsigned char *dh = (unsigned char *)ptc_alloc(pc, (size_t)W * H);
+    unsigned char *hh = (unsigned char *)calloc((size_t)W, H);
+    c->box = ptc_mailbox_alloc(pc, c->dim);
+    int ok = c->box && ptc_mailbox_handle(c->box, hh + (size_t)dist->rank * H) == 0;
+    cudaMemcpyAsync(dh + (size_t)dist->rank * H, hh + (size_t)dist->rank * H, H, cudaMemcpyHostToDevice, s);
+    ncclAllGather(dh + (size_t)dist->rank * H, dh, H, ncclUint8, c->comm, s);
+    cudaMemcpyAsync(hh, dh, (size_t)W * H, cudaMemcpyDeviceToHost, s);
+    if (finish(dist, ctx, "mailbox exchange timeout") < 0) {
+        free(hh);
+        return -1;
+    }
+    if (ok) c->peer_box = ptc_mailbox_open(pc, hh + (size_t)next_rank(dist) * H);
+    free(hh);
+    ok = ok && c->peer_box;
+    float v = ok ? 1.f : 0.f;
+    cudaMemcpyAsync(c->scal, &v, 4, cudaMemcpyHostToDevice, s);
+    ncclAllReduce(c->scal, c->scal, 1, ncclFloat, ncclMin, c->comm, s);
+    cudaMemcpyAsync(&v, c->scal, 4, cudaMemcpyDeviceToHost, s);
+    if (finish(dist, ctx, "mailbox agreement timeout") < 0) return -1;
+    if (v < 1.f) {   /* somebody could not map its successor: NCCL hops everywhere */
+        ptc_mailbox_close(c->peer_box);
+        ptc_mailbox_free(c->box);
+        c->peer_box = c->box = NULL;
+        return 0;
+    }
+    c->ctr = (unsigned *)ptc_alloc(pc, 2 * sizeof(unsigned));
+    c->hop_err = (int *)ptc_alloc(pc, sizeof(int));
+    cudaMemsetAsync(c->ctr, 0, 2 * sizeof(unsigned), s);
+    cudaMemsetAsync(c->hop_err, 0, sizeof(int), s);
+    c->p2p = 1;
+    return finish(dist, ctx, "mailbox setup timeout");
+}
+
+/* A decode hop wait that ran out on the GPU (after the stream finished). */
+static int hop_failed(pt_dist_t *dist, pt_context_t *ctx) {
+    dist_comm_t *c = comm_of(dist);
+    if (!c->p2p) return 0;
+    int e = 0;
+    cudaMemcpyAsync(&e, c->hop_err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)ptc_stream(ctx->dev->ctx));
+    cudaStreamSynchronize((cudaStream_t)ptc_stream(ctx->dev->ctx));
+    if (e) fprintf(stderr, "R%d FAIL: decode hop wait expired\n", dist->rank);
+    return e;
+}
 
 static int join(pt_dist_t *dist, pt_context_t *ctx) {
     if (dist->comm) return 0;
@@ -190,6 +255,7 @@ static int join(pt_dist_t *dist, pt_context_t *ctx) {
     c->rbuf = (float *)ptc_alloc(ctx->dev->ctx, (size_t)(1 + c->dim) * 4);
     c->scal = (float *)ptc_alloc(ctx->dev->ctx, 256);
     dist->comm = c;
+    if (setup_p2p(dist, ctx) < 0) return -1;
     return 0;
 }
 
@@ -215,7 +281,9 @@ int pt_dist_setup_ctx(pt_dist_t *dist, pt_context_t *ctx, const pt_shard_info_t 
 void pt_dist_free(pt_dist_t *dist) {
     dist_comm_t *c = comm_of(dist);
     if (!c) return;
-    ncclCommDestroy(c->comm);
+    ptc_mailbox_close(c->peer_box);
+    ptc_mailbox_free(c->box);
+    if (c->comm) ncclCommDestroy(c->comm);
     free(c);
     dist->comm = NULL;
 }
@@ -225,6 +293,11 @@ void pt_dist_set_verbose(pt_dist_t *dist, int verbose) {
 }
 
 void pt_dist_reset_links(pt_dist_t *dist) { (void)dist; }
+
+int pt_dist_transport(const pt_dist_t *dist) {
+    const dist_comm_t *c = (const dist_comm_t *)dist->comm;
+    return c ? c->p2p : -1;
+}
 
 /* Wait for the stream with the dist deadline; abort the communicator on expiry. */
 static int finish(pt_dist_t *dist, pt_context_t *ctx, const char *what) {
@@ -278,9 +351,6 @@ int pt_dist_allreduce_grads_avg(pt_context_t *ctx, pt_dist_t *dist) {
 
 /* ---- decode ------------------------------------------------------------------ */
 
-static int next_rank(const pt_dist_t *d) { return (d->rank + 1) % d->world_size; }
-static int prev_rank(const pt_dist_t *d) { return (d->rank + d->world_size - 1) % d->world_size; }
-
 /* Enqueue one position's hop sequence for this rank (no host sync). For the
  * head rank in device-loop mode the embedding reads the token from the
  * device and the head advances position/token on the device. */
@@ -291,6 +361,28 @@ static void enqueue_position(pt_dist_t *dist, pt_context_t *ctx, int host_token,
     const size_t msg = (size_t)(1 + c->dim);
     float *x = ptc_decoder_x_dev(dec);
     int *pos_dev = ptc_decoder_pos_dev(dec);
+    if (c->p2p) {
+        ptc_ctx *pc = ctx->dev->ctx;
+        /* GPU-side bound of one hop wait: the dist timeout, at most 60 s (the
+         * host's deadline still bounds the whole call) */
+        const long long tmo = (long long)(timeout_of(dist) < 60000 ? timeout_of(dist) : 60000) * 1000000LL;
+        if (dist->has_embed && dist->has_head) {
+            if (devloop) {
+                ptc_decoder_enqueue_embed_dev(dec);
+            } else {
+                cudaMemcpyAsync(pos_dev, &host_pos, 4, cudaMemcpyHostToDevice, s);
+                ptc_decoder_enqueue_embed(dec, host_token);
+            }
+            ptc_hop_send(pc, x, pos_dev, c->peer_box, c->ctr, c->dim);
+            ptc_hop_recv(pc, c->box, x, NULL, c->ctr + 1, c->dim, c->hop_err, tmo);
+            ptc_decoder_enqueue_head(dec);
+        } else {
+            ptc_hop_recv(pc, c->box, x, pos_dev, c->ctr + 1, c->dim, c->hop_err, tmo);
+            ptc_decoder_enqueue_layers_devpos(dec, dist->l_start, dist->l_end);
+            ptc_hop_send(pc, x, pos_dev, c->peer_box, c->ctr, c->dim);
+        }
+        return;
+    }
     if (dist->has_embed && dist->has_head) {
         if (devloop) {
             ptc_decoder_enqueue_embed_dev(dec);
@@ -327,6 +419,7 @@ int pt_dist_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token) {
     enqueue_position(dist, ctx, token, ctx->pos, 0);
     int next = 0;
     if (finish(dist, ctx, "dist forward recv timeout") < 0) return -1;
+    if (hop_failed(dist, ctx)) return -1;
     if (dist->has_embed && dist->has_head) {
         next = ptc_decoder_fetch_next(ctx->dev->dec, ctx->sync_logits ? ctx->state.logits : NULL);
         ctx->pos++;
@@ -348,6 +441,7 @@ int pt_dist_generate_greedy(pt_context_t *ctx, pt_dist_t *dist, const int *promp
     if (dist->has_embed && dist->has_head) ptc_decoder_generate_begin(dec, prompt, n_prompt);
     for (int p = 0; p < n_pos; p++) enqueue_position(dist, ctx, 0, 0, 1);
     if (finish(dist, ctx, "dist generate timeout") < 0) return -1;
+    if (hop_failed(dist, ctx)) return -1;
     if (dist->has_embed && dist->has_head) {
         ptc_decoder_read_tokens(dec, out_tokens, n_pos);
         ctx->pos = n_pos;

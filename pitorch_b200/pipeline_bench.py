@@ -78,7 +78,9 @@ def run(args, rank, world):
     n_local = int(pipe.ctx.cfg.n_layers)
     per_layer = (L.ptc_decoder_launches_per_step(dec) - (1 if pipe.is_head else 0)) // n_local if n_local else 0
     per_layer = int(pipe.max_over_ranks(float(per_layer)))
-    launches = seq * (per_layer * nl + 2)
+    p2p = L.pt_dist_transport(C.byref(pipe.dist)) == 1
+    # plus, with the NVLink hop transport, one send and one receive kernel per rank
+    launches = seq * (per_layer * nl + 2 + (2 * world if p2p else 0))
     hbm, src = _bench.peaks()
     mean_bytes = float(np.mean([_bench.decode_bytes_per_token(cfg, p) for p in range(seq)]))
     step_gbs = mean_bytes * seq / (ms_step / 1000.0) / 1e9
@@ -92,6 +94,8 @@ def run(args, rank, world):
                                    f"layer pipeline over {world} GPUs",
                        "model": model, "global_batch": 1, "seq_len": seq,
                        "parallelism": f"pp{world} (last rank: embedding + classifier)",
+                       "hop_transport": "peer stores over NVLink (CUDA IPC mailboxes)" if p2p
+                                        else "NCCL send/recv",
                        "l2_policy": "weights > L2 per rank at N<=2; shards of ~57-113 MB at N>=4"},
             "e2e": {"value": seq / (e2e_ms / 1000.0), "unit": "tokens/s",
                     "api": "pt_dist_forward_step per position",

@@ -39,7 +39,9 @@ def _worker(rank, world, port, task, q):
         os.environ["PT_DIST_PORT"] = str(port)
         os.environ["PT_DIST_TIMEOUT_MS"] = "60000"
         from pitorch_b200 import api, synth
-        name, kind = task
+        name, kind = task[:2]
+        if len(task) > 2:
+            os.environ["PT_DIST_P2P"] = task[2]
         cfg = synth.CONFIGS[name]
         blob = synth.make_blob(cfg)
         if kind == "decode":
@@ -76,11 +78,15 @@ def run_ranks(world, task):
     return out
 
 
-@pytest.mark.parametrize("name,world", [("tiny", 2), ("stories15M", 2), ("stories15M", 4), ("stories110M", 4)])
-def test_pipeline_decode_matches_reference(ptlib, name, world):
+@pytest.mark.parametrize("name,world,transport", [("tiny", 2, "1"), ("stories15M", 2, "1"), ("stories15M", 2, "0"),
+                                                  ("stories15M", 4, "1"), ("stories110M", 4, "1"),
+                                                  ("stories110M", 4, "0")])
+def test_pipeline_decode_matches_reference(ptlib, name, world, transport):
+    """transport "1": decode hops as peer stores over NVLink (ptc_hop_*, the
+    default); "0": NCCL send/recv (PT_DIST_P2P=0)."""
     if n_gpus() < world:
         pytest.skip(f"needs {world} GPUs")
-    out = run_ranks(world, (name, "decode"))
+    out = run_ranks(world, (name, "decode", transport))
     g = golden(f"decode_{name}.npz")
     n = int(g["n_pos"])
     head = [o for o in out if o[1]]
