@@ -105,9 +105,17 @@ void pt_generate_greedy(pt_context_t *ctx, const int *prompt, int n_prompt,
 void pt_sync_weights(pt_context_t *ctx);
 /* Fill ctx->grads._mem from the device gradients of the last step. */
 void pt_sync_grads(pt_context_t *ctx);
+/* Checkpoint (no reference counterpart: the Pi build keeps weights only in
+ * RAM): bring the device weights back (pt_sync_weights) and write the
+ * context's model image -- the llama2.c .bin, or the SHRD shard for a
+ * pt_pi_init_shard context -- to path, loadable again with pt_read_file +
+ * pt_pi_init / pt_pi_init_shard. Returns 0, or -1 when the file cannot be
+ * written. */
+int pt_save_weights(pt_context_t *ctx, const char *path);
 
 /* The device context's C-ABI handles (see ptc.h). */
 struct ptc_ctx *pt_ptc_ctx(pt_context_t *ctx);
 struct ptc_decoder *pt_ptc_decoder(pt_context_t *ctx);
+struct ptc_trainer *pt_ptc_trainer(pt_context_t *ctx);   /* NULL without max_T > 0 */
 
 #endif

@@ -56,6 +56,7 @@ pt_dist_result_t pt_dist_train_step(pt_context_t *ctx, pt_dist_t *dist,
  * -1 on a communication timeout. */
 int pt_dist_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token);
 
+
 /* ---- pitorch_b200 additions ---- */
 
 /* Device-resident pipelined greedy decode of n_pos positions on every rank

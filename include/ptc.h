@@ -259,6 +259,15 @@ float *ptc_trainer_grads(ptc_trainer *t);
 float *ptc_trainer_residual(ptc_trainer *t, int l);
 float *ptc_trainer_dres(ptc_trainer *t);
 
+/* Microbatch activation sets for pipeline schedules (GPipe): n sets in all,
+ * each a full forward state for max_T tokens; ptc_trainer_select makes the
+ * forward/backward calls use set m (gradients and weights are shared, so
+ * backward calls accumulate). ptc_trainer_dres_save is the selected set's
+ * [T, dim] buffer for keeping its residual gradient across a schedule. */
+void ptc_trainer_set_microbatches(ptc_trainer *t, int n);
+void ptc_trainer_select(ptc_trainer *t, int m);
+float *ptc_trainer_dres_save(ptc_trainer *t);
+
 /* ---- CUDA event timing on a context's stream ----------------------------- */
 typedef struct ptc_timer ptc_timer;
 ptc_timer *ptc_timer_create(ptc_ctx *c);

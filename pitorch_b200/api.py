@@ -131,8 +131,21 @@ def declare(L):
     _sig(L, "pt_generate_greedy", None, ctx, i32p, C.c_int, C.c_int, i32p)
     _sig(L, "pt_sync_weights", None, ctx)
     _sig(L, "pt_sync_grads", None, ctx)
+    _sig(L, "pt_save_weights", C.c_int, ctx, C.c_char_p)
     _sig(L, "pt_ptc_ctx", vp, ctx)
     _sig(L, "pt_ptc_decoder", vp, ctx)
+    _sig(L, "pt_ptc_trainer", vp, ctx)
+    for name in ("ptc_trainer_zero_grads", "ptc_trainer_fwd_embed", "ptc_trainer_bwd_head",
+                 "ptc_trainer_bwd_embed", "ptc_trainer_sync"):
+        _sig(L, name, None, vp)
+    _sig(L, "ptc_trainer_fwd_head", C.c_float, vp)
+    _sig(L, "ptc_trainer_set_tokens", None, vp, i32p, C.c_int)
+    _sig(L, "ptc_trainer_fwd_layers", None, vp, C.c_int, C.c_int)
+    _sig(L, "ptc_trainer_bwd_layers", None, vp, C.c_int, C.c_int)
+    _sig(L, "ptc_trainer_sgd_layers", None, vp, C.c_float, C.c_int, C.c_int)
+    _sig(L, "ptc_trainer_sgd_head", None, vp, C.c_float)
+    _sig(L, "ptc_trainer_set_microbatches", None, vp, C.c_int)
+    _sig(L, "ptc_trainer_select", None, vp, C.c_int)
     _sig(L, "pt_load_config", None, P(pt_config_t), C.c_void_p)
     _sig(L, "pt_load_weights", None, P(pt_weights_t), P(pt_config_t), C.c_void_p)
     _sig(L, "pt_file_size", C.c_uint, C.c_void_p)

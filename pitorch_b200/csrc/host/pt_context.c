@@ -237,6 +237,7 @@ void pt_free(pt_context_t *ctx) {
 
 struct ptc_ctx *pt_ptc_ctx(pt_context_t *ctx) { return ctx->dev ? ctx->dev->ctx : NULL; }
 struct ptc_decoder *pt_ptc_decoder(pt_context_t *ctx) { return ctx->dev ? ctx->dev->dec : NULL; }
+struct ptc_trainer *pt_ptc_trainer(pt_context_t *ctx) { return ctx->dev ? ctx->dev->trainer : NULL; }
 
 /* ---- decode ------------------------------------------------------------------ */
 

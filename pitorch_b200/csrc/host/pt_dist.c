@@ -495,3 +495,4 @@ pt_dist_result_t pt_dist_train_step(pt_context_t *ctx, pt_dist_t *dist, const in
     (void)ring_sync_ctx;
     return res;
 }
+

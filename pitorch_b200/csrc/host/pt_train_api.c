@@ -8,6 +8,7 @@
  * from the pt_activations_t / pt_grads_t / pt_backward_buf_t address.
  * ctx->grads._mem is a host mirror filled by pt_sync_grads().
  */
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -102,6 +103,17 @@ void pt_sync_weights(pt_context_t *ctx) {
     /* everything after the header: tensors are updated in place on the device */
     size_t hdr = d->is_shard ? 56 : 28;
     ptc_d2h(d->ctx, (char *)d->host_image + hdr, d->dev_image + hdr, d->image_bytes - hdr);
+}
+
+int pt_save_weights(pt_context_t *ctx, const char *path) {
+    struct pt_device *d = ctx->dev;
+    if (!d || !d->host_image) return -1;
+    pt_sync_weights(ctx);
+    FILE *f = fopen(path, "wb");
+    if (!f) return -1;
+    const size_t n = fwrite(d->host_image, 1, d->image_bytes, f);
+    const int rc = fclose(f);
+    return (n == d->image_bytes && rc == 0) ? 0 : -1;
 }
 
 void pt_sync_grads(pt_context_t *ctx) {

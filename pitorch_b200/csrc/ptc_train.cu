@@ -411,6 +411,17 @@ __global__ void k_tr_sgd(float *w, const float *g, size_t n, float lr) {
 // ---------------------------------------------------------------------------
 // Trainer object
 // ---------------------------------------------------------------------------
+// One microbatch's forward state: everything the backward of that microbatch
+// reads. The trainer works on the selected set (its fields below mirror it).
+struct ActSet {
+    float *res, *res_att, *xb_att, *q, *k, *v, *att, *att_out, *xb_ffn, *hb, *hb2, *x_final, *logits;
+    int *tokens;
+    float *loss_rows, *loss;
+    float *dres_save;   // this microbatch's d_res, kept across a pipeline schedule
+    int T;
+};
+constexpr int PTC_MAX_MICROBATCHES = 16;
+
 struct ptc_trainer {
     ptc_ctx *ctx;
     cudaStream_t s;
@@ -432,7 +443,25 @@ struct ptc_trainer {
     size_t n_params;
     float *g_emb, *g_rms_att, *g_wq, *g_wk, *g_wv, *g_wo, *g_rms_ffn, *g_w1, *g_w2, *g_w3, *g_rms_final,
         *g_wcls;
+    // microbatch activation sets (set 0 = the buffers above at creation)
+    ActSet sets[PTC_MAX_MICROBATCHES];
+    int n_sets, cur;
 };
+
+static void save_set(ptc_trainer *tr, int i) {
+    ActSet &a = tr->sets[i];
+    a.res = tr->res; a.res_att = tr->res_att; a.xb_att = tr->xb_att; a.q = tr->q; a.k = tr->k; a.v = tr->v;
+    a.att = tr->att; a.att_out = tr->att_out; a.xb_ffn = tr->xb_ffn; a.hb = tr->hb; a.hb2 = tr->hb2;
+    a.x_final = tr->x_final; a.logits = tr->logits; a.tokens = tr->tokens; a.loss_rows = tr->loss_rows;
+    a.loss = tr->loss; a.T = tr->T;
+}
+static void load_set(ptc_trainer *tr, int i) {
+    const ActSet &a = tr->sets[i];
+    tr->res = a.res; tr->res_att = a.res_att; tr->xb_att = a.xb_att; tr->q = a.q; tr->k = a.k; tr->v = a.v;
+    tr->att = a.att; tr->att_out = a.att_out; tr->xb_ffn = a.xb_ffn; tr->hb = a.hb; tr->hb2 = a.hb2;
+    tr->x_final = a.x_final; tr->logits = a.logits; tr->tokens = a.tokens; tr->loss_rows = a.loss_rows;
+    tr->loss = a.loss; tr->T = a.T;
+}
 
 static int blocks_for(size_t n, int threads, int n_sm) {
     size_t b = (n + threads - 1) / threads;
@@ -524,6 +553,10 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
     if (has_head && !untied && !has_embed) PTC_FATAL("tied classifier needs the embedding on the same rank");
     PTC_CHECK(cudaMemsetAsync(tr->g_mem, 0, n * 4, tr->s));
     PTC_CHECK(cudaStreamSynchronize(tr->s));
+    tr->n_sets = 1;
+    tr->cur = 0;
+    save_set(tr, 0);
+    tr->sets[0].dres_save = A(T * D);
     return tr;
 }
 
@@ -540,6 +573,49 @@ extern "C" float *ptc_trainer_residual(ptc_trainer *tr, int l) {
     return tr->res + (size_t)l * tr->T * tr->D;
 }
 extern "C" float *ptc_trainer_dres(ptc_trainer *tr) { return tr->d_res; }
+
+// Microbatch activation sets for pipeline schedules: n sets in all (set 0
+// exists from creation), each a full copy of the forward state for max_T
+// tokens. Selecting a set makes the forward/backward calls use it.
+extern "C" void ptc_trainer_set_microbatches(ptc_trainer *tr, int n) {
+    if (n < 1 || n > PTC_MAX_MICROBATCHES) PTC_FATAL("microbatches %d outside [1, %d]", n, PTC_MAX_MICROBATCHES);
+    save_set(tr, tr->cur);
+    const size_t T = tr->maxT, D = tr->D, H = tr->H, L = tr->L, K = tr->K, V = tr->V, nh = tr->nh;
+    auto A = [&](size_t e) { return (float *)ptc_alloc(tr->ctx, (e ? e : 1) * 4); };
+    for (int i = tr->n_sets; i < n; i++) {
+        ActSet &a = tr->sets[i];
+        a.res = A((L + 1) * T * D);
+        a.res_att = A(L * T * D);
+        a.xb_att = A(L * T * D);
+        a.q = A(L * T * D);
+        a.k = A(L * T * K);
+        a.v = A(L * T * K);
+        a.att = A(L * nh * T * T);
+        a.att_out = A(L * T * D);
+        a.xb_ffn = A(L * T * D);
+        a.hb = A(L * T * H);
+        a.hb2 = A(L * T * H);
+        a.x_final = A(T * D);
+        a.logits = tr->has_head ? A(T * V) : nullptr;
+        a.tokens = (int *)ptc_alloc(tr->ctx, T * 4);
+        a.loss_rows = A(T);
+        a.loss = A(1);
+        a.dres_save = A(T * D);
+        a.T = tr->T;
+    }
+    if (n > tr->n_sets) tr->n_sets = n;
+}
+
+extern "C" void ptc_trainer_select(ptc_trainer *tr, int m) {
+    if (m < 0 || m >= tr->n_sets) PTC_FATAL("microbatch %d outside [0, %d)", m, tr->n_sets);
+    if (m == tr->cur) return;
+    save_set(tr, tr->cur);
+    load_set(tr, m);
+    tr->cur = m;
+}
+
+// The selected microbatch's d_res keeping buffer ([T, dim]).
+extern "C" float *ptc_trainer_dres_save(ptc_trainer *tr) { return tr->sets[tr->cur].dres_save; }
 
 static GemmArgs G(int M, int N, int K, const float *A, int lda, bool akc, const float *B, int ldb, bool bkc,
                   float *C, int ldc, int epi) {

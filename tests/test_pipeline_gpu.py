@@ -70,9 +70,17 @@ def run_ranks(world, task):
     ps = [ctx.Process(target=_worker, args=(r, world, port, task, q)) for r in range(world)]
     for p in ps:
         p.start()
-    out = [q.get(timeout=600) for _ in range(world)]
-    for p in ps:
-        p.join(timeout=120)
+    out = []
+    try:
+        for _ in range(world):
+            out.append(q.get(timeout=240))
+    finally:
+        for p in ps:   # a rank that died leaves the others waiting: end them
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=30)
+    assert len(out) == world, f"only {len(out)} of {world} ranks reported"
     for r, head, a, b in out:
         assert head is not None, f"rank {r} failed: {a}"
     return out
@@ -106,3 +114,4 @@ def test_pipeline_training_matches_single_gpu(ptlib, world):
     losses = np.array(head[0][2], dtype=np.float64)
     ref = g["losses"][:3].astype(np.float64)
     assert np.all(np.abs(losses - ref) <= 1e-4 * np.abs(ref)), (losses, ref)
+

@@ -115,3 +115,88 @@ def test_staged_training_equals_train_step(ptlib):
     assert a.blob() == b.blob()
     a.close()
     b.close()
+
+
+def accumulate_step(ctx, token_mbs, lr):
+    """One accumulated step on one GPU: zero, forward + backward of every
+    microbatch (pt_backward adds into the gradients), then SGD with lr times
+    the mean gradient. Returns the mean loss."""
+    L, c = ctx.L, ctx.ctx
+    L.pt_zero_grads(C.byref(c.grads))
+    total = 0.0
+    for toks in token_mbs:
+        tp = api.ip(toks)
+        T = len(toks)
+        total += L.pt_forward_train(C.byref(c.cfg), C.byref(c.w), C.byref(c.acts), tp, T, None, None)
+        L.pt_backward(C.byref(c.cfg), C.byref(c.w), C.byref(c.grads), C.byref(c.acts), C.byref(c.bb), tp, T,
+                      None, None)
+    L.pt_sgd_update(C.byref(c.w), C.byref(c.grads), C.c_float(lr / len(token_mbs)), C.byref(c.cfg))
+    return total / len(token_mbs)
+
+
+def test_checkpoint_round_trip(ptlib, tmp_path):
+    """pt_save_weights after training writes a .bin that loads into a new
+    context with the trained weights (same logits as the trained context)."""
+    blob = synth.make_blob("tiny")
+    toks = synth.make_tokens(1024, 16)
+    a = api.Context(blob, max_T=16)
+    for _ in range(3):
+        a.train_step(toks, 1e-2)
+    path = str(tmp_path / "tiny_trained.bin")
+    assert ptlib.pt_save_weights(C.byref(a.ctx), path.encode()) == 0
+    saved = open(path, "rb").read()
+    assert saved == a.blob()
+    assert saved != blob
+    b = api.Context(saved)
+    for p, t in enumerate([1, 5, 9, 13]):
+        a.L.pt_forward_step(C.byref(a.ctx), t)
+        la = np.ctypeslib.as_array(a.ctx.state.logits, shape=(1024,)).copy()
+        b.L.pt_forward_step(C.byref(b.ctx), t)
+        lb = np.ctypeslib.as_array(b.ctx.state.logits, shape=(1024,)).copy()
+        assert rel_err(lb, la) <= 1e-5, p
+    a.close()
+    b.close()
+
+
+def test_microbatch_sets_match_accumulation(ptlib):
+    """The trainer's microbatch activation sets (ptc_trainer_set_microbatches
+    / ptc_trainer_select), driven in the GPipe order on one GPU -- every
+    forward, then every backward in reverse -- equal plain gradient
+    accumulation (accumulate_step): mean losses of 3 steps within 1e-4."""
+    L = ptlib
+    cfg = synth.CONFIGS["stories15M"]
+    T, n_mb, lr = 64, 4, 1e-2
+    mbs = [synth.make_tokens(cfg[5], T, seed=100 + m) for m in range(n_mb)]
+    ref_ctx = api.Context(synth.make_blob(cfg), max_T=T)
+    ref = np.array([accumulate_step(ref_ctx, mbs, lr) for _ in range(3)], dtype=np.float64)
+    ref_ctx.close()
+    ctx = api.Context(synth.make_blob(cfg), max_T=T)
+    tr = L.pt_ptc_trainer(C.byref(ctx.ctx))
+    nl = cfg[2]
+    L.ptc_trainer_set_microbatches(tr, n_mb)
+    for m in range(n_mb):
+        L.ptc_trainer_select(tr, m)
+        L.ptc_trainer_set_tokens(tr, api.ip(mbs[m]), T)
+    got = []
+    for _ in range(3):
+        L.ptc_trainer_zero_grads(tr)
+        total = 0.0
+        for m in range(n_mb):
+            L.ptc_trainer_select(tr, m)
+            L.ptc_trainer_fwd_embed(tr)
+            L.ptc_trainer_fwd_layers(tr, 0, nl)
+            total += L.ptc_trainer_fwd_head(tr)
+        for m in reversed(range(n_mb)):
+            L.ptc_trainer_select(tr, m)
+            L.ptc_trainer_bwd_head(tr)
+            L.ptc_trainer_bwd_layers(tr, 0, nl)
+            L.ptc_trainer_bwd_embed(tr)
+        L.ptc_trainer_sgd_head(tr, C.c_float(lr / n_mb))
+        L.ptc_trainer_sgd_layers(tr, C.c_float(lr / n_mb), 0, nl)
+        L.ptc_trainer_sync(tr)
+        got.append(total / n_mb)
+    L.ptc_trainer_select(tr, 0)
+    ctx.close()
+    got = np.array(got)
+    assert np.all(np.abs(got - ref) <= 1e-4 * np.abs(ref)), (got, ref)
+    assert ref[2] < ref[0]
