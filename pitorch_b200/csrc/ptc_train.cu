@@ -695,7 +695,9 @@ extern "C" void ptc_trainer_fwd_layers(ptc_trainer *tr, int l0, int l1) {
 }
 
 // pt_forward_train_head (pt_train.c:1063-1099): returns the loss (synchronises).
-extern "C" float ptc_trainer_fwd_head(ptc_trainer *tr) {
+// Head forward with the loss copied to pinned memory asynchronously: the
+// caller reads tr->loss_host after synchronising the stream.
+static void fwd_head_enqueue(ptc_trainer *tr) {
     if (!tr->has_head) PTC_FATAL("trainer has no head");
     const int T = tr->T, D = tr->D, V = tr->V;
     cudaStream_t s = tr->s;
@@ -706,7 +708,11 @@ extern "C" float ptc_trainer_fwd_head(ptc_trainer *tr) {
     ptc::k_tr_loss_sum<<<1, 32, 0, s>>>(tr->loss_rows, T - 1, tr->loss);
     PTC_CHECK(cudaGetLastError());
     PTC_CHECK(cudaMemcpyAsync(tr->loss_host, tr->loss, 4, cudaMemcpyDeviceToHost, s));
-    PTC_CHECK(cudaStreamSynchronize(s));
+}
+
+extern "C" float ptc_trainer_fwd_head(ptc_trainer *tr) {
+    fwd_head_enqueue(tr);
+    PTC_CHECK(cudaStreamSynchronize(tr->s));
     return *tr->loss_host;
 }
 
@@ -830,14 +836,14 @@ extern "C" float ptc_trainer_step(ptc_trainer *tr, const int *tokens, int T, flo
     ptc_trainer_zero_grads(tr);
     ptc_trainer_fwd_embed(tr);
     ptc_trainer_fwd_layers(tr, 0, tr->L);
-    const float loss = ptc_trainer_fwd_head(tr);
+    fwd_head_enqueue(tr);   // the loss is read once the whole step ran
     ptc_trainer_bwd_head(tr);
     ptc_trainer_bwd_layers(tr, 0, tr->L);
     ptc_trainer_bwd_embed(tr);
     ptc_trainer_sgd_head(tr, lr);
     ptc_trainer_sgd_layers(tr, lr, 0, tr->L);
     PTC_CHECK(cudaStreamSynchronize(tr->s));
-    return loss;
+    return *tr->loss_host;
 }
 
 extern "C" void ptc_trainer_sync(ptc_trainer *tr) { PTC_CHECK(cudaStreamSynchronize(tr->s)); }
