@@ -483,7 +483,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         return run_reference(args, rank)
-    if world > 1 or args.gpus > 1:
+    if world > 1:   # torchrun: one rank per GPU
         from pitorch_b200 import pipeline_bench
         return pipeline_bench.run(args, rank, world)
     return run_single(args)
