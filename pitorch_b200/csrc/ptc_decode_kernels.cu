@@ -655,17 +655,17 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     rmsnorm_pre<NV>(xr, gr, dim);
-    // The input is consumed (rmsnorm; the residual registers are forced
-    // below): take the ticket now, look at it when the CTA ends.
+    // The input is consumed by rmsnorm; the residual registers are forced
+    // here. Once the barrier below has passed, every thread of the CTA has
+    // done so: the CTA then takes its ticket, looked at when it ends.
 #pragma unroll
     for (int r = 0; r < RV; r++) asm volatile("" ::"f"(res[r].x), "f"(res[r].y), "f"(res[r].z), "f"(res[r].w));
-    __syncthreads();
-    unsigned ticket = 0u;
-    if (a.xclear && tid == FF_THREADS - 1) ticket = atomicAdd(&m.tickets[1], 1u);
 
     // A failed wait is recorded in m.err; the CTA then skips its products
     // but still takes part in the ticket.
     bool ok = __syncthreads_and(mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT));
+    unsigned ticket = 0u;
+    if (a.xclear && tid == FF_THREADS - 1) ticket = atomicAdd(&m.tickets[1], 1u);
     if (ok)
         for (int j = warp; j < nj; j += NW) {
             const float h1 = smem_row_dot<NV>(w1s + (size_t)j * dim, xr, c4, lane);
@@ -757,7 +757,6 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     __shared__ __align__(16) float s_att[AT_MAX_HD];
     __shared__ __align__(16) float s_res[AT_MAX_OUT];
     __shared__ float s_sc[AT_ROUND];
-    __shared__ float s_stat[2];
     __shared__ int s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -946,33 +945,26 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             if (js < n && sub == 0) s_sc[js] = __fmul_rn(acc, scale);
         }
         __syncthreads();
-        if (warp == 0) {
-            float mx = -3.4028235e+38f;
-            for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_sc[j]);
-            mx = warp_max(mx);
-            const float m_new = fmaxf(m_run, mx);
-            float sum = 0.f;
-            for (int j = lane; j < n; j += 32) {
-                const float e = pt_expf(__fsub_rn(s_sc[j], m_new));
-                s_sc[j] = e;
-                sum += e;
-            }
-            sum = warp_sum(sum);
-            if (lane == 0) {
-                const float alpha = pt_expf(__fsub_rn(m_run, m_new));
-                s_stat[0] = m_new;
-                s_stat[1] = alpha;
-                l_run = fmaf(l_run, alpha, sum);
-            }
-        }
-        __syncthreads();
+        // Every warp reduces the round's scores itself (same lanes, same
+        // order, so all threads hold identical values): no serial section
+        // and no broadcast through shared memory.
+        float mx = -3.4028235e+38f;
+        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_sc[j]);
+        mx = warp_max(mx);
+        const float m_new = fmaxf(m_run, mx);
+        float sum = 0.f;
+        for (int j = lane; j < n; j += 32) sum += pt_expf(__fsub_rn(s_sc[j], m_new));
+        sum = warp_sum(sum);
+        const float alpha = pt_expf(__fsub_rn(m_run, m_new));
+        l_run = fmaf(l_run, alpha, sum);
+        m_run = m_new;
         if (grp < ngrp) {
             float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int k = 0; k < VP; k++) {
                 const int j = grp + ngrp * k;
                 if (j < n) {
-                    const float e = s_sc[j];
+                    const float e = pt_expf(__fsub_rn(s_sc[j], m_new));
                     o.x = fmaf(e, vpre[k].x, o.x); o.y = fmaf(e, vpre[k].y, o.y);
                     o.z = fmaf(e, vpre[k].z, o.z); o.w = fmaf(e, vpre[k].w, o.w);
                 }
@@ -980,13 +972,12 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             reinterpret_cast<float4 *>(s_o)[grp * hd4 + d4] = o;
         }
         __syncthreads();
-        m_run = s_stat[0];
         if (tid < hd) {
             float o = 0.f;
             for (int g = 0; g < ngrp; g++) o += s_o[g * hd + tid];
-            o_run = fmaf(o_run, s_stat[1], o);
+            o_run = fmaf(o_run, alpha, o);
         }
-        __syncthreads();   // s_sc, s_o, s_stat reused by the next round
+        if (rt0 + AT_ROUND < t1) __syncthreads();   // s_sc and s_o are reused by the next round
     }
     // partial of this CTA -> slot r of every CTA
     if (tid < hd)
