@@ -711,19 +711,19 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
 // k_attn_fused: the attention half of one layer (llama2.c:229-277) as one
 // kernel of n_heads clusters of AC CTAs. Cluster h does, for head h:
 //   1. rmsnorm(x) and its share of the head's 3*hd q/k/v rows (held in shared
-//      memory, bulk-copied before griddepcontrol.wait); every CTA sends its
-//      raw results to all CTAs of the cluster through distributed shared
-//      memory; cluster barrier;
-//   2. RoPE on q and k (every CTA, same arithmetic); CTA 0 writes the new
-//      K/V row of `pos` into the cache;
-//   3. attention over its chunk of positions [0, pos] (K/V rows of earlier
+//      memory, bulk-copied before griddepcontrol.wait), computed as row
+//      pairs so each warp applies RoPE to its q/k pairs; every CTA sends its
+//      results to all CTAs of the cluster through distributed shared memory;
+//      cluster barrier;
+//   2. attention over its chunk of positions [0, pos] (K/V rows of earlier
 //      positions were loaded into registers before the wait), kept as an
 //      online-softmax partial (max, sum, unnormalised output); partials are
 //      exchanged through distributed shared memory; cluster barrier;
-//   4. every CTA merges the AC partials into the head's attention output and
+//   3. every CTA merges the AC partials into the head's attention output and
 //      multiplies it by its slice of wo (rows [o0, o1), columns of head h),
 //      adding the result into the zeroed output with vector reductions; the
-//      cluster of head 0 also adds the residual x.
+//      cluster of head 0 also adds the residual x; CTA 0 writes the new K/V
+//      row of `pos` into the cache.
 // The only grid-wide dependency is the output sum at L2, so the layer's
 // attention costs one kernel boundary instead of three.
 // ---------------------------------------------------------------------------
@@ -732,6 +732,7 @@ constexpr int AT_THREADS = 256;
 constexpr int AT_MAX_HD = 64;
 constexpr int AT_ROUND = 64;          // positions per attention round (4 threads each)
 constexpr int AT_MAX_OUT = 256;       // wo rows per CTA (dim <= 2048)
+constexpr int AT_PAIRS = 2;           // q/k/v row pairs per warp (3*hd/AC <= 32 rows per CTA)
 
 struct AttnArgs {
     const float *xin;  // layer input; null: the embedding row of step->tok (layer 0)
@@ -824,8 +825,15 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     float4 xr[NV], gr[NV];
     load_gain<NV>(gr, m.rms_att + (size_t)l * dim, c4, lane);
     // RoPE factors of pos for the pair this thread rotates (tid < hd)
-    float2 rcs = make_float2(1.f, 0.f);
-    if (tid < hd) rcs = __ldg(m.rope + (size_t)pos * (hd / 2) + (tid % (hd / 2)));
+    // RoPE factors of pos for the q/k row pairs this warp computes (each warp
+    // owns whole pairs, so it rotates them before the exchange)
+    float2 rcs[AT_PAIRS];
+#pragma unroll
+    for (int k = 0; k < AT_PAIRS; k++) {
+        const int pr = q0 + 2 * warp + 2 * NW * k;
+        rcs[k] = (pr < q1 && pr < 2 * hd) ? __ldg(m.rope + (size_t)pos * (hd / 2) + (pr % hd) / 2)
+                                          : make_float2(1.f, 0.f);
+    }
     const float *xsrc = a.xin ? a.xin : m.emb + (size_t)__ldcg(&m.step->tok) * dim;
     if (!a.xin) load_act<NV>(xr, xsrc, c4, lane);
     // every CTA of the cluster runs before any remote store (no memory
@@ -838,11 +846,27 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             reinterpret_cast<float4 *>(s_res)[i] = __ldcg(reinterpret_cast<const float4 *>(xsrc + o0) + i);
     rmsnorm_pre<NV>(xr, gr, dim);
 
-    // 1. q/k/v rows -> every CTA's s_qkv
+    // 1. q/k/v row pairs, RoPE on the q and k pairs (llama2.c:238-245), then
+    //    to every CTA's s_qkv
     bool bad = !mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT);
-    for (int j = q0 + warp; j < q1; j += NW) {
-        const float v = smem_row_dot<NV>(stage + (size_t)(j - q0) * dim, xr, c4, lane);
-        if (lane < AC) cluster.map_shared_rank(s_qkv, lane)[j] = v;
+#pragma unroll
+    for (int k = 0; k < AT_PAIRS; k++) {
+        const int pr = q0 + 2 * warp + 2 * NW * k;
+        if (pr < q1) {
+            float v0 = smem_row_dot<NV>(stage + (size_t)(pr - q0) * dim, xr, c4, lane);
+            float v1 = smem_row_dot<NV>(stage + (size_t)(pr + 1 - q0) * dim, xr, c4, lane);
+            if (pr < 2 * hd) {
+                const float cs = rcs[k].x, sn = rcs[k].y;
+                const float a0 = v0, a1 = v1;
+                v0 = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
+                v1 = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
+            }
+            if (lane < AC) {
+                float *dst = cluster.map_shared_rank(s_qkv, lane);
+                dst[pr] = v0;
+                dst[pr + 1] = v1;
+            }
+        }
     }
     cluster.sync();
     // Every thread of this CTA has consumed the layer input (rmsnorm, the
@@ -876,19 +900,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
     }
     cp_async_commit();
-    // 2. RoPE (llama2.c:238-245) in place on q and k
-    if (tid < hd) {
-        const int is_k = tid >= hd / 2;
-        const int i = 2 * (tid - (is_k ? hd / 2 : 0));
-        float *v = s_qkv + (is_k ? hd : 0) + i;
-        const float cs = rcs.x, sn = rcs.y;
-        const float a0 = v[0], a1 = v[1];
-        v[0] = __fsub_rn(__fmul_rn(a0, cs), __fmul_rn(a1, sn));
-        v[1] = __fadd_rn(__fmul_rn(a0, sn), __fmul_rn(a1, cs));
-    }
-    __syncthreads();
-
-    // 3. attention over [t0, t1): online softmax in rounds of AT_ROUND
+    // 2. attention over [t0, t1): online softmax in rounds of AT_ROUND
     const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
     float4 qv[QK];
 #pragma unroll
@@ -990,7 +1002,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
     cluster.sync();
 
-    // 4. merge the AC partials (every output thread, same order in every
+    // 3. merge the AC partials (every output thread, same order in every
     // CTA), then wo
     if (tid < hd) {
         float M = -3.4028235e+38f;
@@ -1191,6 +1203,9 @@ int decode_attn_stage(int dim, int nh, int nkv, int seq) {
     if (nh != nkv || dim % nh) return 0;
     const int hd = dim / nh;
     if (hd > AT_MAX_HD || hd % 4 || dim % (4 * AC) || dim / AC > AT_MAX_OUT || dim > 2048) return 0;
+    // whole row pairs per CTA (RoPE pairs stay in one warp), at most
+    // AT_PAIRS pairs per warp
+    if ((3 * hd) % (2 * AC) || 3 * hd / AC > 2 * AT_PAIRS * (AT_THREADS / 32)) return 0;
     (void)seq;   // positions are processed in rounds: no limit from seq_len
     const int qkv_rows = (3 * hd + AC - 1) / AC;
     const int ngrp = AT_THREADS / (hd / 4);
