@@ -42,8 +42,8 @@ typedef struct {
  * (including the KV cache) is on the GPU; after each forward call `x` and
  * `logits` hold host copies of the device values (logits only when the
  * owning context has sync_logits set). key_cache/value_cache are host
- * buffers of the reference's size kept for API compatibility; the device
- * cache is reset with pt_reset_kv. */
+ * buffers of the reference's size kept for API compatibility (zero, never
+ * written by the library); pt_reset_kv resets the device cache. */
 typedef struct {
     float *x;
     float *xb;
