@@ -348,6 +348,7 @@ struct MvArgs {
     int per_stage;     // items per shared-memory stage
     int l;             // layer
     int from_embedding;
+    int *host_next;    // MV_CLS: pinned host word that also receives the argmax (null: none)
 };
 
 template <int MODE>
@@ -576,6 +577,10 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     const unsigned long long key = atomicAdd(&st->amax, 0ull);
     const int next = argmax_key_index(key);
     st->next = next;
+    if (a.host_next) {   // straight into the host's pinned word: no copy node after the kernel
+        *reinterpret_cast<volatile int *>(a.host_next) = next;
+        __threadfence_system();
+    }
     st->amax = 0ull;
     st->done = 0u;
     if (st->mode == 1 && st->pos < m.seq) {
@@ -1337,9 +1342,10 @@ void launch_layers(const DecodeModel &m, int l0, int l1, bool from_embedding, in
     }
 }
 
-void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s) {
+void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s, int *host_next) {
     MvArgs a = mv_args(m.V, m.dim, 1, 0);
     a.W = m.wcls;
+    a.host_next = host_next;
     PTC_NV_SWITCH(nv_of(m.dim), (launch_mv<NV, MV_CLS>(m, a, n_sm, s)));
 }
 

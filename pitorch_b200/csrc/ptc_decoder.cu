@@ -41,11 +41,11 @@ struct ptc_decoder {
     int loop_pos;          // device-loop mode: next position to decode
 };
 
-static void enqueue_kernels(ptc_decoder *d, cudaStream_t s) {
+static void enqueue_kernels(ptc_decoder *d, cudaStream_t s, int *host_next) {
     const DecodeModel &m = d->m;
     if (d->has_embed && m.L == 0) ptc::launch_embed(m, s);
     ptc::launch_layers(m, 0, m.L, d->has_embed != 0, d->n_sm, s);
-    if (d->has_head) ptc::launch_head(m, d->n_sm, s);
+    if (d->has_head) ptc::launch_head(m, d->n_sm, s, host_next);
 }
 
 static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
@@ -54,9 +54,9 @@ static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
     PTC_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     if (host_io)
         PTC_CHECK(cudaMemcpyAsync(d->m.step, d->io, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
-    enqueue_kernels(d, s);
-    if (host_io && d->has_head)
-        PTC_CHECK(cudaMemcpyAsync(&d->io->next, &d->m.step->next, sizeof(int), cudaMemcpyDeviceToHost, s));
+    // host steps: the classifier's last CTA stores the token into the pinned
+    // io->next itself (4 bytes over PCIe), so the graph ends with the kernel
+    enqueue_kernels(d, s, host_io ? &d->io->next : nullptr);
     PTC_CHECK(cudaStreamEndCapture(s, &g));
     cudaGraphExec_t ge;
     PTC_CHECK(cudaGraphInstantiate(&ge, g, 0));
@@ -291,6 +291,7 @@ extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logit
             PTC_CHECK(cudaMemcpyAsync(&d->io->next, &d->m.step->next, sizeof(int), cudaMemcpyDeviceToHost,
                                       d->stream));
     } else {
+        d->io->next = -1;   // overwritten by the classifier
         PTC_CHECK(cudaGraphLaunch(d->g_host, d->stream));
     }
     if (logits_host && d->has_head) {

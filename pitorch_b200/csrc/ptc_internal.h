@@ -25,7 +25,8 @@ int decode_ffn_rows(int dim, int hidden, int n_sm);
 void launch_block(const DecodeModel &m, int kind, int l, int n_sm, cudaStream_t s);
 int decode_attn_stage(int dim, int nh, int nkv, int seq);
 void build_rope_table(float2 *t, int seq, int hd, cudaStream_t s);
-void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s);
+// host_next: pinned host word that also receives the argmax (or null).
+void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s, int *host_next = nullptr);
 void launch_embed(const DecodeModel &m, cudaStream_t s);
 int decode_attn_limits_ok(int hd, int chunk, int n_chunks);
 void launch_matvec(const float *W, const float *x, float *y, int rows, int cols, cudaStream_t s);
