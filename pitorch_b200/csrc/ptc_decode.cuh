@@ -56,6 +56,13 @@ struct DecodeModel {
     int n_chunks;    // ceil(seq / att_chunk)
     StepState *step;
     int *err;        // set (non-zero) by a kernel whose bounded wait expired
+    // Several device-loop tokens captured in one graph: the kernels of the
+    // graph's k-th token decode position step->pos + tok_off (step->pos is
+    // advanced only by the classifier of the last token, adv = 1), and layer
+    // 0 reads step->tok after its wait when tok_off > 0, since it may start
+    // while the previous token's classifier still runs.
+    int tok_off;
+    int adv;
 };
 
 // Decode matvec staging: each CTA streams its contiguous block of weight rows

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     // launches (earlier tokens, or this graph's first node), so they are
     // read before the wait; only q and the row of `pos` come from the
     // kernel this one depends on.
-    const int pos = min(__ldcg(&m.step->pos), m.seq - 1);
+    const int pos = min(__ldcg(&m.step->pos) + m.tok_off, m.seq - 1);
     const int t0 = c * CH;
     const int nc = pos / CH + 1;   // chunks holding positions <= pos
     if (c >= nc) return;           // no positions here: not part of the merge
@@ -425,9 +425,10 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     float4 xr[NV], gr[NV];
     int pos = 0;
     if (MODE == MV_QKV) {
-        pos = __ldcg(&m.step->pos);
+        pos = __ldcg(&m.step->pos) + m.tok_off;
         load_gain<NV>(gr, m.rms_att + (size_t)a.l * m.dim, c4, lane);
-        if (a.from_embedding) load_act<NV>(xr, m.emb + (size_t)__ldcg(&m.step->tok) * m.dim, c4, lane);
+        if (a.from_embedding && m.tok_off == 0)
+            load_act<NV>(xr, m.emb + (size_t)__ldcg(&m.step->tok) * m.dim, c4, lane);
     } else if (MODE == MV_FFN13) {
         load_gain<NV>(gr, m.rms_ffn + (size_t)a.l * m.dim, c4, lane);
     } else if (MODE == MV_CLS) {
@@ -446,6 +447,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     }
     if (MODE == MV_QKV) {
         if (a.from_embedding) {
+            if (m.tok_off != 0) load_act<NV>(xr, m.emb + (size_t)__ldcg(&m.step->tok) * m.dim, c4, lane);
             if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.x, xr, c4, lane);
         } else {
             load_act<NV>(xr, a.in, c4, lane);
@@ -583,13 +585,13 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     }
     st->amax = 0ull;
     st->done = 0u;
-    if (st->mode == 1 && st->pos < m.seq) {
-        const int p = st->pos;
+    const int p = st->pos + m.tok_off;
+    if (st->mode == 1 && p < m.seq) {
         int t = next;
         if (p + 1 < st->n_prompt) t = st->tokens[p + 1];
         else st->tokens[p + 1] = next;
         st->tok = t;
-        st->pos = p + 1;
+        if (m.adv) st->pos = p + 1;
     }
     __threadfence();
 }
@@ -772,7 +774,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     const int dim = m.dim, hd = m.hd, hd4 = hd >> 2, c4 = dim >> 2, l = a.l;
     const int q0 = 3 * hd * r / AC, q1 = 3 * hd * (r + 1) / AC;   // q/k/v rows of this CTA
     const int o0 = dim * r / AC, o1 = dim * (r + 1) / AC;         // wo rows of this CTA
-    const int pos_raw = __ldcg(&m.step->pos);
+    const int pos_raw = __ldcg(&m.step->pos) + m.tok_off;
     const bool pos_ok = pos_raw >= 0 && pos_raw < m.seq;
     const int pos = pos_ok ? pos_raw : 0;
     // positions of this CTA: [t0, t1) of [0, pos]
@@ -839,13 +841,16 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         rcs[k] = (pr < q1 && pr < 2 * hd) ? __ldg(m.rope + (size_t)pos * (hd / 2) + (pr % hd) / 2)
                                           : make_float2(1.f, 0.f);
     }
-    const float *xsrc = a.xin ? a.xin : m.emb + (size_t)__ldcg(&m.step->tok) * dim;
-    if (!a.xin) load_act<NV>(xr, xsrc, c4, lane);
+    // layer 0 reads the token's embedding row: before the wait when this is
+    // the graph's first token, after it otherwise
+    const float *xsrc = a.xin ? a.xin : m.emb + (size_t)(m.tok_off == 0 ? __ldcg(&m.step->tok) : 0) * dim;
+    if (!a.xin && m.tok_off == 0) load_act<NV>(xr, xsrc, c4, lane);
     // every CTA of the cluster runs before any remote store (no memory
     // ordering needed here, so the relaxed form)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
     pdl_wait();
-    if (a.xin) load_act<NV>(xr, xsrc, c4, lane);
+    if (!a.xin && m.tok_off != 0) xsrc = m.emb + (size_t)__ldcg(&m.step->tok) * dim;
+    if (a.xin || m.tok_off != 0) load_act<NV>(xr, xsrc, c4, lane);
     if (h == 0)
         for (int i = tid; i < (o1 - o0) / 4; i += AT_THREADS)
             reinterpret_cast<float4 *>(s_res)[i] = __ldcg(reinterpret_cast<const float4 *>(xsrc + o0) + i);

@@ -35,18 +35,24 @@ struct ptc_decoder {
     int *d_tokens;         // [seq + 1]
     int mode;              // current StepState.mode on the device
     cudaGraphExec_t g_host, g_dev;
+    cudaGraphExec_t g_devk;  // DEV_TOKENS device-loop tokens per launch (null: not used)
     // persistent single-kernel path (ptc_persist.cu)
     bool persist;
     ptc::PersistArgs pa;
     int loop_pos;          // device-loop mode: next position to decode
 };
 
-static void enqueue_kernels(ptc_decoder *d, cudaStream_t s, int *host_next) {
-    const DecodeModel &m = d->m;
+static void enqueue_kernels(ptc_decoder *d, const DecodeModel &m, cudaStream_t s, int *host_next) {
     if (d->has_embed && m.L == 0) ptc::launch_embed(m, s);
     ptc::launch_layers(m, 0, m.L, d->has_embed != 0, d->n_sm, s);
     if (d->has_head) ptc::launch_head(m, d->n_sm, s, host_next);
 }
+
+// Device-loop tokens per graph launch. Inside one graph the programmatic
+// launch chain runs on from one token's classifier into the next token's
+// first layer, whose weight copies then overlap the classifier instead of
+// starting after a graph boundary.
+constexpr int DEV_TOKENS = 8;
 
 static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
     cudaStream_t s = d->stream;
@@ -56,7 +62,7 @@ static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
         PTC_CHECK(cudaMemcpyAsync(d->m.step, d->io, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
     // host steps: the classifier's last CTA stores the token into the pinned
     // io->next itself (4 bytes over PCIe), so the graph ends with the kernel
-    enqueue_kernels(d, s, host_io ? &d->io->next : nullptr);
+    enqueue_kernels(d, d->m, s, host_io ? &d->io->next : nullptr);
     PTC_CHECK(cudaStreamEndCapture(s, &g));
     cudaGraphExec_t ge;
     PTC_CHECK(cudaGraphInstantiate(&ge, g, 0));
@@ -84,6 +90,7 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     PTC_CHECK(cudaSetDevice(ptc_device(c)));
     ptc_decoder *d = new ptc_decoder();
     memset(&d->m, 0, sizeof(d->m));
+    d->m.adv = 1;   // every single-token launch advances the device position
     d->ctx = c;
     d->stream = ptc_ctx_stream(c);
     d->has_embed = has_embed;
@@ -187,6 +194,20 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
 
     d->g_host = capture(d, true);
     d->g_dev = capture(d, false);
+    d->g_devk = nullptr;
+    if (has_embed && has_head && m.L > 0) {
+        cudaGraph_t g;
+        PTC_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        for (int k = 0; k < DEV_TOKENS; k++) {
+            DecodeModel mk = m;
+            mk.tok_off = k;
+            mk.adv = k == DEV_TOKENS - 1;
+            enqueue_kernels(d, mk, s, nullptr);
+        }
+        PTC_CHECK(cudaStreamEndCapture(s, &g));
+        PTC_CHECK(cudaGraphInstantiate(&d->g_devk, g, 0));
+        PTC_CHECK(cudaGraphDestroy(g));
+    }
 
     // Persistent path: one cooperative kernel per launch (see ptc_persist.cu).
     // Opt-in (PTC_DECODE_PERSIST=1): on B200 its 49 grid-barrier phases per
@@ -256,6 +277,7 @@ extern "C" void ptc_decoder_destroy(ptc_decoder *d) {
     cudaStreamSynchronize(d->stream);
     cudaGraphExecDestroy(d->g_host);
     cudaGraphExecDestroy(d->g_dev);
+    if (d->g_devk) cudaGraphExecDestroy(d->g_devk);
     ptc_host_free(d->io);
     ptc_host_free(d->stage);
     delete d;  // device buffers belong to the context arena
@@ -351,7 +373,10 @@ extern "C" void ptc_decoder_enqueue_steps(ptc_decoder *d, int n) {
         d->loop_pos += n > 0 ? n : 0;
         return;
     }
-    for (int i = 0; i < n; i++) PTC_CHECK(cudaGraphLaunch(d->g_dev, d->stream));
+    int i = 0;
+    if (d->g_devk)
+        for (; i + DEV_TOKENS <= n; i += DEV_TOKENS) PTC_CHECK(cudaGraphLaunch(d->g_devk, d->stream));
+    for (; i < n; i++) PTC_CHECK(cudaGraphLaunch(d->g_dev, d->stream));
 }
 
 extern "C" void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n) {
