@@ -336,6 +336,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
 // ---------------------------------------------------------------------------
 enum MvMode { MV_QKV = 0, MV_FFN13 = 1, MV_RESID = 2, MV_CLS = 3 };
 
+// Ring geometry of the classifier (the other modes use MV_STAGES stages of
+// MV_STAGE_BYTES).
+#ifndef PTC_CLS_STAGE_KB
+#define PTC_CLS_STAGE_KB 24
+#endif
+#ifndef PTC_CLS_STAGES
+#define PTC_CLS_STAGES 4
+#endif
+constexpr int CLS_STAGE_BYTES = PTC_CLS_STAGE_KB * 1024;
+constexpr int CLS_STAGES = PTC_CLS_STAGES;
+static_assert(CLS_STAGES * 8 <= MV_BAR_BYTES && MV_STAGES * 8 <= MV_BAR_BYTES, "mbarriers do not fit");
+
 struct MvArgs {
     const float *W;    // MV_RESID: the matrix; MV_CLS: wcls
     const float *in;   // MV_RESID: input vector; MV_QKV: the layer input x
@@ -407,16 +419,17 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     const int it1 = (int)((long)a.n_items * (blockIdx.x + 1) / gridDim.x);
     const int ps = a.per_stage;
     const int n_chunks = (it1 - it0 + ps - 1) / ps;
-    const int stage_floats = MV_STAGE_BYTES / 4;
+    constexpr int NST = MODE == MV_CLS ? CLS_STAGES : MV_STAGES;
+    const int stage_floats = (MODE == MV_CLS ? CLS_STAGE_BYTES : MV_STAGE_BYTES) / 4;
     const int c4 = a.cols >> 2;
 
     if (tid == 0) {
-        for (int s = 0; s < MV_STAGES; s++) mbar_init(&bars[s], 1);
+        for (int s = 0; s < NST; s++) mbar_init(&bars[s], 1);
         mbar_init_fence();
     }
     __syncthreads();
     if (tid == 0)
-        for (int k = 0; k < n_chunks && k < MV_STAGES; k++)
+        for (int k = 0; k < n_chunks && k < NST; k++)
             mv_issue<MODE>(m, a, stages + k * stage_floats, &bars[k], it0 + k * ps, min(it1, it0 + (k + 1) * ps));
 
     // Everything that does not come from the kernel this one depends on is
@@ -442,7 +455,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
 #pragma unroll
         for (int q = 0; q < XPRE; q++) {
             const int i = it0 + warp + q * NW;   // this warp's q-th item (direct mode)
-            xres[q] = (lane == 0 && n_chunks <= MV_STAGES && i < it1) ? __ldcg(a.res_in + i) : 0.f;
+            xres[q] = (lane == 0 && n_chunks <= NST && i < it1) ? __ldcg(a.res_in + i) : 0.f;
         }
     }
     if (MODE == MV_QKV) {
@@ -515,7 +528,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             }
         }
     };
-    if (n_chunks <= MV_STAGES) {
+    if (n_chunks <= NST) {
         // The whole block is in flight at once: each warp takes its items
         // directly, waiting only for the stage that holds each one.
         int q = 0;
@@ -538,23 +551,23 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             for (int k = 0; k < n_chunks; k++) mbar_wait_bounded(&bars[k], 0u, nullptr, 0);
     } else {
         for (int k = 0; k < n_chunks; k++) {
-            const int s = k % MV_STAGES;
+            const int s = k % NST;
             const float *stage = stages + s * stage_floats;
-            const bool got = mbar_wait_bounded(&bars[s], (unsigned)((k / MV_STAGES) & 1), m.err, ERR_MBAR_TIMEOUT);
+            const bool got = mbar_wait_bounded(&bars[s], (unsigned)((k / NST) & 1), m.err, ERR_MBAR_TIMEOUT);
             if (__syncthreads_or(!got)) {   // block-uniform give-up
                 ok = false;
                 if (tid == 0)   // let copies still in flight land before the CTA exits
-                    for (int kk = k + 1; kk < n_chunks && kk < k + MV_STAGES; kk++)
-                        mbar_wait_bounded(&bars[kk % MV_STAGES], (unsigned)((kk / MV_STAGES) & 1), nullptr, 0);
+                    for (int kk = k + 1; kk < n_chunks && kk < k + NST; kk++)
+                        mbar_wait_bounded(&bars[kk % NST], (unsigned)((kk / NST) & 1), nullptr, 0);
                 break;
             }
             const int c0 = it0 + k * ps, c1 = min(it1, c0 + ps);
             for (int i = c0 + warp; i < c1; i += NW)
                 do_item(stage, i - c0, i, (MODE == MV_RESID && lane == 0) ? __ldcg(a.res_in + i) : 0.f);
             __syncthreads();
-            if (tid == 0 && k + MV_STAGES < n_chunks) {
+            if (tid == 0 && k + NST < n_chunks) {
                 fence_proxy_async_smem();
-                const int kk = k + MV_STAGES;
+                const int kk = k + NST;
                 mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps));
             }
         }
@@ -1147,16 +1160,18 @@ __global__ void k_embed(DecodeModel m);
 template <int NV, int MODE>
 static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) {
     static bool configured = false;  // per instantiation
+    const int stage_bytes = MODE == MV_CLS ? CLS_STAGE_BYTES : MV_STAGE_BYTES;
+    const int n_stages = MODE == MV_CLS ? CLS_STAGES : MV_STAGES;
     if (!configured) {
         PTC_CHECK(cudaFuncSetAttribute(k_mv<NV, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       MV_SMEM_BYTES));
+                                       MV_BAR_BYTES + n_stages * stage_bytes));
         // Same (maximal) shared-memory carveout for every decode kernel, so
         // consecutive kernels can co-reside on an SM without reconfiguring L1.
         PTC_CHECK(cudaFuncSetAttribute(k_mv<NV, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
         configured = true;
     }
     const int item_bytes = a.slots * a.cols * 4;
-    a.per_stage = MV_STAGE_BYTES / item_bytes;
+    a.per_stage = stage_bytes / item_bytes;
     if (a.per_stage < 1) PTC_FATAL("decode row of %d floats does not fit a staging buffer", a.cols);
     const int grid = a.n_items < n_sm ? a.n_items : n_sm;
     // Only the stages a CTA can fill are reserved, so that the next kernels
@@ -1164,8 +1179,8 @@ static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) 
     // streams early.
     const int items_max = (a.n_items + grid - 1) / grid;
     int stages = (items_max + a.per_stage - 1) / a.per_stage;
-    if (stages > MV_STAGES) stages = MV_STAGES;
-    const size_t smem = (size_t)MV_BAR_BYTES + (size_t)stages * MV_STAGE_BYTES;
+    if (stages > n_stages) stages = n_stages;
+    const size_t smem = (size_t)MV_BAR_BYTES + (size_t)stages * stage_bytes;
     launch_pdl(k_mv<NV, MODE>, dim3(grid), dim3(MV_THREADS), smem, s, m, a);
 }
 

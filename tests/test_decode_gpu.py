@@ -67,6 +67,23 @@ def test_device_loop_generate_equals_host_loop(ptlib):
     ctx.close()
 
 
+@pytest.mark.parametrize("mode", ["default", "0"])
+def test_device_loop_any_length(ptlib, monkeypatch, mode):
+    """The device loop decodes 8 positions per graph launch and the rest one
+    per launch; every split gives the reference's stream, including a long
+    prompt teacher-forced across launch boundaries."""
+    if mode != "default":
+        monkeypatch.setenv("PTC_DECODE_FUSED", mode)
+    g = golden("decode_stories15M.npz")
+    ctx = api.Context(synth.make_blob("stories15M"))
+    for n in (1, 7, 8, 13, 29):
+        assert np.array_equal(ctx.generate_greedy(g["prompt"], n), g["tokens"][:n]), n
+    # 19 prompt tokens: the reference's own stream as the forced prefix
+    prompt = np.concatenate([g["prompt"][:1], g["tokens"][:18]]).astype(np.int32)
+    assert np.array_equal(ctx.generate_greedy(prompt, 37), g["tokens"][:37])
+    ctx.close()
+
+
 def test_reset_kv_restarts_sequence(ptlib):
     g = golden("decode_tiny.npz")
     ctx = api.Context(synth.make_blob("tiny"))
