@@ -71,7 +71,6 @@ constexpr int MV_THREADS = 256;
 constexpr int MV_STAGES = 4;
 constexpr int MV_STAGE_BYTES = 24 * 1024;
 constexpr int MV_BAR_BYTES = 128;   // mbarriers at the front, stages 128-byte aligned after
-constexpr int MV_SMEM_BYTES = MV_BAR_BYTES + MV_STAGES * MV_STAGE_BYTES;
 
 // Fused FFN (k_ffn): one CTA per SM, whole w1/w3/w2t row blocks resident.
 constexpr int FF_THREADS = 256;

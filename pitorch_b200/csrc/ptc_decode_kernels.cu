@@ -891,14 +891,19 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             }
         }
     }
-    cluster.sync();
+    // This CTA's q/k/v values are in every CTA's s_qkv: arrive (release) on
+    // the cluster barrier now and wait for it only before reading s_qkv, so
+    // the copies below are issued while the barrier completes.
+    asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
+    __syncthreads();
     // Every thread of this CTA has consumed the layer input (rmsnorm, the
     // residual copy), so the CTA takes its ticket now; the result is only
     // looked at when the CTA ends, where the last one clears the buffer.
     unsigned ticket = 0u;
     if (tid == AT_THREADS - 1) ticket = atomicAdd(&m.tickets[0], 1u);
-    // The staging rows are consumed: the wo slice (rows [o0, o1), the hd
-    // columns of head h) takes their place, 16 bytes per thread and copy.
+    // The staging rows are consumed by this CTA's warps: the wo slice (rows
+    // [o0, o1), the hd columns of head h) takes their place, 16 bytes per
+    // thread and copy.
     {
         const float *wo_base = m.wo + (size_t)l * dim * dim + (size_t)h * hd;
         for (int f = tid; f < (o1 - o0) * hd4; f += AT_THREADS) {
@@ -923,6 +928,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
     }
     cp_async_commit();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // s_qkv complete
     // 2. attention over [t0, t1): online softmax in rounds of AT_ROUND
     const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
     float4 qv[QK];
