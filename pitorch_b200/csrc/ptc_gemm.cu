@@ -19,11 +19,72 @@
 #include "ptc_common.cuh"
 #include "ptc_gemm.h"
 
+#include <cooperative_groups.h>
 #include <string.h>
 
 #include "../../include/ptc.h"
 
 namespace ptc {
+
+namespace cg = cooperative_groups;
+
+// One reduced element pair (m, n), (m, n + 1) through the product's epilogue
+// (n even; N is even for RoPE products, so pairs never straddle rows).
+__device__ __forceinline__ void store_pair(const GemmArgs &g, int m, int n, float v0, float v1) {
+    if (g.epi == EPI_ROPE) {
+        if (n + 1 >= g.N) return;
+        const float th = rope_theta(n, g.rope_hd, m);
+        const float cs = pt_cosf(th), sn = pt_sinf(th);
+        float *c = g.C + (size_t)m * g.ldc + n;
+        c[0] = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
+        c[1] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
+        return;
+    }
+    const float v[2] = {v0, v1};
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        if (n + j >= g.N) continue;
+        float *c = g.C + (size_t)m * g.ldc + n + j;
+        switch (g.epi) {
+            case EPI_STORE: *c = v[j]; break;
+            case EPI_ACCUM: *c = *c + v[j]; break;
+            case EPI_RESID: *c = __fadd_rn(g.R[(size_t)m * g.ldr + n + j], v[j]); break;
+            default: *c = v[j]; break;
+        }
+    }
+}
+
+// Split-K inside a thread-block cluster: the cluster's CTAs are the splits of
+// one BM x BN tile. Each parks its partial tile in its own (free) staging
+// buffer; after a cluster barrier CTA r sums rows [r*BM/cs, (r+1)*BM/cs) of
+// all partials in split order -- the order of k_splitk_reduce, so results
+// are the same bit for bit -- and stores them through the epilogue.
+template <int BM, int BN, int TM, int TN, int NT>
+__device__ __forceinline__ void cluster_reduce(const GemmArgs &g, const float (&acc)[TM][TN], float *tile, int m0,
+                                               int n0, int tx, int ty) {
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j += 4)
+            *reinterpret_cast<float4 *>(&tile[(ty * TM + i) * BN + tx * TN + j]) =
+                make_float4(acc[i][j], acc[i][j + 1], acc[i][j + 2], acc[i][j + 3]);
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    const int cs = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+    const int rows = BM / cs, r0 = rank * rows;
+    for (int e = 2 * (int)threadIdx.x; e < rows * BN; e += 2 * NT) {
+        const int rr = r0 + e / BN, cc = e % BN;
+        const int m = m0 + rr, n = n0 + cc;
+        float v0 = 0.f, v1 = 0.f;
+        for (int s = 0; s < cs; s++) {
+            const float *p = cl.map_shared_rank(tile, s) + rr * BN + cc;
+            v0 += p[0];
+            v1 += p[1];
+        }
+        if (m < g.M && n < g.N) store_pair(g, m, n, v0, v1);
+    }
+    cl.sync();   // no CTA leaves while another still reads its tile
+}
 
 // Store a thread's TM x TN block (rows mb.., columns nb..) with the
 // product's epilogue, or into the split-K partial buffer.
@@ -170,8 +231,10 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_gemm_v(GemmArgs g, in
     constexpr int NT = (BM / TM) * (BN / TN);
     constexpr int A4 = BM * BK / 4 / NT, B4 = BN * BK / 4 / NT;
     static_assert(A4 >= 1 && B4 >= 1 && A4 * 4 * NT == BM * BK && B4 * 4 * NT == BN * BK, "tile / threads");
-    __shared__ __align__(16) float As[2][BK][BM + 4];
-    __shared__ __align__(16) float Bs[2][BK][BN + 4];
+    constexpr int SA = 2 * BK * (BM + 4), SB = 2 * BK * (BN + 4);
+    __shared__ __align__(16) float sbuf[SA + SB];
+    auto As = reinterpret_cast<float (*)[BK][BM + 4]>(sbuf);
+    auto Bs = reinterpret_cast<float (*)[BK][BN + 4]>(sbuf + SA);
     const int tid = threadIdx.x;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int split = blockIdx.z;
@@ -275,6 +338,12 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_gemm_v(GemmArgs g, in
         __syncthreads();
         buf ^= 1;
     }
+    if constexpr (BM * BN <= SA + SB) {
+        if (g.cluster_red) {   // the loop ended with a barrier: sbuf is free
+            cluster_reduce<BM, BN, TM, TN, NT>(g, acc, sbuf, m0, n0, tx, ty);
+            return;
+        }
+    }
     gemm_epilogue<TM, TN>(g, acc, m0 + ty * TM, n0 + tx * TN, split);
 }
 
@@ -326,15 +395,30 @@ static void launch_tile(const GemmArgs &g, cudaStream_t s) {
     PTC_CHECK(cudaGetLastError());
 }
 
+template <int BM, int BN, int BK, int TM, int TN, bool A_KC, bool B_KC>
+static void launch_v(const GemmArgs &g, int kper, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
+    cfg.blockDim = dim3((BM / TM) * (BN / TN));
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (g.cluster_red) {   // one cluster = the splits of one tile
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = g.splits;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    PTC_CHECK(cudaLaunchKernelEx(&cfg, k_gemm_v<BM, BN, BK, TM, TN, A_KC, B_KC>, g, kper));
+}
+
 template <int BM, int BN, int BK, int TM, int TN>
 static void launch_tile_v(const GemmArgs &g, int kper, cudaStream_t s) {
-    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.splits);
-    dim3 block((BM / TM) * (BN / TN));
-    if (g.a_kcontig && g.b_kcontig) k_gemm_v<BM, BN, BK, TM, TN, true, true><<<grid, block, 0, s>>>(g, kper);
-    else if (g.a_kcontig) k_gemm_v<BM, BN, BK, TM, TN, true, false><<<grid, block, 0, s>>>(g, kper);
-    else if (g.b_kcontig) k_gemm_v<BM, BN, BK, TM, TN, false, true><<<grid, block, 0, s>>>(g, kper);
-    else k_gemm_v<BM, BN, BK, TM, TN, false, false><<<grid, block, 0, s>>>(g, kper);
-    PTC_CHECK(cudaGetLastError());
+    if (g.a_kcontig && g.b_kcontig) launch_v<BM, BN, BK, TM, TN, true, true>(g, kper, s);
+    else if (g.a_kcontig) launch_v<BM, BN, BK, TM, TN, true, false>(g, kper, s);
+    else if (g.b_kcontig) launch_v<BM, BN, BK, TM, TN, false, true>(g, kper, s);
+    else launch_v<BM, BN, BK, TM, TN, false, false>(g, kper, s);
 }
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
@@ -374,9 +458,12 @@ void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
         int kper = (g.K + splits - 1) / splits;
         kper = (kper + BK - 1) / BK * BK;
         g.splits = (g.K + kper - 1) / kper;
+        // 64x64 tiles split 2, 4 or 8 ways reduce inside a cluster (at most
+        // 8 CTAs, whole rows per CTA); anything else through the workspace
+        g.cluster_red = !big && g.splits > 1 && g.splits <= 8 && 64 % g.splits == 0;
         if (big) launch_tile_v<128, 128, 8, 8, 8>(g, kper, s);
         else launch_tile_v<64, 64, 16, 4, 4>(g, kper, s);
-        if (g.splits > 1) {
+        if (g.splits > 1 && !g.cluster_red) {
             int blocks = (int)(((size_t)g.M * g.N + 255) / 256);
             if (blocks > 8 * n_sm) blocks = 8 * n_sm;
             k_splitk_reduce<<<blocks, 256, 0, s>>>(g);

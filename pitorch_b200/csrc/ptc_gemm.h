@@ -30,6 +30,9 @@ struct GemmArgs {
     float *partial;   // split-K workspace (may be null: no split)
     size_t partial_cap;  // floats available in `partial`
     int splits;       // set by gemm()
+    int cluster_red;  // set by gemm(): the splits of a tile form a thread-block
+                      // cluster and sum their partials through distributed
+                      // shared memory (no workspace, no reduction kernel)
 };
 
 void gemm(GemmArgs g, int n_sm, cudaStream_t s);
