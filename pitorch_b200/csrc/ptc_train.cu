@@ -118,6 +118,160 @@ __global__ void __launch_bounds__(128) k_tr_attn_fwd(const float *q, const float
     }
 }
 
+// Row-block variants of the two per-row attention kernels, for T <= TB_T:
+// one CTA per (head, TB_R consecutive query rows), one warp per row. The
+// head's K and V rows 0..n_s-1 (n_s = last row of the block + 1) are staged
+// once per CTA in shared memory with a row stride of hd + 4 floats (16-byte
+// rows; the float4 reads of 8 consecutive rows then hit distinct banks).
+// Lane j of a warp owns positions j, j + 32, ... of its row.
+constexpr int TB_R = 8;
+constexpr int TB_J = 8;
+constexpr int TB_T = 32 * TB_J;
+
+size_t attn_block_smem(int T, int hd) {
+    return ((size_t)2 * T * (hd + 4) + (size_t)TB_R * hd + (size_t)TB_R * T) * 4;
+}
+
+__device__ __forceinline__ void stage_kv_rows(float *sK, float *sV, const float *k, const float *v, int n_s,
+                                              int K, int koff, int hd) {
+    const int hd4 = hd >> 2, ks = hd + 4;
+    for (int f = threadIdx.x; f < n_s * hd4; f += blockDim.x) {
+        const int s = f / hd4, c = f - s * hd4;
+        reinterpret_cast<float4 *>(sK + (size_t)s * ks)[c] =
+            __ldg(reinterpret_cast<const float4 *>(k + (size_t)s * K + koff) + c);
+        reinterpret_cast<float4 *>(sV + (size_t)s * ks)[c] =
+            __ldg(reinterpret_cast<const float4 *>(v + (size_t)s * K + koff) + c);
+    }
+}
+
+// Forward (pt_train.c:224-259): att row t = softmax(q_t . k_s * scale) over
+// s <= t (zeros after t), att_out[t, h] = sum_s att[s] v_s.
+__global__ void __launch_bounds__(TB_R * 32) k_tr_attn_fwd_blk(const float *q, const float *k, const float *v,
+                                                              float *att, float *out, int T, int nh, int nkv,
+                                                              int hd) {
+    extern __shared__ __align__(16) float sm[];
+    const int h = blockIdx.x, t0 = blockIdx.y * TB_R;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = nh * hd, K = nkv * hd, koff = (h / (nh / nkv)) * hd, hd4 = hd >> 2, ks = hd + 4;
+    const int n_s = min(T, t0 + TB_R);
+    float *sK = sm, *sV = sm + (size_t)T * ks, *sQ = sV + (size_t)T * ks, *sP = sQ + TB_R * hd;
+    stage_kv_rows(sK, sV, k, v, n_s, K, koff, hd);
+    const int t = t0 + warp;
+    if (t < T)
+        for (int d = lane; d < hd; d += 32) sQ[warp * hd + d] = q[(size_t)t * D + h * hd + d];
+    __syncthreads();
+    if (t >= T) return;   // no block barrier follows
+    const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
+    const float4 *q4 = reinterpret_cast<const float4 *>(sQ + warp * hd);
+    float sc[TB_J];
+    float mx = -3.4028235e+38f;
+#pragma unroll
+    for (int j = 0; j < TB_J; j++) {
+        const int sp = lane + 32 * j;
+        sc[j] = 0.f;
+        if (sp <= t) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(sK + (size_t)sp * ks);
+            float acc = 0.f;
+            for (int c = 0; c < hd4; c++) acc = dot4(k4[c], q4[c], acc);
+            sc[j] = __fmul_rn(acc, scale);
+            mx = fmaxf(mx, sc[j]);
+        }
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < TB_J; j++) {
+        if (lane + 32 * j <= t) {
+            sc[j] = pt_expf(__fsub_rn(sc[j], mx));
+            sum += sc[j];
+        }
+    }
+    sum = warp_sum(sum);
+    const float inv = __fdiv_rn(1.0f, sum);
+    float *arow = att + ((size_t)h * T + t) * T, *prow = sP + warp * T;
+#pragma unroll
+    for (int j = 0; j < TB_J; j++) {
+        const int sp = lane + 32 * j;
+        if (sp < T) {
+            const float pv = (sp <= t) ? __fmul_rn(sc[j], inv) : 0.f;
+            arow[sp] = pv;
+            prow[sp] = pv;
+        }
+    }
+    __syncwarp();
+    float o0 = 0.f, o1 = 0.f;
+    for (int sp = 0; sp <= t; sp++) {
+        const float pv = prow[sp];
+        const float *vr = sV + (size_t)sp * ks;
+        if (lane < hd) o0 = fmaf(pv, vr[lane], o0);
+        if (lane + 32 < hd) o1 = fmaf(pv, vr[lane + 32], o1);
+    }
+    float *orow = out + (size_t)t * D + h * hd;
+    if (lane < hd) orow[lane] = o0;
+    if (lane + 32 < hd) orow[lane + 32] = o1;
+}
+
+// Backward part 1 (pt_train.c:780-812) for rows t < n_rows: dP = d_ao . v,
+// dS[t][s] = P[t][s] (dP[s] - <dP, P[t]>) * scale, d_q[t] = sum_s dS[t][s] k_s.
+__global__ void __launch_bounds__(TB_R * 32) k_tr_attn_bwd_q_blk(const float *d_ao, const float *att,
+                                                                const float *k, const float *v, float *dS,
+                                                                float *d_q, int T, int n_rows, int nh, int nkv,
+                                                                int hd) {
+    extern __shared__ __align__(16) float sm[];
+    const int h = blockIdx.x, t0 = blockIdx.y * TB_R;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = nh * hd, K = nkv * hd, koff = (h / (nh / nkv)) * hd, hd4 = hd >> 2, ks = hd + 4;
+    const int n_s = min(n_rows, t0 + TB_R);
+    float *sK = sm, *sV = sm + (size_t)T * ks, *sD = sV + (size_t)T * ks, *sP = sD + TB_R * hd;
+    stage_kv_rows(sK, sV, k, v, n_s, K, koff, hd);
+    const int t = t0 + warp;
+    if (t < n_rows)
+        for (int d = lane; d < hd; d += 32) sD[warp * hd + d] = d_ao[(size_t)t * D + h * hd + d];
+    __syncthreads();
+    if (t >= n_rows) return;   // no block barrier follows
+    const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
+    const float4 *d4 = reinterpret_cast<const float4 *>(sD + warp * hd);
+    const float *P = att + ((size_t)h * T + t) * T;
+    float dp[TB_J], pr[TB_J];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < TB_J; j++) {
+        const int sp = lane + 32 * j;
+        dp[j] = 0.f;
+        pr[j] = 0.f;
+        if (sp <= t) {
+            const float4 *v4 = reinterpret_cast<const float4 *>(sV + (size_t)sp * ks);
+            float acc = 0.f;
+            for (int c = 0; c < hd4; c++) acc = dot4(v4[c], d4[c], acc);
+            dp[j] = acc;
+            pr[j] = P[sp];
+            dot = fmaf(acc, pr[j], dot);
+        }
+    }
+    dot = warp_sum(dot);
+    float *dsr = dS + ((size_t)h * T + t) * T, *xrow = sP + warp * T;
+#pragma unroll
+    for (int j = 0; j < TB_J; j++) {
+        const int sp = lane + 32 * j;
+        if (sp < T) {
+            const float x = (sp <= t) ? __fmul_rn(__fmul_rn(pr[j], __fsub_rn(dp[j], dot)), scale) : 0.f;
+            dsr[sp] = x;
+            xrow[sp] = x;
+        }
+    }
+    __syncwarp();
+    float a0 = 0.f, a1 = 0.f;
+    for (int sp = 0; sp <= t; sp++) {
+        const float x = xrow[sp];
+        const float *kr = sK + (size_t)sp * ks;
+        if (lane < hd) a0 = fmaf(x, kr[lane], a0);
+        if (lane + 32 < hd) a1 = fmaf(x, kr[lane + 32], a1);
+    }
+    float *qrow = d_q + (size_t)t * D + h * hd;
+    if (lane < hd) qrow[lane] = a0;
+    if (lane + 32 < hd) qrow[lane + 32] = a1;
+}
+
 // sh = silu(h1) * h3 with the training form (h1 * sig) * h3 (pt_train.c:281-284).
 __global__ void k_tr_silu_gate(float *sh, const float *h1, const float *h3, size_t n) {
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
@@ -657,6 +811,26 @@ extern "C" void ptc_trainer_fwd_embed(ptc_trainer *tr) {
 }
 
 // pt_forward_train_layers_range (pt_train.c:954-1061)
+// The row-block attention kernels need T <= TB_T, whole float4 head rows and
+// their shared-memory staging within a CTA's limit; otherwise the per-row
+// kernels run.
+static bool attn_blocked(ptc_trainer *tr, int T) {
+    if (T > ptc::TB_T || tr->hd % 4 || tr->hd > 64) return false;
+    const size_t smem = ptc::attn_block_smem(T, tr->hd);
+    if (smem > 200 * 1024) return false;
+    static size_t configured[64];   // per device: largest size set so far
+    int dev = 0;
+    PTC_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) PTC_FATAL("device index %d", dev);
+    if (smem > configured[dev]) {
+        PTC_CHECK(cudaFuncSetAttribute(ptc::k_tr_attn_fwd_blk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        PTC_CHECK(cudaFuncSetAttribute(ptc::k_tr_attn_bwd_q_blk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem));
+        configured[dev] = smem;
+    }
+    return true;
+}
+
 extern "C" void ptc_trainer_fwd_layers(ptc_trainer *tr, int l0, int l1) {
     const int T = tr->T, D = tr->D, H = tr->H, K = tr->K, nh = tr->nh;
     cudaStream_t s = tr->s;
@@ -672,10 +846,17 @@ extern "C" void ptc_trainer_fwd_layers(ptc_trainer *tr, int l0, int l1) {
         g.rope_hd = tr->hd;
         run_gemm(tr, g);
         run_gemm(tr, G(T, K, D, xa, D, true, tr->w.wv + (size_t)l * K * D, D, true, tr->v + LK, K, ptc::EPI_STORE));
-        const size_t smem = (size_t)(tr->hd + T) * 4;
-        ptc::k_tr_attn_fwd<<<dim3(nh, T), 128, smem, s>>>(tr->q + LD, tr->k + LK, tr->v + LK,
-                                                          tr->att + (size_t)l * nh * T * T, tr->att_out + LD,
-                                                          T, nh, tr->nkv, tr->hd);
+        if (attn_blocked(tr, T)) {
+            ptc::k_tr_attn_fwd_blk<<<dim3(nh, (T + ptc::TB_R - 1) / ptc::TB_R), ptc::TB_R * 32,
+                                     ptc::attn_block_smem(T, tr->hd), s>>>(
+                tr->q + LD, tr->k + LK, tr->v + LK, tr->att + (size_t)l * nh * T * T, tr->att_out + LD, T, nh,
+                tr->nkv, tr->hd);
+        } else {
+            const size_t smem = (size_t)(tr->hd + T) * 4;
+            ptc::k_tr_attn_fwd<<<dim3(nh, T), 128, smem, s>>>(tr->q + LD, tr->k + LK, tr->v + LK,
+                                                              tr->att + (size_t)l * nh * T * T, tr->att_out + LD,
+                                                              T, nh, tr->nkv, tr->hd);
+        }
         PTC_CHECK(cudaGetLastError());
         g = G(T, D, D, tr->att_out + LD, D, true, tr->w.wo + (size_t)l * D * D, D, true, rmid, D, ptc::EPI_RESID);
         g.R = rin;
@@ -766,10 +947,16 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         run_gemm(tr, G(D, D, n, tr->d_res, D, false, tr->att_out + LD, D, false, tr->g_wo + (size_t)l * D * D, D,
                        ptc::EPI_ACCUM));
         // attention
-        const size_t smem = (size_t)(tr->hd + T) * 4;
         const float *att_l = tr->att + (size_t)l * nh * T * T;
-        ptc::k_tr_attn_bwd_q<<<dim3(nh, n), 128, smem, s>>>(tr->d_aout, att_l, tr->q + LD, tr->k + LK, tr->v + LK,
-                                                            tr->dS, tr->d_q, T, nh, tr->nkv, tr->hd);
+        if (attn_blocked(tr, T)) {
+            ptc::k_tr_attn_bwd_q_blk<<<dim3(nh, (n + ptc::TB_R - 1) / ptc::TB_R), ptc::TB_R * 32,
+                                       ptc::attn_block_smem(T, tr->hd), s>>>(
+                tr->d_aout, att_l, tr->k + LK, tr->v + LK, tr->dS, tr->d_q, T, n, nh, tr->nkv, tr->hd);
+        } else {
+            const size_t smem = (size_t)(tr->hd + T) * 4;
+            ptc::k_tr_attn_bwd_q<<<dim3(nh, n), 128, smem, s>>>(tr->d_aout, att_l, tr->q + LD, tr->k + LK,
+                                                                tr->v + LK, tr->dS, tr->d_q, T, nh, tr->nkv, tr->hd);
+        }
         ptc::k_tr_attn_bwd_kv<<<dim3(tr->nkv, n), 128, 0, s>>>(tr->d_aout, att_l, tr->q + LD, tr->dS, tr->d_k,
                                                               tr->d_v, T, n, nh, tr->nkv, tr->hd);
         ptc::k_tr_rope_bwd<<<blocks_for((size_t)n * D / 2, 256, tr->n_sm), 256, 0, s>>>(

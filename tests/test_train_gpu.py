@@ -57,6 +57,25 @@ def test_tiny_train_losses_grads_weights(ptlib):
     ctx.close()
 
 
+def test_train_beyond_256_positions(ptlib):
+    """T > 256 takes the per-row attention kernels (the row-block ones cover
+    T <= 256): a narrow model with seq_len 320 trained at T = 300."""
+    cfg = (64, 176, 2, 4, 4, 1024, 320)
+    blob = synth.make_blob(cfg)
+    T = 300
+    toks = synth.make_tokens(1024, T, seed=7)
+    ctx = api.Context(blob, max_T=T)
+    ref = oracle.Model(blob, max_T=T)
+    for step in range(2):
+        loss = ctx.train_step(toks, 1e-3)
+        rl = ref.train_step(toks, 1e-3)
+        assert abs(loss - rl) <= TOL * abs(rl), (step, loss, rl)
+        gg, rg = grads_of(ctx), ref.grads()
+        for name, sl in tensor_slices(cfg):
+            assert rel_err(gg[sl], rg[sl]) <= TOL, (step, name, rel_err(gg[sl], rg[sl]))
+    ctx.close()
+
+
 def test_15M_train_20_steps_T256(ptlib):
     g = golden("train_stories15M.npz")
     T = int(g["T"])
