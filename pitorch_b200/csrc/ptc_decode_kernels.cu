@@ -654,12 +654,17 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
     }
     __syncthreads();
     if (tid == 0) {
+        // one bulk copy per row: the rows then stream in parallel (one copy
+        // per matrix measured 3.6 us/token slower at 110M)
         const size_t off = ((size_t)a.l * m.hidden + j0) * dim;
+        const unsigned rb = (unsigned)dim * 4u;
         mbar_expect_tx(&bars[0], 2u * bytes);
-        bulk_g2s(w1s, m.w1 + off, bytes, &bars[0]);
-        bulk_g2s(w3s, m.w3 + off, bytes, &bars[0]);
         mbar_expect_tx(&bars[1], bytes);
-        bulk_g2s(w2s, m.w2t + off, bytes, &bars[1]);
+        for (int j = 0; j < nj; j++) {
+            bulk_g2s(w1s + (size_t)j * dim, m.w1 + off + (size_t)j * dim, rb, &bars[0]);
+            bulk_g2s(w3s + (size_t)j * dim, m.w3 + off + (size_t)j * dim, rb, &bars[0]);
+        }
+        for (int j = 0; j < nj; j++) bulk_g2s(w2s + (size_t)j * dim, m.w2t + off + (size_t)j * dim, rb, &bars[1]);
     }
     float4 xr[NV], gr[NV];
     load_gain<NV>(gr, m.rms_ffn + (size_t)a.l * dim, c4, lane);
