@@ -809,11 +809,13 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         const size_t D = dim, K = m.kvd;
         const float *mats[3] = {m.wq + (size_t)l * D * D, m.wk + (size_t)l * K * D, m.wv + (size_t)l * K * D};
         mbar_expect_tx(&bars[0], (unsigned)((q1 - q0) * dim * 4));
+        // one bulk copy per row, as in k_ffn (0.9 us/token faster at 110M
+        // than one copy per matrix segment)
         for (int sgm = 0; sgm < 3; sgm++) {
             const int lo = max(q0, sgm * hd), hi = min(q1, (sgm + 1) * hd);
-            if (lo < hi)
-                bulk_g2s(stage + (size_t)(lo - q0) * dim, mats[sgm] + (size_t)(h * hd + lo - sgm * hd) * dim,
-                         (unsigned)((hi - lo) * dim * 4), &bars[0]);
+            for (int r = lo; r < hi; r++)
+                bulk_g2s(stage + (size_t)(r - q0) * dim, mats[sgm] + (size_t)(h * hd + r - sgm * hd) * dim,
+                         (unsigned)(dim * 4), &bars[0]);
         }
     }
     if (tid == 32 && t1 - t0 > AT_ROUND) {

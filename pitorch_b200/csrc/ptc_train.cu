@@ -1016,6 +1016,28 @@ extern "C" void ptc_trainer_sgd_head(ptc_trainer *tr, float lr) {
     PTC_CHECK(cudaGetLastError());
 }
 
+// pt_sgd_update over every parameter (pt_train.c:875-896). When the weights
+// sit in device memory in the order and spacing of the gradient buffer (the
+// uploaded .bin image: embedding, per-layer tensors, final norm), one launch
+// covers all of them instead of one per tensor.
+static void sgd_all(ptc_trainer *tr, float lr) {
+    const float *w0 = tr->w.token_embedding, *g0 = tr->g_emb;
+    const float *pw[] = {tr->w.rms_att_weight, tr->w.wq, tr->w.wk, tr->w.wv, tr->w.wo, tr->w.rms_ffn_weight,
+                         tr->w.w1, tr->w.w2, tr->w.w3, tr->w.rms_final_weight};
+    const float *pg[] = {tr->g_rms_att, tr->g_wq, tr->g_wk, tr->g_wv, tr->g_wo, tr->g_rms_ffn,
+                         tr->g_w1, tr->g_w2, tr->g_w3, tr->g_rms_final};
+    bool packed = w0 && g0;
+    for (int i = 0; i < 10 && packed; i++) packed = pw[i] - w0 == pg[i] - g0;
+    if (!packed) {
+        ptc_trainer_sgd_head(tr, lr);
+        ptc_trainer_sgd_layers(tr, lr, 0, tr->L);
+        return;
+    }
+    sgd_range(tr, w0, g0, (size_t)(tr->g_rms_final + tr->D - g0), lr);
+    if (tr->g_wcls && tr->g_wcls != tr->g_emb) sgd_range(tr, tr->w.wcls, tr->g_wcls, (size_t)tr->V * tr->D, lr);
+    PTC_CHECK(cudaGetLastError());
+}
+
 // pt_train_step (pitorch/pt.c:339-364) on a full-model trainer.
 extern "C" float ptc_trainer_step(ptc_trainer *tr, const int *tokens, int T, float lr) {
     if (!tr->has_embed || !tr->has_head) PTC_FATAL("ptc_trainer_step needs embedding and head");
@@ -1027,8 +1049,7 @@ extern "C" float ptc_trainer_step(ptc_trainer *tr, const int *tokens, int T, flo
     ptc_trainer_bwd_head(tr);
     ptc_trainer_bwd_layers(tr, 0, tr->L);
     ptc_trainer_bwd_embed(tr);
-    ptc_trainer_sgd_head(tr, lr);
-    ptc_trainer_sgd_layers(tr, lr, 0, tr->L);
+    sgd_all(tr, lr);
     PTC_CHECK(cudaStreamSynchronize(tr->s));
     return *tr->loss_host;
 }
