@@ -107,7 +107,7 @@ class ClockSampler:
 # capture of the 16-position bench case (positions 0-15, so the attention
 # block's KV share is that of those positions, not of the mean position):
 # dram__bytes_read.sum + dram__bytes_write.sum.
-TRAFFIC = {"attention block": 9515520, "ffn block": 18909696, "classifier": 102196000}
+TRAFFIC = {"attention block": 9518848, "ffn block": 18914048, "classifier": 102196000}
 TRAFFIC_SOURCE = ("ncu --set full, one launch each, python bench.py --positions 16 --steps 1 --warmup 1 "
                   "--no-cpu-baseline (attention block at a position < 16: its KV bytes are those of that position)")
 
