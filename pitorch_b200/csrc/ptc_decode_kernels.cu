@@ -1172,17 +1172,8 @@ __global__ void k_embed(DecodeModel m);
 
 template <int NV, int MODE>
 static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) {
-    static bool configured = false;  // per instantiation
     const int stage_bytes = MODE == MV_CLS ? CLS_STAGE_BYTES : MV_STAGE_BYTES;
     const int n_stages = MODE == MV_CLS ? CLS_STAGES : MV_STAGES;
-    if (!configured) {
-        PTC_CHECK(cudaFuncSetAttribute(k_mv<NV, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       MV_BAR_BYTES + n_stages * stage_bytes));
-        // Same (maximal) shared-memory carveout for every decode kernel, so
-        // consecutive kernels can co-reside on an SM without reconfiguring L1.
-        PTC_CHECK(cudaFuncSetAttribute(k_mv<NV, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        configured = true;
-    }
     const int item_bytes = a.slots * a.cols * 4;
     a.per_stage = stage_bytes / item_bytes;
     if (a.per_stage < 1) PTC_FATAL("decode row of %d floats does not fit a staging buffer", a.cols);
@@ -1194,6 +1185,9 @@ static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) 
     int stages = (items_max + a.per_stage - 1) / a.per_stage;
     if (stages > n_stages) stages = n_stages;
     const size_t smem = (size_t)MV_BAR_BYTES + (size_t)stages * stage_bytes;
+    // Every decode kernel gets the same (maximal) shared-memory carveout, so
+    // consecutive kernels co-reside on an SM without reconfiguring L1.
+    ensure_kernel_smem((const void *)k_mv<NV, MODE>, smem);
     launch_pdl(k_mv<NV, MODE>, dim3(grid), dim3(MV_THREADS), smem, s, m, a);
 }
 
@@ -1209,27 +1203,16 @@ static MvArgs mv_args(int n_items, int cols, int slots, int l) {
 
 template <int NV>
 static void launch_ffn(const DecodeModel &m, FfnArgs a, int n_sm, cudaStream_t s) {
-    static bool configured = false;  // per instantiation
-    if (!configured) {
-        PTC_CHECK(cudaFuncSetAttribute(k_ffn<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       MV_BAR_BYTES + FF_MAX_SMEM));
-        PTC_CHECK(cudaFuncSetAttribute(k_ffn<NV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        configured = true;
-    }
     const int grid = m.hidden < n_sm ? m.hidden : n_sm;
     const size_t smem = (size_t)MV_BAR_BYTES + 3 * (size_t)m.ffn_rows * m.dim * 4;
+    ensure_kernel_smem((const void *)k_ffn<NV>, smem);
     launch_pdl(k_ffn<NV>, dim3(grid), dim3(FF_THREADS), smem, s, m, a);
 }
 
 template <int NV>
 static void launch_attn_fused(const DecodeModel &m, AttnArgs a, cudaStream_t s) {
     const size_t smem = (size_t)MV_BAR_BYTES + (size_t)m.attn_stage * 4;
-    static size_t configured = 0;  // per instantiation: largest size set so far
-    if (smem > configured) {
-        PTC_CHECK(cudaFuncSetAttribute(k_attn_fused<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        PTC_CHECK(cudaFuncSetAttribute(k_attn_fused<NV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        configured = smem;
-    }
+    ensure_kernel_smem((const void *)k_attn_fused<NV>, smem);
     a.stage_floats = m.attn_stage;
     launch_cluster_pdl(k_attn_fused<NV>, dim3(m.nh * AC), dim3(AT_THREADS), smem, AC, s, m, a);
 }
@@ -1293,12 +1276,8 @@ static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float
     a.from_embedding = from_embedding ? 1 : 0;
     a.in = x_in;
     PTC_NV_SWITCH(nvd, (launch_mv<NV, MV_QKV>(m, a, n_sm, s)));
-    static bool attn_configured = false;
-    if (!attn_configured) {
-        PTC_CHECK(cudaFuncSetAttribute(k_attn, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        PTC_CHECK(cudaFuncSetAttribute(k_embed, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        attn_configured = true;
-    }
+    ensure_kernel_smem((const void *)k_attn, 0);
+    ensure_kernel_smem((const void *)k_embed, 0);
     launch_pdl(k_attn, dim3(m.nh, m.n_chunks), dim3(ATT_THREADS), 0, s, m, l);
     a = mv_args(m.dim, m.dim, 1, l);
     a.W = m.wo + (size_t)l * m.dim * m.dim;

@@ -18,6 +18,11 @@ cudaStream_t ptc_ctx_stream(ptc_ctx *c);
 int ptc_ctx_device(ptc_ctx *c);
 
 namespace ptc {
+// Grants `kernel` at least `smem` bytes of dynamic shared memory and the
+// maximal shared-memory carveout on the current device. cudaFuncSetAttribute
+// acts on one device, so what each (kernel, device) pair was granted is
+// remembered per pair; thread-safe.
+void ensure_kernel_smem(const void *kernel, size_t smem);
 struct DecodeModel;
 // Layers [l0, l1) of one decode position; the range reads and leaves x in m.x.
 void launch_layers(const DecodeModel &m, int l0, int l1, bool from_embedding, int n_sm, cudaStream_t s);

@@ -700,11 +700,7 @@ void persist_launch(const PersistArgs &a, int n_sm, cudaStream_t s) {
 #undef PS_CASE
         default: PTC_FATAL("persistent decode: dim %d too large", a.m.dim);
     }
-    static void *configured[32];
-    if (configured[nvd] != (void *)kern) {
-        PTC_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        configured[nvd] = (void *)kern;
-    }
+    ensure_kernel_smem((const void *)kern, smem);
     PTC_CHECK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), s));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_sm);

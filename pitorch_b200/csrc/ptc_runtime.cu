@@ -10,6 +10,8 @@
 #include <string.h>
 #include <time.h>
 
+#include <map>
+#include <utility>
 #include <vector>
 
 #include "../../include/ptc.h"
@@ -25,6 +27,25 @@ struct ptc_ctx {
 };
 
 static const size_t kGrowChunk = 256ull << 20;
+
+namespace ptc {
+void ensure_kernel_smem(const void *kernel, size_t smem) {
+    static pthread_mutex_t mu = PTHREAD_MUTEX_INITIALIZER;
+    static std::map<std::pair<const void *, int>, size_t> granted;
+    int dev = 0;
+    PTC_CHECK(cudaGetDevice(&dev));
+    pthread_mutex_lock(&mu);
+    const auto key = std::make_pair(kernel, dev);
+    auto it = granted.find(key);
+    if (it == granted.end() || it->second < smem) {
+        if (it == granted.end())
+            PTC_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        PTC_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        granted[key] = smem;
+    }
+    pthread_mutex_unlock(&mu);
+}
+}  // namespace ptc
 
 extern "C" int ptc_device_count(void) {
     int n = 0;

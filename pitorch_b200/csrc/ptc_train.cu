@@ -818,16 +818,8 @@ static bool attn_blocked(ptc_trainer *tr, int T) {
     if (T > ptc::TB_T || tr->hd % 4 || tr->hd > 64) return false;
     const size_t smem = ptc::attn_block_smem(T, tr->hd);
     if (smem > 200 * 1024) return false;
-    static size_t configured[64];   // per device: largest size set so far
-    int dev = 0;
-    PTC_CHECK(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) PTC_FATAL("device index %d", dev);
-    if (smem > configured[dev]) {
-        PTC_CHECK(cudaFuncSetAttribute(ptc::k_tr_attn_fwd_blk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        PTC_CHECK(cudaFuncSetAttribute(ptc::k_tr_attn_bwd_q_blk, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem));
-        configured[dev] = smem;
-    }
+    ptc::ensure_kernel_smem((const void *)ptc::k_tr_attn_fwd_blk, smem);
+    ptc::ensure_kernel_smem((const void *)ptc::k_tr_attn_bwd_q_blk, smem);
     return true;
 }
 
