@@ -578,7 +578,9 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     if (lane == 0) s_best[warp] = best;
     __syncthreads();
     StepState *st = m.step;
+    int err_seen = 0;   // thread 0: an earlier kernel's expired wait (host steps)
     if (tid == 0) {
+        if (a.host_next) err_seen = __ldcg(m.err);   // its latency overlaps the atomics below
         unsigned long long b = 0ull;
         for (int w = 0; w < NW; w++) b = s_best[w] > b ? s_best[w] : b;
         if (b) atomicMax(&st->amax, b);
@@ -593,7 +595,9 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     const int next = argmax_key_index(key);
     st->next = next;
     if (a.host_next) {   // straight into the host's pinned word: no copy node after the kernel
-        *reinterpret_cast<volatile int *>(a.host_next) = next;
+        // -1 sends the host to the error word, so a token computed after an
+        // expired wait is never returned as valid
+        *reinterpret_cast<volatile int *>(a.host_next) = err_seen ? -1 : next;
         __threadfence_system();
     }
     st->amax = 0ull;
