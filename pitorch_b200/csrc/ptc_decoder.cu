@@ -1,12 +1,14 @@
 // ptc_decoder.cu -- decode state and the captured CUDA graphs of one
 // position (host side of the decode kernels).
 //
-// Two graphs are captured per decoder, both built from the same PDL-chained
-// kernels (ptc_decode_kernels.cu):
-//   host graph:   [copy {pos, token} from pinned memory] -> kernels ->
-//                 [copy argmax to pinned memory]   (pt_forward_step path)
-//   device graph: kernels only; position and token advance on the device,
-//                 so a whole greedy decode is a chain of graph launches.
+// Graphs captured per decoder, all built from the same PDL-chained kernels
+// (ptc_decode_kernels.cu):
+//   host graph:     [copy {pos, token} from pinned memory] -> kernels; the
+//                   classifier's last CTA stores the argmax into pinned
+//                   memory itself (pt_forward_step path)
+//   device graphs:  kernels only, for one position and for DEV_TOKENS
+//                   positions; position and token advance on the device, so
+//                   a whole greedy decode is a chain of graph launches.
 #include <string.h>
 
 #include "../../include/ptc.h"
@@ -210,8 +212,8 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     }
 
     // Persistent path: one cooperative kernel per launch (see ptc_persist.cu).
-    // Opt-in (PTC_DECODE_PERSIST=1): on B200 its 49 grid-barrier phases per
-    // token currently cost slightly more than the 61-kernel PDL graph.
+    // Opt-in (PTC_DECODE_PERSIST=1): on B200 its grid-barrier phases per
+    // token cost more than the PDL graphs of two kernels per layer.
     const char *want_persist = getenv("PTC_DECODE_PERSIST");
     d->persist = m.L > 0 && ptc::persist_supported(m, d->n_sm) && want_persist && want_persist[0] == '1';
     if (d->persist) {
