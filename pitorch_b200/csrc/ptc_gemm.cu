@@ -423,6 +423,13 @@ static void launch_tile_v(const GemmArgs &g, int kper, cudaStream_t s) {
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
+void launch_splitk_reduce(const GemmArgs &g, int n_sm, cudaStream_t s) {
+    int blocks = (int)(((size_t)g.M * g.N + 255) / 256);
+    if (blocks > 8 * n_sm) blocks = 8 * n_sm;
+    k_splitk_reduce<<<blocks, 256, 0, s>>>(g);
+    PTC_CHECK(cudaGetLastError());
+}
+
 // The vectorised kernel reads float4s along each operand's contiguous
 // dimension: that dimension (K for a k-contiguous operand, else M or N) and
 // the leading dimensions must be multiples of 4, the bases 16-byte aligned.
@@ -443,6 +450,12 @@ void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
         return;
     }
     if (vec_ok(g)) {
+        // The classifier's products (about 2.4 GFLOP each at 15M) on the
+        // tensor cores; the layer products are too small to gain.
+        if (gemm_tc_enabled() && (double)g.M * g.N * g.K >= 1e9 && aligned16(g.C) &&
+            (g.epi != EPI_RESID || aligned16(g.R)) && g.ldc % 4 == 0 && (g.epi != EPI_RESID || g.ldr % 4 == 0) &&
+            gemm_tc(g, n_sm, s))
+            return;
         // Tile: 128x128 when the product alone fills the GPU, else 64x64;
         // then split K (chunks of at least 64, a multiple of the k-tile)
         // until about one wave of CTAs covers the SMs.
@@ -463,12 +476,7 @@ void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
         g.cluster_red = !big && g.splits > 1 && g.splits <= 8 && 64 % g.splits == 0;
         if (big) launch_tile_v<128, 128, 8, 8, 8>(g, kper, s);
         else launch_tile_v<64, 64, 16, 4, 4>(g, kper, s);
-        if (g.splits > 1 && !g.cluster_red) {
-            int blocks = (int)(((size_t)g.M * g.N + 255) / 256);
-            if (blocks > 8 * n_sm) blocks = 8 * n_sm;
-            k_splitk_reduce<<<blocks, 256, 0, s>>>(g);
-            PTC_CHECK(cudaGetLastError());
-        }
+        if (g.splits > 1 && !g.cluster_red) launch_splitk_reduce(g, n_sm, s);
         return;
     }
     const bool big = (long)g.M * g.N >= (long)128 * 128 * n_sm;

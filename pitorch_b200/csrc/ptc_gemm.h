@@ -37,4 +37,12 @@ struct GemmArgs {
 
 void gemm(GemmArgs g, int n_sm, cudaStream_t s);
 
+// Fixed-order sum of g.splits partials from g.partial into C with g's epilogue.
+void launch_splitk_reduce(const GemmArgs &g, int n_sm, cudaStream_t s);
+
+// Tensor-core fp32 GEMM (ptc_gemm_tc.cu), used by gemm() for the large
+// products unless PTC_GEMM_TC=0; returns false when it does not take g.
+bool gemm_tc_enabled();
+bool gemm_tc(const GemmArgs &g, int n_sm, cudaStream_t s);
+
 }  // namespace ptc
