@@ -452,7 +452,7 @@ void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
     if (vec_ok(g)) {
         // The classifier's products (about 2.4 GFLOP each at 15M) on the
         // tensor cores; the layer products are too small to gain.
-        if (gemm_tc_enabled() && (double)g.M * g.N * g.K >= 1e9 && aligned16(g.C) &&
+        if (gemm_tc_enabled() && !g.no_alloc && (double)g.M * g.N * g.K >= 1e9 && aligned16(g.C) &&
             (g.epi != EPI_RESID || aligned16(g.R)) && g.ldc % 4 == 0 && (g.epi != EPI_RESID || g.ldr % 4 == 0) &&
             gemm_tc(g, n_sm, s))
             return;

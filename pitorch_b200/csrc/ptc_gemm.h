@@ -30,6 +30,8 @@ struct GemmArgs {
     float *partial;   // split-K workspace (may be null: no split)
     size_t partial_cap;  // floats available in `partial`
     int splits;       // set by gemm()
+    int no_alloc;     // 1: no allocation may happen (keeps the product off the
+                      // tensor-core kernel, whose workspace is allocated on demand)
     int cluster_red;  // set by gemm(): the splits of a tile form a thread-block
                       // cluster and sum their partials through distributed
                       // shared memory (no workspace, no reduction kernel)

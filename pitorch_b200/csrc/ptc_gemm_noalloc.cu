@@ -84,6 +84,7 @@ extern "C" int ptc_sgemm_noalloc(int M, int N, int K, const float *A, int lda, i
     // them, so whatever an earlier call left in the array is never read.
     g.partial = g_scratch_dev[dev];
     g.partial_cap = PTC_SGEMM_NOALLOC_MAX_MN;
+    g.no_alloc = 1;
     ptc::gemm(g, g_sm_count[dev], (cudaStream_t)stream);
     return 0;
 }
