@@ -4,10 +4,10 @@
 // :475-492).
 //
 // CUTLASS's sm100 "FastFP32" collective (header templates, instantiated here)
-// loads fp32 tiles by TMA (no multicast: cluster 1x1x1), splits each operand
-// element into three bf16 parts in shared memory and sums the leading partial
-// products with tcgen05.mma into fp32 accumulators in tensor memory, which
-// keeps fp32 accuracy. The epilogue is D = A.B (+ C): store, accumulate or
+// loads fp32 tiles by TMA in the non-multicast form (cluster 1x1x1, this
+// GPU's own memory), splits each operand element into three bf16 parts in
+// shared memory and sums all nine partial products with tcgen05.mma into
+// fp32 accumulators in tensor memory, which keeps fp32 accuracy. The epilogue is D = A.B (+ C): store, accumulate or
 // residual add; RoPE products stay on the SIMT kernel.
 //
 // Products whose tile grid cannot fill the GPU (the classifier input
