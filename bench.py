@@ -146,8 +146,10 @@ def run_reference(args, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{MODEL} batch-1 greedy decode", "positions_per_step": sample,
-                   "prompt": N_PROMPT, "parallelism": "cpu-1thread"},
+        # the device arm's workload; each step times a bounded sample of it
+        "config": {"workload": f"{MODEL} batch-1 greedy decode, {cfg[6]} positions per step",
+                   "model": MODEL, "global_batch": 1, "seq_len": cfg[6], "parallelism": "cpu-1thread",
+                   "sample_positions_per_step": sample, "prompt": N_PROMPT},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": impl,
                          "sample": f"first {sample} positions of the seeded 110M decode per step"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
