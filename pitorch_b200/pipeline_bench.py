@@ -102,6 +102,11 @@ def run(args, rank, world):
                     "h2d_bytes_per_step": 8 * seq, "d2h_bytes_per_step": 4 * seq,
                     "wall_ms_per_step": e2e_wall, "token_stream_equals_device_loop": same},
             "gpu_launches": args.steps * launches,
+            # per-kernel rooflines are measured by the N = 1 line (the same
+            # kernels); across stages the decode is one serial stream
+            "roofline": {"kernel": "whole decode step, serial over the pipeline stages", "bound": "hbm",
+                         "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
+                         "traffic": None, "peak_source": f"{src} hbm_gbs"},
             "step_roofline": {"bytes_per_token": mean_bytes, "achieved": step_gbs, "peak": hbm, "unit": "GB/s",
                               "frac": step_gbs / hbm, "peak_source": f"{src} hbm_gbs",
                               "basis": "serial: each token's weights and KV stream once, stage after stage"},
