@@ -416,7 +416,7 @@ def train_flops(cfg, T):
 
 def run_train(args):
     """Training throughput: pt_train_step on the stories15M shape, T = 256
-    seeded tokens, lr 1e-3 (the BASELINE training config), timed with CUDA
+    seeded tokens, lr 1e-3 (the reference's training benchmark settings), timed with CUDA
     events around K whole steps (each returns its loss to the host)."""
     import oracle
     import pitorch_b200
