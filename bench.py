@@ -108,8 +108,10 @@ class ClockSampler:
 # block's KV share is that of those positions, not of the mean position):
 # dram__bytes_read.sum + dram__bytes_write.sum.
 TRAFFIC = {"attention block": 9518848, "ffn block": 18914048, "classifier": 102196000}
-TRAFFIC_SOURCE = ("ncu --set full, one launch each, python bench.py --positions 16 --steps 1 --warmup 1 "
-                  "--no-cpu-baseline (attention block at a position < 16: its KV bytes are those of that position)")
+TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:'k_attn_fused|k_ffn' -s 40 -c 2 "
+                  "-o k_attn_ffn_110M python bench.py --positions 16 --steps 1 --warmup 1 --no-cpu-baseline "
+                  "(profiles/k_attn_fused_k_ffn_110M.md; the attention block at a position < 16, so its "
+                  "KV bytes are those of that position)")
 
 
 def decode_bytes_per_token(cfg, pos):
@@ -124,22 +126,41 @@ def decode_bytes_per_token(cfg, pos):
     return weights + kv + 4 * dim
 
 
+def stratified_positions(n, seq):
+    """n decode positions spread evenly over [0, seq): a CPU sample whose
+    mean cost per token is that of the whole decode (attention grows with
+    the position)."""
+    return [int((k + 0.5) * seq / n) for k in range(n)]
+
+
+def time_cpu_positions(m, positions, n_layers, token=1):
+    """The reference's own forward (pt_forward_embed, pt_forward_layers_range,
+    pt_forward_head: llama2.c:201-206) at each sampled position; the KV rows
+    of earlier positions are whatever the cache holds, which changes no
+    arithmetic cost. Returns seconds."""
+    t0 = time.perf_counter()
+    for p in positions:
+        m.forward_embed(token)
+        m.forward_layers_range(p, 0, n_layers)
+        m.forward_head()
+    return time.perf_counter() - t0
+
+
 def run_reference(args, rank):
     if rank != 0:
         return 0
     import oracle
     cfg = synth.CONFIGS[MODEL]
     blob = synth.make_blob(cfg)
-    prompt = synth.make_prompt(cfg[5], N_PROMPT)
     impl = "reference" if oracle.ref_available() else "port"
     m = oracle.Model(blob, impl=impl)
     sample = 24   # positions per step: a bounded sample of the 1024-position decode
+    positions = stratified_positions(sample, cfg[6])
     for _ in range(args.warmup):
-        m.decode_greedy(prompt, sample)
-    t0 = time.perf_counter()
+        time_cpu_positions(m, positions, cfg[2])
+    dt = 0.0
     for _ in range(args.steps):
-        m.decode_greedy(prompt, sample)
-    dt = time.perf_counter() - t0
+        dt += time_cpu_positions(m, positions, cfg[2])
     v = sample * args.steps / dt
     line = {
         "metric": METRIC, "value": v, "unit": "tokens/s", "impl": "reference",
@@ -151,23 +172,50 @@ def run_reference(args, rank):
                    "model": MODEL, "global_batch": 1, "seq_len": cfg[6], "parallelism": "cpu-1thread",
                    "sample_positions_per_step": sample, "prompt": N_PROMPT},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": impl,
-                         "sample": f"first {sample} positions of the seeded 110M decode per step"},
+                         "sample": f"{sample} positions per step spread evenly over the 1024-position "
+                                   f"decode ({positions[0]}, {positions[1]}, ..., {positions[-1]}), the "
+                                   "reference's staged forward at each, single thread"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-def cpu_baseline_sample(blob, prompt):
+def cpu_baseline_sample(blob, cfg):
     import oracle
     impl = "reference" if oracle.ref_available() else "port"
     m = oracle.Model(blob, impl=impl)
     n = 96
-    t0 = time.perf_counter()
-    m.decode_greedy(prompt, n)
-    dt = time.perf_counter() - t0
+    positions = stratified_positions(n, cfg[6])
+    dt = time_cpu_positions(m, positions, cfg[2])
     return {"value": n / dt, "unit": "tokens/s", "cores": 1, "kind": impl,
-            "sample": f"positions 0..{n - 1} of the seeded 110M greedy decode, single thread"}
+            "sample": f"{n} positions spread evenly over the 1024-position decode ({positions[0]}, "
+                      f"{positions[1]}, ..., {positions[-1]}), the reference's staged forward at each "
+                      "(pt_forward_embed, pt_forward_layers_range, pt_forward_head), single thread"}
+
+
+NEAR_TIE = 1e-5   # top-2 gap / max|logit| below which another fp32 order may flip the argmax
+
+
+def stream_parity(tokens, seq):
+    """The timed decode's token stream against the reference host C's
+    1024-position stream (tests/golden/decode_stories110M_long.npz): equal up
+    to the reference's first near-tie, after which a different fp32
+    summation order may legitimately pick the other token."""
+    path = os.path.join(REPO, "tests", "golden", "decode_stories110M_long.npz")
+    if not os.path.exists(path):
+        return {"fixture": None}
+    g = np.load(path)
+    ref = g["tokens"][:seq]
+    clear = g["top2_gap"][:seq] >= NEAR_TIE * g["logit_absmax"][:seq]
+    clear[: N_PROMPT - 1] = True
+    first_tie = int(np.argmin(clear)) if not clear.all() else seq
+    eq = tokens[:seq] == ref
+    matched = int(np.argmin(eq)) if not eq.all() else seq
+    return {"fixture": "tests/golden/decode_stories110M_long.npz (reference host C)",
+            "compared": "token stream of the last timed step", "first_near_tie": first_tie,
+            "matched_positions": matched, "equal_up_to_first_near_tie": bool(matched > first_tie),
+            "equal_positions": int(eq.sum()), "positions": int(seq)}
 
 
 def run_single(args):
@@ -212,6 +260,8 @@ def run_single(args):
             L.ptc_timer_stop(timer)
             ms_total += L.ptc_timer_ms(timer)
     ms_per_step = ms_total / args.steps
+    toks_timed = np.zeros(seq, np.int32)
+    L.ptc_decoder_read_tokens(dec, api.ip(toks_timed), seq)
     value = seq / (ms_per_step / 1000.0)
 
     # ---- e2e through pt_forward_step (host token in / host token out) -------
@@ -298,9 +348,100 @@ def run_single(args):
                           "roofline_tokens_per_s": hbm * 1e9 / mean_bytes},
         "gpu_launches": args.steps * seq * launches_per_step,
         "clocks": clocks,
+        "parity": stream_parity(toks_timed, seq),
     }
     if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_sample(blob, prompt)
+        line["cpu_baseline"] = cpu_baseline_sample(blob, cfg)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+ATTN_PHASES = [("release after the previous kernel's end", None, 1),
+               ("x read + rmsnorm", 1, 2), ("q/k/v rows resident", 2, 3), ("q/k/v exchange (cluster)", 3, 4),
+               ("attention rounds", 4, 5), ("partial exchange (cluster)", 5, 6),
+               ("merge + wo rows + reductions", 6, 7)]
+FFN_PHASES = [("release after the previous kernel's end", None, 1), ("x read + rmsnorm", 1, 2),
+              ("w1/w3 rows resident", 2, 3), ("silu(h1)*h3 + w2t rows resident", 3, 4),
+              ("w2t product + reductions", 4, 7)]
+CLS_PHASES = [("release after the previous kernel's end", None, 1), ("x read + rmsnorm", 1, 2),
+              ("32000 rows + logits", 2, 6), ("argmax + step state (last CTA)", 6, 7)]
+
+
+def run_timeline(args):
+    """Phase timeline of the decode kernels (ptc_decoder_trace): the 110M
+    device loop runs to position `start` untraced, then 16 positions with
+    every kernel stamping %globaltimer at its phase points. Each phase is the
+    time between the LAST CTA of the kernel passing one point and the last
+    CTA passing the next, so the sum over a position's kernels is its
+    critical path. Medians over the 16 positions (and over layers 1..L-1 for
+    the layer kernels). Stamping adds two atomics per CTA per point, so the
+    traced positions run slightly slower than untraced ones."""
+    import ctypes as C
+    import pitorch_b200
+    from pitorch_b200 import api
+    L = pitorch_b200.lib()
+    cfg = synth.CONFIGS[MODEL]
+    dim, hidden, nl, nh, nkv, V, seq = cfg
+    blob = synth.make_blob(cfg)
+    prompt = synth.make_prompt(V, N_PROMPT)
+    ctx = api.Context(blob)
+    dec = ctx.ptc_decoder()
+    pctx = ctx.ptc_ctx()
+    start = args.timeline_start - args.timeline_start % 8
+    L.ptc_decoder_reset(dec)
+    L.ptc_decoder_generate_begin(dec, api.ip(prompt), N_PROMPT)
+    L.ptc_decoder_enqueue_steps(dec, start)
+    L.ptc_sync(pctx)
+    n = L.ptc_decoder_trace(dec, 1)
+    L.ptc_decoder_enqueue_steps(dec, 16)
+    L.ptc_sync(pctx)
+    buf = (C.c_ulonglong * n)()
+    L.ptc_decoder_read_trace(dec, buf, n)
+    L.ptc_decoder_trace(dec, 0)
+    ctx.close()
+    t = np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(16, 2 * nl + 1, 8, 2)
+    last = t[..., 1]    # latest CTA per event (ns)
+    first = t[..., 0]
+    order = [(start + i) % 16 for i in range(16)]
+
+    def phase_stats(k_list, phases, skip_first_pos=False):
+        out = {}
+        for name, a, b in phases:
+            vals = []
+            for i, slot in enumerate(order):
+                if skip_first_pos and i == 0:
+                    continue
+                for k in k_list:
+                    if a is None:   # previous kernel's end: k-1, or the previous position's classifier
+                        if k > 0:
+                            prev = last[slot, k - 1, 7]
+                        elif i > 0:
+                            prev = last[order[i - 1], 2 * nl, 7]
+                        else:
+                            continue
+                        vals.append(last[slot, k, b] - prev)
+                    else:
+                        vals.append(last[slot, k, b] - last[slot, k, a])
+            out[name] = float(np.median(vals)) / 1000.0 if vals else None
+        return out
+
+    attn = phase_stats([2 * l for l in range(1, nl)], ATTN_PHASES)
+    ffn = phase_stats([2 * l + 1 for l in range(1, nl)], FFN_PHASES)
+    cls = phase_stats([2 * nl], CLS_PHASES)
+    per_pos = [(last[order[i], 2 * nl, 7] - last[order[i - 1], 2 * nl, 7]) / 1000.0 for i in range(1, 16)]
+    layer = [(last[slot, 2 * l + 1, 7] - last[slot, 2 * l - 1, 7]) / 1000.0
+             for slot in order[1:] for l in range(1, nl)]
+    # how early each kernel's CTAs are resident before their release: the
+    # window the weight copies issued before griddepcontrol.wait have
+    lead = {nm: float(np.median([(last[s_, k, 1] - first[s_, k, 0]) / 1000.0 for s_ in order
+                                 for k in ks]))
+            for nm, ks in (("attention block", [2 * l for l in range(1, nl)]),
+                           ("ffn block", [2 * l + 1 for l in range(1, nl)]), ("classifier", [2 * nl]))}
+    line = {"metric": "decode phase timeline (us, median)", "model": MODEL,
+            "positions": [start, start + 15], "us_per_position": float(np.median(per_pos)),
+            "us_per_layer": float(np.median(layer)), "attention_block": attn, "ffn_block": ffn,
+            "classifier": cls, "first_cta_start_to_release_us": lead,
+            "note": "latest CTA per phase point; traced positions pay two atomics per CTA per point"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -478,9 +619,14 @@ def main():
                     help="isolated fp32 matvec sweep (one JSON line per W shape) instead of the decode")
     ap.add_argument("--sweep-shapes", default="", help="e.g. 32000x768,2048x768 (default: the 9 shapes)")
     ap.add_argument("--train", action="store_true", help="stories15M training step (T=256) instead of the decode")
+    ap.add_argument("--timeline", action="store_true",
+                    help="phase timeline of the decode kernels over 16 positions (ptc_decoder_trace)")
+    ap.add_argument("--timeline-start", type=int, default=504, help="first traced position (multiple of 8)")
     args = ap.parse_args()
     if args.sweep:
         return run_sweep(args)
+    if args.timeline:
+        return run_timeline(args)
     if args.train and args.impl != "reference" and int(os.environ.get("WORLD_SIZE", "1")) == 1:
         return run_train(args)
     rank = int(os.environ.get("RANK", "0"))

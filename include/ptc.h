@@ -173,15 +173,18 @@ int ptc_wait_deadline(ptc_ctx *c, int timeout_ms);
 
 /* Weights were updated in place (training): refresh derived device copies. */
 void ptc_decoder_weights_updated(ptc_decoder *d);
-/* 1 when the decoder runs each launch as the single persistent kernel. */
-int ptc_decoder_is_persistent(ptc_decoder *d);
-/* Phase timeline of the persistent kernel (profiling): record, for the
- * first max_barriers grid barriers of each launch, when CTA 0 finished its
- * phase work and when the barrier released (%globaltimer ns, 2 entries per
- * barrier). max_barriers <= 0 turns it off. ptc_decoder_read_trace copies up
- * to n entries out and returns how many. */
-void ptc_decoder_trace(ptc_decoder *d, int max_barriers);
-int ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, int n);
+/* Phase timeline of the decode kernels (profiling; no reference
+ * counterpart -- the reference's trace.c records host spans only). on != 0
+ * clears the record and makes the attention block, the FFN block and the
+ * classifier stamp %globaltimer (ns) at fixed points of their work; 0 stops
+ * it. For position p (recorded modulo 16), kernel k (2l: attention block of
+ * layer l, 2l+1: FFN block of layer l, 2L: classifier) and event e < 8,
+ * entries 2i and 2i+1 with i = ((p % 16) * (2L + 1) + k) * 8 + e hold the
+ * earliest and the latest stamp over the kernel's CTAs (an event a kernel
+ * does not have keeps ~0 / 0). Returns the number of entries;
+ * ptc_decoder_read_trace copies up to n of them and returns how many. */
+size_t ptc_decoder_trace(ptc_decoder *d, int on);
+size_t ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, size_t n);
 
 /* ---- GEMM: replaces sgemm_rect_tmu (pitorch/ops/gemm/gemm_rect.h:13-27,
  *      gemm_rect.c:28-104), C[M][N] (+)= A[M][K] * B[K][N] -------------------- */
@@ -199,6 +202,13 @@ void ptc_sgemm(int M, int N, int K, const float *A, int lda, int a_kcontig,
                const float *B, int ldb, int b_kcontig, float *C, int ldc, int accumulate,
                float *workspace, size_t workspace_floats, void *stream);
 
+/* Launch counters of the GEMM paths since the library was loaded (no
+ * reference counterpart; the Pi build has one QPU path). out[0] tensor-core
+ * (tcgen05) kernels, out[1] SIMT tile kernels, out[2] split-K reduction
+ * kernels, out[3] SIMT launches whose K-splits were summed inside a
+ * thread-block cluster. Counts are per process and cover every device. */
+void ptc_gemm_counters(long long out[4]);
+
 /* ptc_sgemm for callers that cannot allocate device memory -- no
  * counterpart in the reference. Code that runs while a stream is being
  * captured into a CUDA graph, inside an allocator callback, or under a host
@@ -208,7 +218,10 @@ void ptc_sgemm(int M, int N, int K, const float *A, int lda, int a_kcontig,
  * PTC_SGEMM_NOALLOC_MAX_MN floats (4 MiB) that every GPU loading the library
  * keeps until exit. Same product and layouts as ptc_sgemm.
  *  - Returns 0 on success, -1 (with a message on stderr) when M*N exceeds
- *    PTC_SGEMM_NOALLOC_MAX_MN or the device set-up fails.
+ *    PTC_SGEMM_NOALLOC_MAX_MN or the device set-up fails. A kernel launch
+ *    that the CUDA runtime rejects (an invalid launch, or one made inside a
+ *    capture that does not allow it) aborts the process, as every CUDA
+ *    failure of this library does; it does not return -1.
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress) for that device; make that first call before
  *    any stream capture.

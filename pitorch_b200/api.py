@@ -209,9 +209,9 @@ def declare(L):
     _sig(L, "ptc_decoder_enqueue_steps", None, vp, C.c_int)
     _sig(L, "ptc_decoder_read_tokens", None, vp, i32p, C.c_int)
     _sig(L, "ptc_decoder_reset", None, vp)
-    _sig(L, "ptc_decoder_is_persistent", C.c_int, vp)
-    _sig(L, "ptc_decoder_trace", None, vp, C.c_int)
-    _sig(L, "ptc_decoder_read_trace", C.c_int, vp, C.POINTER(C.c_ulonglong), C.c_int)
+    _sig(L, "ptc_decoder_trace", C.c_size_t, vp, C.c_int)
+    _sig(L, "ptc_decoder_read_trace", C.c_size_t, vp, C.POINTER(C.c_ulonglong), C.c_size_t)
+    _sig(L, "ptc_gemm_counters", None, C.POINTER(C.c_longlong))
     _sig(L, "ptc_decoder_enqueue_embed", None, vp, C.c_int)
     _sig(L, "ptc_decoder_enqueue_layers", None, vp, C.c_int, C.c_int, C.c_int)
     _sig(L, "ptc_decoder_enqueue_head", None, vp)
@@ -219,6 +219,10 @@ def declare(L):
     _sig(L, "ptc_decoder_launches_per_step", C.c_int, vp)
     _sig(L, "ptc_decoder_fetch_next", C.c_int, vp, f32p)
     _sig(L, "ptc_decoder_step", C.c_int, vp, C.c_int, C.c_int, f32p)
+    _sig(L, "ptc_mailbox_alloc", vp, vp, C.c_int)
+    _sig(L, "ptc_mailbox_free", None, vp)
+    _sig(L, "ptc_hop_send", None, vp, vp, vp, vp, vp, C.c_int)
+    _sig(L, "ptc_hop_recv", None, vp, vp, vp, vp, vp, C.c_int, vp, C.c_longlong)
     _sig(L, "ptc_timer_create", vp, vp)
     _sig(L, "ptc_timer_start", None, vp)
     _sig(L, "ptc_timer_stop", None, vp)

@@ -186,6 +186,12 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Order-preserving map of a float to uint32 (larger float -> larger key).
 __device__ __forceinline__ uint32_t float_key(float f) {
     uint32_t u = __float_as_uint(f);
@@ -230,10 +236,52 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// L2 eviction priority of this kernel's own loads (createpolicy; no device
+// setting changes): POL_NONE issues the plain forms.
+enum L2Pol { POL_NONE = 0, POL_FIRST = 1, POL_LAST = 2, POL_NORMAL = 3 };
+__device__ __forceinline__ uint64_t make_l2_policy(int kind) {
+    uint64_t p = 0;
+    if (kind == POL_FIRST) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    else if (kind == POL_LAST) asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    else if (kind == POL_NORMAL) asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// bulk_g2s with an L2 cache policy (kind != POL_NONE) or without.
+__device__ __forceinline__ void bulk_g2s_pol(void *dst, const void *src, unsigned bytes, uint64_t *bar, int kind,
+                                             uint64_t pol) {
+    if (kind == POL_NONE) {
+        bulk_g2s(dst, src, bytes, bar);
+        return;
+    }
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 // Per-thread asynchronous 16-byte global->shared copies (dst, src 16-byte
 // aligned), completed by cp_async_wait_all.
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16_pol(void *dst, const void *src, int kind, uint64_t pol) {
+    if (kind == POL_NONE) {
+        cp_async16(dst, src);
+        return;
+    }
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "l"(pol)
+                 : "memory");
+}
+// 128-bit L2-only load with an L2 cache policy (or the plain __ldcg).
+__device__ __forceinline__ float4 ldcg_pol(const float4 *p, int kind, uint64_t pol) {
+    if (kind == POL_NONE) return __ldcg(p);
+    float4 v;
+    asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
@@ -242,6 +290,14 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_pol(const void *src, unsigned bytes, int kind, uint64_t pol) {
+    if (kind == POL_NONE) {
+        prefetch_l2(src, bytes);
+        return;
+    }
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(pol)
+                 : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
     unsigned ok;

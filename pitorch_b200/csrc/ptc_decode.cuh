@@ -15,7 +15,7 @@ struct StepState {
     int next;                 // argmax of this step's logits
     int n_prompt;             // device-loop mode: prompt length
     int mode;                 // 0: host drives pos/tok; 1: device loop
-    int pad0;
+    int trace_on;             // 1: kernels stamp the phase timeline
     unsigned done;            // classifier CTAs finished (reset by the last)
     unsigned pad1;
     unsigned long long amax;  // packed (value, index) running argmax
@@ -63,7 +63,19 @@ struct DecodeModel {
     // while the previous token's classifier still runs.
     int tok_off;
     int adv;
+    // Phase timeline (ptc_decoder_trace), stamped only while step->trace_on:
+    // for traced position p, kernel k of the position (2l: attention block of
+    // layer l, 2l+1: its FFN block, 2L: the classifier) and event e, the
+    // earliest and the latest %globaltimer over the kernel's CTAs at
+    // trace[2 * (((p % TRACE_POS) * (2L + 1) + k) * TRACE_EV + e)] (+1).
+    unsigned long long *trace;
+    // L2 eviction priorities (L2Pol) of the kernels' own loads: layer weights,
+    // classifier rows, KV cache rows.
+    int pol_w, pol_cls, pol_kv;
 };
+
+constexpr int TRACE_POS = 16;
+constexpr int TRACE_EV = 8;
 
 // Decode matvec staging: each CTA streams its contiguous block of weight rows
 // through a ring of shared-memory stages filled by bulk (TMA) copies.
@@ -78,5 +90,6 @@ constexpr int FF_MAX_SMEM = 200 * 1024;
 
 // Error codes written to DecodeModel::err.
 constexpr int ERR_MBAR_TIMEOUT = 1;
+constexpr int ERR_POS_RANGE = 2;   // a kernel was asked for a position outside [0, seq_len)
 
 }  // namespace ptc

@@ -127,6 +127,26 @@ __device__ __forceinline__ void store_vec(float *dst, const float4 (&x)[NV], int
     }
 }
 
+// Phase timeline stamp by thread 0 of a CTA, only while tracing: the slot of
+// (position, kernel k, event e) keeps the earliest and the latest time.
+__device__ __forceinline__ void trace_ev(const DecodeModel &m, bool on, int pos, int k, int e) {
+    if (!on || threadIdx.x != 0) return;
+    const unsigned long long t = globaltimer_ns();
+    unsigned long long *slot = m.trace + 2 * (((size_t)(pos % TRACE_POS) * (2 * m.L + 1) + k) * TRACE_EV + e);
+    atomicMin(slot, t);
+    atomicMax(slot + 1, t);
+}
+
+__device__ __forceinline__ bool trace_on(const DecodeModel &m) {
+    return m.trace != nullptr && __ldcg(&m.step->trace_on) != 0;
+}
+
+// A position outside the KV cache: the kernels compute nothing that could be
+// mistaken for a result of it and record the error for the host.
+__device__ __forceinline__ void flag_pos_range(const DecodeModel &m) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicExch(m.err, ERR_POS_RANGE);
+}
+
 // ---------------------------------------------------------------------------
 // k_attn: grid (n_heads, n_chunks), 256 threads. CTA (h, c) covers positions
 // [c*CH, c*CH+CH) ∩ [0, pos] (CH = 64): scores q.k * 1/sqrt(hd), a
@@ -159,7 +179,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
     // launches (earlier tokens, or this graph's first node), so they are
     // read before the wait; only q and the row of `pos` come from the
     // kernel this one depends on.
-    const int pos = min(__ldcg(&m.step->pos) + m.tok_off, m.seq - 1);
+    const int pos_raw = __ldcg(&m.step->pos) + m.tok_off;
+    if (pos_raw < 0 || pos_raw >= m.seq) {
+        flag_pos_range(m);
+        return;
+    }
+    const int pos = pos_raw;
     const int t0 = c * CH;
     const int nc = pos / CH + 1;   // chunks holding positions <= pos
     if (c >= nc) return;           // no positions here: not part of the merge
@@ -365,7 +390,7 @@ struct MvArgs {
 
 template <int MODE>
 __device__ __forceinline__ void mv_issue(const DecodeModel &m, const MvArgs &a, float *stage, uint64_t *bar,
-                                         int c0, int c1) {
+                                         int c0, int c1, uint64_t pol) {
     const size_t rb = (size_t)a.cols * 4;  // bytes per row
     const int n = c1 - c0;
     if (MODE == MV_QKV) {
@@ -389,7 +414,8 @@ __device__ __forceinline__ void mv_issue(const DecodeModel &m, const MvArgs &a, 
         bulk_g2s(stage + (size_t)a.per_stage * a.cols, m.w3 + off, (unsigned)(n * rb), bar);
     } else {
         mbar_expect_tx(bar, (unsigned)(n * rb));
-        bulk_g2s(stage, a.W + (size_t)c0 * a.cols, (unsigned)(n * rb), bar);
+        bulk_g2s_pol(stage, a.W + (size_t)c0 * a.cols, (unsigned)(n * rb), bar, MODE == MV_CLS ? m.pol_cls : POL_NONE,
+                     pol);
     }
 }
 
@@ -428,15 +454,20 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         mbar_init_fence();
     }
     __syncthreads();
+    const uint64_t cls_pol = MODE == MV_CLS ? make_l2_policy(m.pol_cls) : 0ull;
     if (tid == 0)
         for (int k = 0; k < n_chunks && k < NST; k++)
-            mv_issue<MODE>(m, a, stages + k * stage_floats, &bars[k], it0 + k * ps, min(it1, it0 + (k + 1) * ps));
+            mv_issue<MODE>(m, a, stages + k * stage_floats, &bars[k], it0 + k * ps, min(it1, it0 + (k + 1) * ps),
+                           cls_pol);
 
     // Everything that does not come from the kernel this one depends on is
     // loaded before the wait: rmsnorm gains (weights), the position and --
     // for layer 0 -- the token's embedding row (set by an earlier launch).
     float4 xr[NV], gr[NV];
     int pos = 0;
+    const bool tr = MODE == MV_CLS && trace_on(m);
+    const int tpos = MODE == MV_CLS ? __ldcg(&m.step->pos) + m.tok_off : 0;
+    trace_ev(m, tr, tpos, 2 * m.L, 0);
     if (MODE == MV_QKV) {
         pos = __ldcg(&m.step->pos) + m.tok_off;
         load_gain<NV>(gr, m.rms_att + (size_t)a.l * m.dim, c4, lane);
@@ -448,6 +479,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         load_gain<NV>(gr, m.rms_final, c4, lane);
     }
     pdl_wait();
+    trace_ev(m, tr, tpos, 2 * m.L, 1);
     // residual rows this warp will update (RESID): issued with the input
     constexpr int XPRE = 4;
     float xres[XPRE];
@@ -473,10 +505,12 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         load_act<NV>(xr, m.x, c4, lane);
         rmsnorm_pre<NV>(xr, gr, m.dim);
         if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.xn, xr, c4, lane);
+        trace_ev(m, tr, tpos, 2 * m.L, 2);
     } else {
         load_act<NV>(xr, a.in, c4, lane);
     }
     const bool pos_ok = (MODE != MV_QKV) || (pos >= 0 && pos < m.seq);
+    if (!pos_ok) flag_pos_range(m);
 
     unsigned long long best = 0ull;
     bool ok = true;
@@ -568,7 +602,8 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             if (tid == 0 && k + NST < n_chunks) {
                 fence_proxy_async_smem();
                 const int kk = k + NST;
-                mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps));
+                mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps),
+                               cls_pol);
             }
         }
     }
@@ -577,6 +612,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
 
     if (lane == 0) s_best[warp] = best;
     __syncthreads();
+    trace_ev(m, tr, tpos, 2 * m.L, 6);
     StepState *st = m.step;
     int err_seen = 0;   // thread 0: an earlier kernel's expired wait (host steps)
     if (tid == 0) {
@@ -611,6 +647,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         if (m.adv) st->pos = p + 1;
     }
     __threadfence();
+    trace_ev(m, tr, tpos, 2 * m.L, 7);
 }
 
 // ---------------------------------------------------------------------------
@@ -651,6 +688,9 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
     const int j1 = (int)((long)m.hidden * (blockIdx.x + 1) / gridDim.x);
     const int nj = j1 - j0;
     const unsigned bytes = (unsigned)nj * (unsigned)dim * 4u;
+    const bool tr = trace_on(m);
+    const int tpos = tr ? __ldcg(&m.step->pos) + m.tok_off : 0;
+    trace_ev(m, tr, tpos, 2 * a.l + 1, 0);
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -662,17 +702,21 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
         // per matrix measured 3.6 us/token slower at 110M)
         const size_t off = ((size_t)a.l * m.hidden + j0) * dim;
         const unsigned rb = (unsigned)dim * 4u;
+        const int pk = m.pol_w;
+        const uint64_t pol = make_l2_policy(pk);
         mbar_expect_tx(&bars[0], 2u * bytes);
         mbar_expect_tx(&bars[1], bytes);
         for (int j = 0; j < nj; j++) {
-            bulk_g2s(w1s + (size_t)j * dim, m.w1 + off + (size_t)j * dim, rb, &bars[0]);
-            bulk_g2s(w3s + (size_t)j * dim, m.w3 + off + (size_t)j * dim, rb, &bars[0]);
+            bulk_g2s_pol(w1s + (size_t)j * dim, m.w1 + off + (size_t)j * dim, rb, &bars[0], pk, pol);
+            bulk_g2s_pol(w3s + (size_t)j * dim, m.w3 + off + (size_t)j * dim, rb, &bars[0], pk, pol);
         }
-        for (int j = 0; j < nj; j++) bulk_g2s(w2s + (size_t)j * dim, m.w2t + off + (size_t)j * dim, rb, &bars[1]);
+        for (int j = 0; j < nj; j++)
+            bulk_g2s_pol(w2s + (size_t)j * dim, m.w2t + off + (size_t)j * dim, rb, &bars[1], pk, pol);
     }
     float4 xr[NV], gr[NV];
     load_gain<NV>(gr, m.rms_ffn + (size_t)a.l * dim, c4, lane);
     pdl_wait();
+    trace_ev(m, tr, tpos, 2 * a.l + 1, 1);
     load_act<NV>(xr, a.xin, c4, lane);
     // the residual this thread adds (CTA 0): issued with the input
     constexpr int RV = 2;   // float4 columns per thread: dim <= 4 * RV * FF_THREADS
@@ -684,6 +728,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     rmsnorm_pre<NV>(xr, gr, dim);
+    trace_ev(m, tr, tpos, 2 * a.l + 1, 2);
     // The input is consumed by rmsnorm; the residual registers are forced
     // here. Once the barrier below has passed, every thread of the CTA has
     // done so: the CTA then takes its ticket, looked at when it ends.
@@ -693,6 +738,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
     // A failed wait is recorded in m.err; the CTA then skips its products
     // but still takes part in the ticket.
     bool ok = __syncthreads_and(mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT));
+    trace_ev(m, tr, tpos, 2 * a.l + 1, 3);
     unsigned ticket = 0u;
     if (a.xclear && tid == FF_THREADS - 1) ticket = atomicAdd(&m.tickets[1], 1u);
     if (ok)
@@ -703,6 +749,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
         }
     if (ok) ok = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
     ok = __syncthreads_and(ok);   // also publishes s_hb
+    trace_ev(m, tr, tpos, 2 * a.l + 1, 4);
     if (ok) {
         const float4 *w2s4 = reinterpret_cast<const float4 *>(w2s);
 #pragma unroll
@@ -725,6 +772,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
         mbar_wait_bounded(&bars[0], 0u, nullptr, 0);
         mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
     }
+    trace_ev(m, tr, tpos, 2 * a.l + 1, 7);
     if (a.xclear) {
         if (tid == FF_THREADS - 1) s_last = (ticket == gridDim.x - 1);
         __syncthreads();
@@ -798,7 +846,12 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     const int o0 = dim * r / AC, o1 = dim * (r + 1) / AC;         // wo rows of this CTA
     const int pos_raw = __ldcg(&m.step->pos) + m.tok_off;
     const bool pos_ok = pos_raw >= 0 && pos_raw < m.seq;
+    // out of range: computed at position 0 so that every cluster barrier is
+    // still reached, with no K/V write and the error recorded
     const int pos = pos_ok ? pos_raw : 0;
+    if (!pos_ok) flag_pos_range(m);
+    const bool tr = trace_on(m);
+    trace_ev(m, tr, pos, 2 * l, 0);
     // positions of this CTA: [t0, t1) of [0, pos]
     const int ppc = (pos + AC) / AC;
     const int t0 = min(r * ppc, pos + 1), t1 = min(t0 + ppc, pos + 1);
@@ -809,6 +862,8 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         mbar_init_fence();
     }
     __syncthreads();
+    const int pkw = m.pol_w, pkk = m.pol_kv;
+    const uint64_t polw = make_l2_policy(pkw), polk = make_l2_policy(pkk);
     if (tid == 0) {
         const size_t D = dim, K = m.kvd;
         const float *mats[3] = {m.wq + (size_t)l * D * D, m.wk + (size_t)l * K * D, m.wv + (size_t)l * K * D};
@@ -818,16 +873,16 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         for (int sgm = 0; sgm < 3; sgm++) {
             const int lo = max(q0, sgm * hd), hi = min(q1, (sgm + 1) * hd);
             for (int r = lo; r < hi; r++)
-                bulk_g2s(stage + (size_t)(r - q0) * dim, mats[sgm] + (size_t)(h * hd + r - sgm * hd) * dim,
-                         (unsigned)(dim * 4), &bars[0]);
+                bulk_g2s_pol(stage + (size_t)(r - q0) * dim, mats[sgm] + (size_t)(h * hd + r - sgm * hd) * dim,
+                             (unsigned)(dim * 4), &bars[0], pkw, polw);
         }
     }
     if (tid == 32 && t1 - t0 > AT_ROUND) {
         // positions past the first round are read after the wait: warm L2
         const int tp = t0 + AT_ROUND, te = min(t1, pos);
         if (te > tp) {
-            prefetch_l2(m.kc + (head_base + tp) * hd, (unsigned)((te - tp) * hd * 4));
-            prefetch_l2(m.vc + (head_base + tp) * hd, (unsigned)((te - tp) * hd * 4));
+            prefetch_l2_pol(m.kc + (head_base + tp) * hd, (unsigned)((te - tp) * hd * 4), pkk, polk);
+            prefetch_l2_pol(m.vc + (head_base + tp) * hd, (unsigned)((te - tp) * hd * 4), pkk, polk);
         }
     }
     // K/V rows of the first round's earlier positions: written by earlier
@@ -843,13 +898,13 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
 #pragma unroll
         for (int i = 0; i < QK; i++) {
             const int cc = sub + 4 * i;
-            kv[i] = (cc < hd4 && js < n0 && t0 + js != pos) ? __ldcg(kb + (size_t)js * hd4 + cc)
+            kv[i] = (cc < hd4 && js < n0 && t0 + js != pos) ? ldcg_pol(kb + (size_t)js * hd4 + cc, pkk, polk)
                                                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int k = 0; k < VP; k++) {
             const int j = grp + ngrp * k;
-            vpre[k] = (grp < ngrp && j < n0 && t0 + j != pos) ? __ldcg(vb + (size_t)j * hd4 + d4)
+            vpre[k] = (grp < ngrp && j < n0 && t0 + j != pos) ? ldcg_pol(vb + (size_t)j * hd4 + d4, pkk, polk)
                                                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
@@ -873,16 +928,19 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     // ordering needed here, so the relaxed form)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
     pdl_wait();
+    trace_ev(m, tr, pos, 2 * l, 1);
     if (!a.xin && m.tok_off != 0) xsrc = m.emb + (size_t)__ldcg(&m.step->tok) * dim;
     if (a.xin || m.tok_off != 0) load_act<NV>(xr, xsrc, c4, lane);
     if (h == 0)
         for (int i = tid; i < (o1 - o0) / 4; i += AT_THREADS)
             reinterpret_cast<float4 *>(s_res)[i] = __ldcg(reinterpret_cast<const float4 *>(xsrc + o0) + i);
     rmsnorm_pre<NV>(xr, gr, dim);
+    trace_ev(m, tr, pos, 2 * l, 2);
 
     // 1. q/k/v row pairs, RoPE on the q and k pairs (llama2.c:238-245), then
     //    to every CTA's s_qkv
     bool bad = !mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT);
+    trace_ev(m, tr, pos, 2 * l, 3);
 #pragma unroll
     for (int k = 0; k < AT_PAIRS; k++) {
         const int pr = q0 + 2 * warp + 2 * NW * k;
@@ -919,7 +977,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         const float *wo_base = m.wo + (size_t)l * dim * dim + (size_t)h * hd;
         for (int f = tid; f < (o1 - o0) * hd4; f += AT_THREADS) {
             const int row = f / hd4, c = f - row * hd4;
-            cp_async16(stage + (size_t)row * hd + 4 * c, wo_base + (size_t)(o0 + row) * dim + 4 * c);
+            cp_async16_pol(stage + (size_t)row * hd + 4 * c, wo_base + (size_t)(o0 + row) * dim + 4 * c, pkw, polw);
         }
     }
     // K/V rows of the earlier positions past the first round: copied now
@@ -934,12 +992,13 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     if (n2 > 0) {
         const float *kb = m.kc + (head_base + p2) * hd, *vb = m.vc + (head_base + p2) * hd;
         for (int f = tid; f < n2 * hd4; f += AT_THREADS) {
-            cp_async16(kv2 + 4 * f, kb + 4 * f);
-            cp_async16(kv2 + (size_t)n2 * hd + 4 * f, vb + 4 * f);
+            cp_async16_pol(kv2 + 4 * f, kb + 4 * f, pkk, polk);
+            cp_async16_pol(kv2 + (size_t)n2 * hd + 4 * f, vb + 4 * f, pkk, polk);
         }
     }
     cp_async_commit();
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // s_qkv complete
+    trace_ev(m, tr, pos, 2 * l, 4);
     // 2. attention over [t0, t1): online softmax in rounds of AT_ROUND
     const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
     float4 qv[QK];
@@ -963,7 +1022,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
                 const int cc = sub + 4 * i, p = rt0 + js;
                 float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (cc < hd4 && js < n && p != pos)
-                    val = (p - p2 < n2) ? ks[(size_t)(p - p2) * hd4 + cc] : __ldcg(kb + (size_t)js * hd4 + cc);
+                    val = (p - p2 < n2) ? ks[(size_t)(p - p2) * hd4 + cc] : ldcg_pol(kb + (size_t)js * hd4 + cc, pkk, polk);
                 kv[i] = val;
             }
 #pragma unroll
@@ -971,7 +1030,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
                 const int j = grp + ngrp * k, p = rt0 + j;
                 float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (grp < ngrp && j < n && p != pos)
-                    val = (p - p2 < n2) ? vs[(size_t)(p - p2) * hd4 + d4] : __ldcg(vb + (size_t)j * hd4 + d4);
+                    val = (p - p2 < n2) ? vs[(size_t)(p - p2) * hd4 + d4] : ldcg_pol(vb + (size_t)j * hd4 + d4, pkk, polk);
                 vpre[k] = val;
             }
         }
@@ -1031,6 +1090,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
         if (rt0 + AT_ROUND < t1) __syncthreads();   // s_sc and s_o are reused by the next round
     }
+    trace_ev(m, tr, pos, 2 * l, 5);
     // partial of this CTA -> slot r of every CTA
     if (tid < hd)
         for (int k = 0; k < AC; k++) cluster.map_shared_rank(&s_part[0][0], k)[r * (AT_MAX_HD + 4) + tid] = o_run;
@@ -1041,6 +1101,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             p[AT_MAX_HD + 1] = l_run;
         }
     cluster.sync();
+    trace_ev(m, tr, pos, 2 * l, 6);
 
     // 3. merge the AC partials (every output thread, same order in every
     // CTA), then wo
@@ -1088,6 +1149,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         float *dst = (tid < hd ? m.kc : m.vc) + (head_base + pos) * hd + d;
         *dst = s_qkv[(tid < hd ? hd : 2 * hd) + d];
     }
+    trace_ev(m, tr, pos, 2 * l, 7);
     if (tid == AT_THREADS - 1) s_last = (ticket == gridDim.x - 1);
     __syncthreads();
     if (s_last) {
@@ -1377,6 +1439,30 @@ __global__ void k_embed(DecodeModel m) {
 
 void launch_embed(const DecodeModel &m, cudaStream_t s) {
     launch_pdl(k_embed, dim3((m.dim + 255) / 256), dim3(256), 0, s, m);
+}
+
+// dst[c][r] = src[r][c] for a rows x cols matrix, through a padded 32x32 tile.
+__global__ void k_transpose(float *dst, const float *src, int rows, int cols) {
+    __shared__ float tile[32][33];
+    const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int r = by + j, c = bx + threadIdx.x;
+        if (r < rows && c < cols) tile[j][threadIdx.x] = src[(size_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int c = bx + j, r = by + threadIdx.x;
+        if (c < cols && r < rows) dst[(size_t)c * rows + r] = tile[threadIdx.x][j];
+    }
+}
+
+// w2t[l] = w2[l]^T for each layer ([dim, hidden] -> [hidden, dim]): the FFN
+// block reads the w2 column of each of its hidden units as one contiguous row.
+void transpose_w2(const DecodeModel &m, float *w2t, cudaStream_t s) {
+    for (int l = 0; l < m.L; l++)
+        k_transpose<<<dim3((m.hidden + 31) / 32, (m.dim + 31) / 32), dim3(32, 8), 0, s>>>(
+            w2t + (size_t)l * m.hidden * m.dim, m.w2 + (size_t)l * m.dim * m.hidden, m.dim, m.hidden);
+    PTC_CHECK(cudaGetLastError());
 }
 
 // RoPE factors (cos, sin) of every (position, pair) with pitorch's angle and

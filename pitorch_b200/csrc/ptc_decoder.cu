@@ -9,13 +9,13 @@
 //   device graphs:  kernels only, for one position and for DEV_TOKENS
 //                   positions; position and token advance on the device, so
 //                   a whole greedy decode is a chain of graph launches.
+#include <stdio.h>
 #include <string.h>
 
 #include "../../include/ptc.h"
 #include "ptc_common.cuh"
 #include "ptc_decode.cuh"
 #include "ptc_internal.h"
-#include "ptc_persist.h"
 
 using ptc::DecodeModel;
 using ptc::StepState;
@@ -38,10 +38,8 @@ struct ptc_decoder {
     int mode;              // current StepState.mode on the device
     cudaGraphExec_t g_host, g_dev;
     cudaGraphExec_t g_devk;  // DEV_TOKENS device-loop tokens per launch (null: not used)
-    // persistent single-kernel path (ptc_persist.cu)
-    bool persist;
-    ptc::PersistArgs pa;
-    int loop_pos;          // device-loop mode: next position to decode
+    size_t trace_n;        // entries of m.trace
+    int trace_on;          // host copy of step->trace_on
 };
 
 static void enqueue_kernels(ptc_decoder *d, const DecodeModel &m, cudaStream_t s, int *host_next) {
@@ -77,6 +75,8 @@ static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
 static void check_err(ptc_decoder *d) {
     int e = 0;
     PTC_CHECK(cudaMemcpy(&e, d->m.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e == ptc::ERR_POS_RANGE)
+        PTC_FATAL("decode kernel reported error %d: a position at or past seq_len %d was decoded", e, d->m.seq);
     if (e) PTC_FATAL("decode kernel reported error %d (bounded wait on a weight stage expired)", e);
 }
 
@@ -159,6 +159,17 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     m.fused_ffn = m.L > 0 && m.ffn_rows > 0 && !no_fuse;
     m.attn_stage = ptc::decode_attn_stage(m.dim, m.nh, m.nkv, m.seq);
     m.fused_attn = m.fused_ffn && m.attn_stage > 0 && !ffn_only;
+    // L2 eviction priorities of the fused kernels' own loads. PTC_L2_POLICY
+    // = "w,cls,kv" with 0 none, 1 evict_first, 2 evict_last, 3 evict_normal
+    // (default: none).
+    if (const char *pe = getenv("PTC_L2_POLICY")) {
+        int a = 0, b = 0, k = 0;
+        if (sscanf(pe, "%d,%d,%d", &a, &b, &k) == 3 && a >= 0 && a <= 3 && b >= 0 && b <= 3 && k >= 0 && k <= 3) {
+            m.pol_w = a;
+            m.pol_cls = b;
+            m.pol_kv = k;
+        }
+    }
     m.tickets = (unsigned *)ptc_alloc(c, 64);
     PTC_CHECK(cudaMemsetAsync(m.tickets, 0, 64, s));
     if (m.fused_attn) {
@@ -166,11 +177,13 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
         ptc::build_rope_table(rope, m.seq, m.hd, s);
         m.rope = rope;
     }
-    if (m.fused_ffn || (m.L > 0 && ptc::persist_supported(m, d->n_sm))) {
+    if (m.fused_ffn) {
         float *w2t = (float *)ptc_alloc(c, (size_t)m.L * m.hidden * m.dim * 4);
-        ptc::persist_transpose_w2(m, w2t, s);
+        ptc::transpose_w2(m, w2t, s);
         m.w2t = w2t;
     }
+    d->trace_n = (size_t)2 * ptc::TRACE_POS * (2 * m.L + 1) * ptc::TRACE_EV;
+    m.trace = (unsigned long long *)ptc_alloc(c, d->trace_n * sizeof(unsigned long long));
     if (m.fused_ffn) {
         m.xm = (float *)ptc_alloc(c, (size_t)m.dim * 4);
         m.xo = (float *)ptc_alloc(c, (size_t)m.L * m.dim * 4);
@@ -211,67 +224,36 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
         PTC_CHECK(cudaGraphDestroy(g));
     }
 
-    // Persistent path: one cooperative kernel per launch (see ptc_persist.cu).
-    // Opt-in (PTC_DECODE_PERSIST=1): on B200 its grid-barrier phases per
-    // token cost more than the PDL graphs of two kernels per layer.
-    const char *want_persist = getenv("PTC_DECODE_PERSIST");
-    d->persist = m.L > 0 && ptc::persist_supported(m, d->n_sm) && want_persist && want_persist[0] == '1';
-    if (d->persist) {
-        int coop = 0;
-        PTC_CHECK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ptc_device(c)));
-        if (!coop) d->persist = false;
-    }
-    if (d->persist) {
-        ptc::PersistArgs &pa = d->pa;
-        memset(&pa, 0, sizeof(pa));
-        pa.m = m;
-        pa.has_embed = has_embed;
-        pa.has_head = has_head;
-        pa.w2t = m.w2t;
-        pa.x1 = (float *)ptc_alloc(c, (size_t)m.dim * 4);
-        pa.max_chunks = d->n_sm / m.nh > 0 ? d->n_sm / m.nh : 1;
-        pa.att_part = (float *)ptc_alloc(c, (size_t)m.nh * pa.max_chunks * (m.hd + 2) * 4);
-        pa.bar = (unsigned *)ptc_alloc(c, 256);
-        PTC_CHECK(cudaStreamSynchronize(s));
-    }
-    d->loop_pos = 0;
     return d;
 }
 
 // Re-derive device-side copies that depend on the weights (the transposed
-// w2 of the fused FFN and the persistent path) after an in-place update.
+// w2 of the fused FFN) after an in-place update.
 extern "C" void ptc_decoder_weights_updated(ptc_decoder *d) {
     if (!d->m.w2t) return;
-    ptc::persist_transpose_w2(d->m, (float *)d->m.w2t, d->stream);
+    ptc::transpose_w2(d->m, (float *)d->m.w2t, d->stream);
 }
 
-extern "C" int ptc_decoder_is_persistent(ptc_decoder *d) { return d->persist ? 1 : 0; }
-
-extern "C" void ptc_decoder_trace(ptc_decoder *d, int max_barriers) {
-    if (!d->persist) return;
-    if (max_barriers <= 0) {
-        d->pa.trace = nullptr;
-        d->pa.trace_cap = 0;
-        return;
+extern "C" size_t ptc_decoder_trace(ptc_decoder *d, int on) {
+    if (on) {   // earliest stamps start high, latest stamps low
+        unsigned long long *h = (unsigned long long *)malloc(d->trace_n * sizeof(unsigned long long));
+        for (size_t i = 0; i < d->trace_n; i++) h[i] = (i & 1) ? 0ull : ~0ull;
+        PTC_CHECK(cudaMemcpyAsync(d->m.trace, h, d->trace_n * sizeof(unsigned long long), cudaMemcpyHostToDevice,
+                                  d->stream));
+        PTC_CHECK(cudaStreamSynchronize(d->stream));
+        free(h);
     }
-    d->pa.trace = (unsigned long long *)ptc_alloc(d->ctx, (size_t)2 * max_barriers * 8);
-    d->pa.trace_cap = 2 * max_barriers;
-    PTC_CHECK(cudaMemsetAsync(d->pa.trace, 0, (size_t)2 * max_barriers * 8, d->stream));
+    d->trace_on = on ? 1 : 0;
+    PTC_CHECK(cudaMemcpyAsync(&d->m.step->trace_on, &d->trace_on, sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    return d->trace_n;
 }
 
-extern "C" int ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, int n) {
-    if (!d->persist || !d->pa.trace) return 0;
-    if (n > d->pa.trace_cap) n = d->pa.trace_cap;
-    PTC_CHECK(cudaMemcpyAsync(out, d->pa.trace, (size_t)n * 8, cudaMemcpyDeviceToHost, d->stream));
+extern "C" size_t ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, size_t n) {
+    if (n > d->trace_n) n = d->trace_n;
+    PTC_CHECK(cudaMemcpyAsync(out, d->m.trace, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     return n;
-}
-
-static void persist_run(ptc_decoder *d, int n_steps) {
-    d->pa.n_steps = n_steps;
-    ptc::persist_launch(d->pa, d->n_sm, d->stream);
-    // every CTA has read the last argmax key; clear it for the next head
-    PTC_CHECK(cudaMemsetAsync(&d->m.step->amax, 0, sizeof(unsigned long long), d->stream));
 }
 
 extern "C" void ptc_decoder_destroy(ptc_decoder *d) {
@@ -308,16 +290,8 @@ extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logit
     set_mode(d, 0);
     d->io->pos = pos;
     d->io->tok = token;
-    if (d->persist) {
-        PTC_CHECK(cudaMemcpyAsync(d->m.step, d->io, 2 * sizeof(int), cudaMemcpyHostToDevice, d->stream));
-        persist_run(d, 1);
-        if (d->has_head)
-            PTC_CHECK(cudaMemcpyAsync(&d->io->next, &d->m.step->next, sizeof(int), cudaMemcpyDeviceToHost,
-                                      d->stream));
-    } else {
-        d->io->next = -1;   // overwritten by the classifier
-        PTC_CHECK(cudaGraphLaunch(d->g_host, d->stream));
-    }
+    d->io->next = -1;   // overwritten by the classifier
+    PTC_CHECK(cudaGraphLaunch(d->g_host, d->stream));
     if (logits_host && d->has_head) {
         PTC_CHECK(cudaMemcpyAsync(d->stage, d->m.logits, (size_t)d->m.V * 4, cudaMemcpyDeviceToHost,
                                   d->stream));
@@ -361,20 +335,13 @@ extern "C" void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, in
     st.n_prompt = n_prompt;
     st.mode = 1;
     st.tokens = d->d_tokens;
+    st.trace_on = d->trace_on;
     PTC_CHECK(cudaMemcpyAsync(d->m.step, &st, sizeof(st), cudaMemcpyHostToDevice, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     d->mode = 1;
-    d->loop_pos = 0;
 }
 
 extern "C" void ptc_decoder_enqueue_steps(ptc_decoder *d, int n) {
-    if (d->persist && d->has_embed && d->has_head) {
-        // one launch decodes up to the end of the cache
-        if (n > d->m.seq - d->loop_pos) n = d->m.seq - d->loop_pos;
-        if (n > 0) persist_run(d, n);
-        d->loop_pos += n > 0 ? n : 0;
-        return;
-    }
     int i = 0;
     if (d->g_devk)
         for (; i + DEV_TOKENS <= n; i += DEV_TOKENS) PTC_CHECK(cudaGraphLaunch(d->g_devk, d->stream));
@@ -461,7 +428,6 @@ extern "C" void ptc_decoder_enqueue_kernel(ptc_decoder *d, int kind, int l, int 
 }
 
 extern "C" int ptc_decoder_launches_per_step(ptc_decoder *d) {
-    if (d->persist) return 1;
     const ptc::DecodeModel &m = d->m;
     const int per_layer = m.fused_attn ? 2 : m.fused_ffn ? 4 : 5;
     return per_layer * m.L + (d->has_head ? 1 : 0) + (d->has_embed && m.L == 0 ? 1 : 0);

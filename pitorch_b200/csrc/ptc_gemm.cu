@@ -22,9 +22,15 @@
 #include <cooperative_groups.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "../../include/ptc.h"
 
 namespace ptc {
+
+static std::atomic<long long> g_gemm_counts[GC_N];
+
+void gemm_count(int which) { g_gemm_counts[which].fetch_add(1, std::memory_order_relaxed); }
 
 namespace cg = cooperative_groups;
 
@@ -393,6 +399,7 @@ static void launch_tile(const GemmArgs &g, cudaStream_t s) {
     else if (g.b_kcontig) k_gemm<BM, BN, BK, TM, TN, false, true><<<grid, block, 0, s>>>(g);
     else k_gemm<BM, BN, BK, TM, TN, false, false><<<grid, block, 0, s>>>(g);
     PTC_CHECK(cudaGetLastError());
+    gemm_count(GC_SIMT);
 }
 
 template <int BM, int BN, int BK, int TM, int TN, bool A_KC, bool B_KC>
@@ -411,6 +418,8 @@ static void launch_v(const GemmArgs &g, int kper, cudaStream_t s) {
         cfg.numAttrs = 1;
     }
     PTC_CHECK(cudaLaunchKernelEx(&cfg, k_gemm_v<BM, BN, BK, TM, TN, A_KC, B_KC>, g, kper));
+    gemm_count(GC_SIMT);
+    if (g.cluster_red) gemm_count(GC_CLUSTER_REDUCED);
 }
 
 template <int BM, int BN, int BK, int TM, int TN>
@@ -428,6 +437,7 @@ void launch_splitk_reduce(const GemmArgs &g, int n_sm, cudaStream_t s) {
     if (blocks > 8 * n_sm) blocks = 8 * n_sm;
     k_splitk_reduce<<<blocks, 256, 0, s>>>(g);
     PTC_CHECK(cudaGetLastError());
+    gemm_count(GC_SPLITK_REDUCE);
 }
 
 // The vectorised kernel reads float4s along each operand's contiguous
@@ -453,9 +463,12 @@ void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
         // The classifier's products (about 2.4 GFLOP each at 15M) on the
         // tensor cores; the layer products are too small to gain.
         if (gemm_tc_enabled() && !g.no_alloc && (double)g.M * g.N * g.K >= 1e9 && aligned16(g.C) &&
-            (g.epi != EPI_RESID || aligned16(g.R)) && g.ldc % 4 == 0 && (g.epi != EPI_RESID || g.ldr % 4 == 0) &&
-            gemm_tc(g, n_sm, s))
-            return;
+            (g.epi != EPI_RESID || aligned16(g.R)) && g.ldc % 4 == 0 && (g.epi != EPI_RESID || g.ldr % 4 == 0)) {
+            if (gemm_tc(g, n_sm, s)) return;
+            if (gemm_tc_required() && g.epi != EPI_ROPE)
+                PTC_FATAL("PTC_GEMM_TC=1: the tensor-core GEMM refused %d x %d x %d (a_kcontig %d, b_kcontig %d)",
+                          g.M, g.N, g.K, (int)g.a_kcontig, (int)g.b_kcontig);
+        }
         // Tile: 128x128 when the product alone fills the GPU, else 64x64;
         // then split K (chunks of at least 64, a multiple of the k-tile)
         // until about one wave of CTAs covers the SMs.
@@ -492,12 +505,7 @@ void gemm(GemmArgs g, int n_sm, cudaStream_t s) {
     g.splits = splits;
     if (big) launch_tile<128, 128, 8, 8, 8>(g, s);
     else launch_tile<64, 64, 16, 4, 4>(g, s);
-    if (splits > 1) {
-        int blocks = (int)(((size_t)g.M * g.N + 255) / 256);
-        if (blocks > 8 * n_sm) blocks = 8 * n_sm;
-        k_splitk_reduce<<<blocks, 256, 0, s>>>(g);
-        PTC_CHECK(cudaGetLastError());
-    }
+    if (splits > 1) launch_splitk_reduce(g, n_sm, s);
 }
 
 }  // namespace ptc
@@ -518,4 +526,8 @@ extern "C" void ptc_sgemm(int M, int N, int K, const float *A, int lda, int a_kc
     g.partial = workspace;
     g.partial_cap = workspace ? workspace_floats : 0;
     ptc::gemm(g, n_sm, (cudaStream_t)stream);
+}
+
+extern "C" void ptc_gemm_counters(long long *out) {
+    for (int i = 0; i < ptc::GC_N; i++) out[i] = ptc::g_gemm_counts[i].load(std::memory_order_relaxed);
 }

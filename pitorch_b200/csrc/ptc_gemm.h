@@ -39,12 +39,21 @@ struct GemmArgs {
 
 void gemm(GemmArgs g, int n_sm, cudaStream_t s);
 
+// Per-process launch counters of the GEMM paths (ptc_gemm_counters):
+// tensor-core kernels, SIMT tile kernels, split-K reduction kernels, and
+// SIMT launches whose splits were summed inside a cluster.
+enum GemmCounter { GC_TENSOR_CORE = 0, GC_SIMT = 1, GC_SPLITK_REDUCE = 2, GC_CLUSTER_REDUCED = 3, GC_N = 4 };
+void gemm_count(int which);
+
 // Fixed-order sum of g.splits partials from g.partial into C with g's epilogue.
 void launch_splitk_reduce(const GemmArgs &g, int n_sm, cudaStream_t s);
 
 // Tensor-core fp32 GEMM (ptc_gemm_tc.cu), used by gemm() for the large
 // products unless PTC_GEMM_TC=0; returns false when it does not take g.
 bool gemm_tc_enabled();
+// PTC_GEMM_TC=1: every product that qualifies must run on the tensor cores
+// (a CUTLASS refusal is then fatal instead of falling back).
+bool gemm_tc_required();
 bool gemm_tc(const GemmArgs &g, int n_sm, cudaStream_t s);
 
 }  // namespace ptc

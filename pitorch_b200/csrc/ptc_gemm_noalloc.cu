@@ -25,15 +25,21 @@ static __device__ __align__(256) float g_sgemm_noalloc_scratch[PTC_SGEMM_NOALLOC
 
 namespace {
 constexpr int kMaxDevices = 64;
-float *g_scratch_dev[kMaxDevices];   // device address of the array, per device
+// Per device: the array's device address and the SM count. A set-up stores
+// the SM count first and then publishes the pointer with a release store;
+// readers load the pointer with acquire, so a non-null pointer comes with a
+// valid SM count.
+float *g_scratch_dev[kMaxDevices];
 int g_sm_count[kMaxDevices];
 pthread_mutex_t g_setup_mu = PTHREAD_MUTEX_INITIALIZER;
+
+float *scratch_of(int dev) { return __atomic_load_n(&g_scratch_dev[dev], __ATOMIC_ACQUIRE); }
 
 // One-time set-up for the current device: resolve the array's device address.
 bool setup_device(int dev) {
     bool ok = true;
     pthread_mutex_lock(&g_setup_mu);
-    if (!g_scratch_dev[dev]) {
+    if (!scratch_of(dev)) {
         float *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress((void **)&p, g_sgemm_noalloc_scratch);
         int n_sm = 0;
@@ -44,7 +50,7 @@ bool setup_device(int dev) {
             ok = false;
         } else {
             g_sm_count[dev] = n_sm;
-            g_scratch_dev[dev] = p;
+            __atomic_store_n(&g_scratch_dev[dev], p, __ATOMIC_RELEASE);
         }
     }
     pthread_mutex_unlock(&g_setup_mu);
@@ -71,7 +77,11 @@ extern "C" int ptc_sgemm_noalloc(int M, int N, int K, const float *A, int lda, i
         fprintf(stderr, "pitorch_b200: ptc_sgemm_noalloc: no usable current device\n");
         return -1;
     }
-    if (!g_scratch_dev[dev] && !setup_device(dev)) return -1;
+    float *scratch = scratch_of(dev);
+    if (!scratch) {
+        if (!setup_device(dev)) return -1;
+        scratch = scratch_of(dev);
+    }
 
     ptc::GemmArgs g;
     memset(&g, 0, sizeof(g));
@@ -82,7 +92,7 @@ extern "C" int ptc_sgemm_noalloc(int M, int N, int K, const float *A, int lda, i
     g.epi = accumulate ? ptc::EPI_ACCUM : ptc::EPI_STORE;
     // Every split writes all of its M*N partials before the reduction reads
     // them, so whatever an earlier call left in the array is never read.
-    g.partial = g_scratch_dev[dev];
+    g.partial = scratch;
     g.partial_cap = PTC_SGEMM_NOALLOC_MAX_MN;
     g.no_alloc = 1;
     ptc::gemm(g, g_sm_count[dev], (cudaStream_t)stream);

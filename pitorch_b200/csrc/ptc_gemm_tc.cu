@@ -112,6 +112,7 @@ bool run_tc(int M, int N, int K, int L, const float *A, int64_t lda, int64_t bsa
     if (gemm.initialize(args, ws, s) != cutlass::Status::kSuccess) return false;
     if (gemm.run(s) != cutlass::Status::kSuccess) PTC_FATAL("tensor-core GEMM launch failed (%d x %d x %d)", M, N, K);
     PTC_CHECK(cudaGetLastError());
+    gemm_count(GC_TENSOR_CORE);
     return true;
 }
 
@@ -156,6 +157,14 @@ bool gemm_tc_enabled() {
         return !(e && e[0] == '0');
     }();
     return on;
+}
+
+bool gemm_tc_required() {
+    static const bool req = [] {
+        const char *e = getenv("PTC_GEMM_TC");
+        return e && e[0] == '1';
+    }();
+    return req;
 }
 
 bool gemm_tc(const GemmArgs &g, int n_sm, cudaStream_t s) {

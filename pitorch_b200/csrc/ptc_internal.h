@@ -30,6 +30,7 @@ int decode_ffn_rows(int dim, int hidden, int n_sm);
 void launch_block(const DecodeModel &m, int kind, int l, int n_sm, cudaStream_t s);
 int decode_attn_stage(int dim, int nh, int nkv, int seq);
 void build_rope_table(float2 *t, int seq, int hd, cudaStream_t s);
+void transpose_w2(const DecodeModel &m, float *w2t, cudaStream_t s);
 // host_next: pinned host word that also receives the argmax (or null).
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s, int *host_next = nullptr);
 void launch_embed(const DecodeModel &m, cudaStream_t s);

@@ -26,11 +26,6 @@ struct MailboxHeader {
 
 static size_t mailbox_bytes(int dim) { return sizeof(MailboxHeader) + (size_t)dim * 4; }
 
-__device__ __forceinline__ unsigned long long globaltimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -65,7 +60,7 @@ __global__ void k_hop_recv(const unsigned char *box, float *__restrict__ x, int 
     __shared__ int s_ok;
     if (threadIdx.x == 0) {
         const unsigned want = *recvd + 1;
-        const unsigned long long t0 = globaltimer();
+        const unsigned long long t0 = globaltimer_ns();
         // after one expired wait the link is broken: the hops queued behind
         // it return at once instead of each waiting out its own deadline
         int ok = 0;
@@ -74,7 +69,7 @@ __global__ void k_hop_recv(const unsigned char *box, float *__restrict__ x, int 
                 ok = 1;
                 break;
             }
-            if (globaltimer() - t0 > timeout_ns) break;
+            if (globaltimer_ns() - t0 > timeout_ns) break;
             __nanosleep(128);
         }
         if (ok) *recvd = want;

@@ -164,9 +164,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", default=os.path.join(REPO, "..", "reference"))
     ap.add_argument("--skip-slow", action="store_true")
+    ap.add_argument("--only-110M-long", action="store_true",
+                    help="regenerate decode_stories110M_long.npz alone (about 100 s)")
     args = ap.parse_args()
     if not oracle.ref_available():
         sys.exit("oracle/_ref/libptref.so missing: run make -C oracle first")
+    if args.only_110M_long:
+        make_decode("stories110M", 1024, [255, 511, 767, 1023], suffix="_long")
+        return
     make_ops(args.ref_root)
     make_backward(args.ref_root)
     make_matvec_kat()
@@ -178,6 +183,8 @@ def main():
         make_decode("stories110M", 64, [63])
         # the whole 1024-position cache: attention over more than 512 positions
         make_decode("stories42M", 1024, [511, 700, 1023], suffix="_long")
+        # the benchmark's configuration: 110M over the whole 1024-position cache
+        make_decode("stories110M", 1024, [255, 511, 767, 1023], suffix="_long")
         make_train("stories15M", 256, 20)
 
 

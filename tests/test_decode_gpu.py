@@ -7,6 +7,9 @@ restatement pinned to it. Tolerance: max|dlogit| / max|logit| <= 1e-4 per
 position; greedy token streams must be identical.
 """
 import ctypes as C
+import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -17,6 +20,7 @@ from pitorch_b200 import api, synth
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-4
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def check_stream(ctx, name, n_pos=None, fixture=None):
@@ -140,16 +144,108 @@ def test_matvec_callback_is_gpu(ptlib):
     ctx.close()
 
 
-def test_persistent_kernel_path_matches_reference(ptlib, monkeypatch):
-    """The opt-in single-kernel decode (PTC_DECODE_PERSIST=1) gives the same
-    stream as the reference, through pt_forward_step and the device loop."""
-    monkeypatch.setenv("PTC_DECODE_PERSIST", "1")
+def test_shard_chain_on_one_gpu_matches_reference(ptlib):
+    """The shard path on one GPU: the world = 4 shards of stories15M (ranks
+    0-2 hold two layers each, rank 3 the embedding and the classifier, the
+    layout of tools/shard_weights.py:49-66) loaded with pt_pi_init_shard into
+    four contexts on device 0, and chained per position as the reference's
+    ring passes x around (pitorch/dist/pt_dist_pipeline.c:287-357):
+    pt_forward_embed on the head shard, pt_forward_layers_range on each
+    layer shard, pt_forward_head on the head shard. The greedy stream equals
+    the reference's full-model decode over all 256 positions, and the
+    fixture's logits rows agree within the decode tolerance."""
+    g = golden("decode_stories15M.npz")
+    full = synth.make_blob("stories15M")
+    world = 4
+    ctxs = [api.Context(api.make_shard(full, r, world), device=0, shard=True) for r in range(world)]
+    try:
+        head, layers = ctxs[-1], ctxs[:-1]
+        assert head.shard.has_embed and head.shard.has_head
+        assert [c.shard.n_local for c in layers] == [2, 2, 2]
+        assert not any(c.shard.has_embed or c.shard.has_head for c in layers)
+        dim, V = head.cfg.dim, head.cfg.vocab_size
+        n = int(g["n_pos"])
+        prompt = g["prompt"]
+        rows = {int(r): row for r, row in zip(g["rows"], g["logits_rows"])}
+        tok, toks = int(prompt[0]), []
+        for p in range(n):
+            ptlib.pt_forward_embed(C.byref(head.ctx.w), head.ctx.state.x, dim, tok)
+            x = head.ctx.state.x
+            for c in layers:
+                C.memmove(c.ctx.state.x, x, dim * 4)
+                ptlib.pt_forward_layers_range(C.byref(c.ctx.cfg), C.byref(c.ctx.w), C.byref(c.ctx.state), p, 0,
+                                              c.shard.n_local, None)
+                x = c.ctx.state.x
+            C.memmove(head.ctx.state.x, x, dim * 4)
+            ptlib.pt_forward_head(C.byref(head.ctx.cfg), C.byref(head.ctx.w), C.byref(head.ctx.state), None)
+            nxt = int(ptlib.pt_argmax(head.ctx.state.logits, V))
+            if p in rows:
+                logits = np.ctypeslib.as_array(head.ctx.state.logits, shape=(V,))
+                assert rel_err(logits, rows[p]) <= TOL, p
+            nxt = int(prompt[p + 1]) if p + 1 < len(prompt) else nxt
+            toks.append(nxt)
+            tok = nxt
+        assert np.array_equal(np.array(toks), g["tokens"][:n])
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_phase_timeline_records_every_kernel(ptlib):
+    """ptc_decoder_trace: with tracing on, every kernel of a traced position
+    stamps its phase points in order, and the decode still matches the
+    reference (stamping changes no result)."""
     g = golden("decode_stories15M.npz")
     ctx = api.Context(synth.make_blob("stories15M"))
-    assert ptlib.ptc_decoder_is_persistent(ctx.ptc_decoder()) == 1
-    check_stream(ctx, "stories15M")
-    assert np.array_equal(ctx.generate_greedy(g["prompt"], 256), g["tokens"])
+    dec = ctx.ptc_decoder()
+    n = ptlib.ptc_decoder_trace(dec, 1)
+    toks = ctx.generate_greedy(g["prompt"], 16)
+    assert np.array_equal(toks, g["tokens"][:16])
+    buf = (C.c_ulonglong * n)()
+    assert ptlib.ptc_decoder_read_trace(dec, buf, n) == n
+    ptlib.ptc_decoder_trace(dec, 0)
+    L = ctx.cfg.n_layers
+    t = np.frombuffer(buf, dtype=np.uint64).reshape(16, 2 * L + 1, 8, 2)
+    NONE = np.uint64(0xFFFFFFFFFFFFFFFF)
+    events = {"attn": [0, 1, 2, 3, 4, 5, 6, 7], "ffn": [0, 1, 2, 3, 4, 7], "cls": [0, 1, 2, 6, 7]}
+    for p in range(16):
+        for k in range(2 * L + 1):
+            kind = "cls" if k == 2 * L else ("attn" if k % 2 == 0 else "ffn")
+            ev = events[kind]
+            lo = t[p, k, ev, 0]
+            hi = t[p, k, ev, 1]
+            assert np.all(lo != NONE) and np.all(hi >= lo), (p, k)
+            # the latest CTA passes the events in order
+            assert np.all(np.diff(hi.astype(np.int64)) >= 0), (p, k, hi)
+        # kernels of one position run in order: each starts after the
+        # previous one's first CTA started
+        starts = t[p, :, 0, 0].astype(np.int64)
+        assert np.all(np.diff(starts) > 0), (p, starts)
     ctx.close()
+
+
+def test_position_past_the_cache_is_an_error(ptlib):
+    """A device-loop decode driven past seq_len is reported, not computed:
+    the kernels record ERR_POS_RANGE and reading the tokens fails loudly
+    (checked in a child process, which aborts)."""
+    code = (
+        "import sys; sys.path.insert(0, 'tests')\n"
+        "from pitorch_b200 import api, synth\n"
+        "import pitorch_b200, numpy as np, ctypes as C\n"
+        "L = pitorch_b200.lib()\n"
+        "ctx = api.Context(synth.make_blob('tiny'))\n"
+        "dec = ctx.ptc_decoder()\n"
+        "seq = ctx.cfg.seq_len\n"
+        "prompt = (C.c_int * 1)(5)\n"
+        "L.ptc_decoder_reset(dec)\n"
+        "L.ptc_decoder_generate_begin(dec, prompt, 1)\n"
+        "L.ptc_decoder_enqueue_steps(dec, seq + 2)\n"
+        "out = (C.c_int * seq)()\n"
+        "L.ptc_decoder_read_tokens(dec, out, seq)\n"
+        "print('NOT REPORTED')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0 and "NOT REPORTED" not in r.stdout, (r.returncode, r.stdout[-500:])
+    assert "past seq_len" in r.stderr, r.stderr[-1000:]
 
 
 @pytest.mark.parametrize("mode", ["0", "ffn"])
@@ -167,26 +263,25 @@ def test_unfused_layer_paths_match_reference(ptlib, monkeypatch, mode):
 NEAR_TIE = 1e-5   # top-2 logit gap / max|logit| below which fp32 order may flip the argmax
 
 
-@pytest.mark.parametrize("mode", ["default", "ffn"])
-def test_42M_full_cache_decode(ptlib, monkeypatch, mode):
-    """All 1024 positions of the 42M decode (attention over more than 512
-    positions: a second round of K/V per cluster CTA in the fused kernel).
+def check_full_cache(name, fixture):
+    """All seq_len positions of a decode against the reference's fixture.
 
-    The seeded model's logits are small and flat, so the reference's own
-    stream has near-ties (top-2 gap down to 0 at position 571) that any other
-    fp32 summation order may resolve differently. Hence:
+    The seeded models' logits are small and flat, so the reference's own
+    stream has near-ties (at 42M the top-2 gap is 0 at position 571) that any
+    other fp32 summation order may resolve differently. Hence:
       teacher-forced  -- the reference's tokens as inputs at every position:
-        logits at 511, 700, 1023 within TOL; our argmax equals the reference's
-        token wherever its top-2 gap is at least NEAR_TIE of max|logit|;
+        the fixture's logits rows within TOL, max|logit| at every position;
+        our argmax equals the reference's token wherever its top-2 gap is at
+        least NEAR_TIE of max|logit|;
       free-running    -- the device loop equals the reference's stream up to
-        its first near-tie."""
-    if mode != "default":
-        monkeypatch.setenv("PTC_DECODE_FUSED", mode)
-    g = golden("decode_stories42M_long.npz")
+        its first near-tie.
+    Returns (positions compared free-running, clear positions)."""
+    g = golden(fixture)
     ref_toks = g["tokens"]
+    n = len(ref_toks)
     forced = np.concatenate([g["prompt"][:1], ref_toks[:-1]]).astype(np.int32)
-    ctx = api.Context(synth.make_blob("stories42M"))
-    _, logits = ctx.decode_greedy(forced, 1024, want_logits=True)
+    ctx = api.Context(synth.make_blob(name))
+    _, logits = ctx.decode_greedy(forced, n, want_logits=True)
     for r, row in zip(g["rows"], g["logits_rows"]):
         assert rel_err(logits[r], row) <= TOL, int(r)
     am = np.abs(logits).max(axis=1)
@@ -196,9 +291,30 @@ def test_42M_full_cache_decode(ptlib, monkeypatch, mode):
     mine = logits.argmax(axis=1)
     assert clear.sum() > 0.95 * len(clear)
     assert np.array_equal(mine[clear], ref_toks[clear]), np.nonzero((mine != ref_toks) & clear)[0][:5]
-    free = ctx.generate_greedy(g["prompt"], 1024)
+    free = ctx.generate_greedy(g["prompt"], n)
     tie = ~clear
     tie[: len(g["prompt"]) - 1] = False
-    first_tie = int(np.argmax(tie)) if tie.any() else 1024
+    first_tie = int(np.argmax(tie)) if tie.any() else n
     assert np.array_equal(free[:first_tie + 1], ref_toks[:first_tie + 1]), first_tie
     ctx.close()
+    return first_tie + 1, int(clear.sum())
+
+
+@pytest.mark.parametrize("mode", ["default", "ffn"])
+def test_42M_full_cache_decode(ptlib, monkeypatch, mode):
+    """All 1024 positions of the 42M decode (attention over more than 512
+    positions: a second round of K/V per cluster CTA in the fused kernel)."""
+    if mode != "default":
+        monkeypatch.setenv("PTC_DECODE_FUSED", mode)
+    check_full_cache("stories42M", "decode_stories42M_long.npz")
+
+
+@pytest.mark.parametrize("mode", ["default", "0"])
+def test_110M_full_cache_decode(ptlib, monkeypatch, mode):
+    """The benchmark's own configuration: all 1024 positions of the 110M
+    decode, for the default two-kernel layer and the deterministic
+    five-kernel layer (PTC_DECODE_FUSED=0), against the reference host C's
+    1024-position stream and its logits rows at 255, 511, 767 and 1023."""
+    if mode != "default":
+        monkeypatch.setenv("PTC_DECODE_FUSED", mode)
+    check_full_cache("stories110M", "decode_stories110M_long.npz")
