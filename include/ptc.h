@@ -181,7 +181,9 @@ void ptc_decoder_weights_updated(ptc_decoder *d);
  * layer l, 2l+1: FFN block of layer l, 2L: classifier) and event e < 8,
  * entries 2i and 2i+1 with i = ((p % 16) * (2L + 1) + k) * 8 + e hold the
  * earliest and the latest stamp over the kernel's CTAs (an event a kernel
- * does not have keeps ~0 / 0). Returns the number of entries;
+ * does not have keeps ~0 / 0). Tracing is a parameter of the kernels, so
+ * turning it on or off synchronises the decoder's stream and re-captures
+ * its graphs (call it between decodes). Returns the number of entries;
  * ptc_decoder_read_trace copies up to n of them and returns how many. */
 size_t ptc_decoder_trace(ptc_decoder *d, int on);
 size_t ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, size_t n);
@@ -254,6 +256,9 @@ float ptc_trainer_step(ptc_trainer *t, const int *tokens, int T, float lr);
 
 /* Staged pieces (enqueue only, except fwd_head which returns the loss). */
 void ptc_trainer_set_tokens(ptc_trainer *t, const int *tokens, int T);
+/* The sequence length of the next staged calls without new tokens (a layer
+ * range that receives its input rows from another stage). */
+void ptc_trainer_set_T(ptc_trainer *t, int T);
 void ptc_trainer_zero_grads(ptc_trainer *t);
 void ptc_trainer_fwd_embed(ptc_trainer *t);
 void ptc_trainer_fwd_layers(ptc_trainer *t, int l_start, int l_end);

@@ -15,7 +15,7 @@ struct StepState {
     int next;                 // argmax of this step's logits
     int n_prompt;             // device-loop mode: prompt length
     int mode;                 // 0: host drives pos/tok; 1: device loop
-    int trace_on;             // 1: kernels stamp the phase timeline
+    int pad0;
     unsigned done;            // classifier CTAs finished (reset by the last)
     unsigned pad1;
     unsigned long long amax;  // packed (value, index) running argmax
@@ -63,15 +63,13 @@ struct DecodeModel {
     // while the previous token's classifier still runs.
     int tok_off;
     int adv;
-    // Phase timeline (ptc_decoder_trace), stamped only while step->trace_on:
+    // Phase timeline (ptc_decoder_trace), stamped only when non-null (the
+    // decoder re-captures its graphs to turn it on or off):
     // for traced position p, kernel k of the position (2l: attention block of
     // layer l, 2l+1: its FFN block, 2L: the classifier) and event e, the
     // earliest and the latest %globaltimer over the kernel's CTAs at
     // trace[2 * (((p % TRACE_POS) * (2L + 1) + k) * TRACE_EV + e)] (+1).
     unsigned long long *trace;
-    // L2 eviction priorities (L2Pol) of the kernels' own loads: layer weights,
-    // classifier rows, KV cache rows.
-    int pol_w, pol_cls, pol_kv;
 };
 
 constexpr int TRACE_POS = 16;

@@ -127,6 +127,28 @@ __device__ __forceinline__ void store_vec(float *dst, const float4 (&x)[NV], int
     }
 }
 
+// The input vector of a kernel, read ONCE per CTA: its threads load
+// consecutive float4s into shared memory, and after a block barrier every
+// warp takes its lanes' float4s from there. Reading it per warp made all
+// warps of all CTAs fetch the same few L2 lines (about a thousand requests
+// per line per kernel), which queued at the L2 slices holding them.
+__device__ __forceinline__ void stage_vec(float4 *s_x4, const float *src, int c4) {
+    const float4 *src4 = reinterpret_cast<const float4 *>(src);
+    for (int i = threadIdx.x; i < c4; i += blockDim.x) s_x4[i] = __ldcg(src4 + i);
+}
+
+template <int NV>
+__device__ __forceinline__ void vec_from_smem(float4 (&x)[NV], const float4 *s_x4, int c4, int lane) {
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const int c = lane + 32 * v;
+        x[v] = (c < c4) ? s_x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// Bytes of the shared-memory copy of an n-float vector (128-byte multiple).
+__host__ __device__ constexpr int vec_smem_bytes(int n) { return (n * 4 + 127) / 128 * 128; }
+
 // Phase timeline stamp by thread 0 of a CTA, only while tracing: the slot of
 // (position, kernel k, event e) keeps the earliest and the latest time.
 __device__ __forceinline__ void trace_ev(const DecodeModel &m, bool on, int pos, int k, int e) {
@@ -137,9 +159,15 @@ __device__ __forceinline__ void trace_ev(const DecodeModel &m, bool on, int pos,
     atomicMax(slot + 1, t);
 }
 
-__device__ __forceinline__ bool trace_on(const DecodeModel &m) {
-    return m.trace != nullptr && __ldcg(&m.step->trace_on) != 0;
-}
+__device__ __forceinline__ bool trace_on(const DecodeModel &m) { return m.trace != nullptr; }
+
+// L2 eviction priority of the decode kernels' own loads: the layer weights
+// and the KV rows are read once per token and marked evict_first, so that
+// they do not push the small activation vectors and the next kernels' data
+// out of L2 (measured 5052 -> 5139 tok/s at 110M against no hint; an
+// evict_last mark on the classifier rows changed nothing).
+constexpr int kPolWeights = POL_FIRST;
+constexpr int kPolKV = POL_FIRST;
 
 // A position outside the KV cache: the kernels compute nothing that could be
 // mistaken for a result of it and record the error for the host.
@@ -390,7 +418,7 @@ struct MvArgs {
 
 template <int MODE>
 __device__ __forceinline__ void mv_issue(const DecodeModel &m, const MvArgs &a, float *stage, uint64_t *bar,
-                                         int c0, int c1, uint64_t pol) {
+                                         int c0, int c1) {
     const size_t rb = (size_t)a.cols * 4;  // bytes per row
     const int n = c1 - c0;
     if (MODE == MV_QKV) {
@@ -414,8 +442,7 @@ __device__ __forceinline__ void mv_issue(const DecodeModel &m, const MvArgs &a, 
         bulk_g2s(stage + (size_t)a.per_stage * a.cols, m.w3 + off, (unsigned)(n * rb), bar);
     } else {
         mbar_expect_tx(bar, (unsigned)(n * rb));
-        bulk_g2s_pol(stage, a.W + (size_t)c0 * a.cols, (unsigned)(n * rb), bar, MODE == MV_CLS ? m.pol_cls : POL_NONE,
-                     pol);
+        bulk_g2s(stage, a.W + (size_t)c0 * a.cols, (unsigned)(n * rb), bar);
     }
 }
 
@@ -436,7 +463,8 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     pdl_trigger();
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
-    float *stages = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES);
+    float4 *s_x4 = reinterpret_cast<float4 *>(smem_raw + MV_BAR_BYTES);   // the input vector
+    float *stages = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES + vec_smem_bytes(a.cols));
     __shared__ unsigned long long s_best[MV_THREADS / 32];
     __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -454,11 +482,9 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         mbar_init_fence();
     }
     __syncthreads();
-    const uint64_t cls_pol = MODE == MV_CLS ? make_l2_policy(m.pol_cls) : 0ull;
     if (tid == 0)
         for (int k = 0; k < n_chunks && k < NST; k++)
-            mv_issue<MODE>(m, a, stages + k * stage_floats, &bars[k], it0 + k * ps, min(it1, it0 + (k + 1) * ps),
-                           cls_pol);
+            mv_issue<MODE>(m, a, stages + k * stage_floats, &bars[k], it0 + k * ps, min(it1, it0 + (k + 1) * ps));
 
     // Everything that does not come from the kernel this one depends on is
     // loaded before the wait: rmsnorm gains (weights), the position and --
@@ -466,13 +492,13 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     float4 xr[NV], gr[NV];
     int pos = 0;
     const bool tr = MODE == MV_CLS && trace_on(m);
-    const int tpos = MODE == MV_CLS ? __ldcg(&m.step->pos) + m.tok_off : 0;
+    const int tpos = tr ? __ldcg(&m.step->pos) + m.tok_off : 0;
     trace_ev(m, tr, tpos, 2 * m.L, 0);
+    const bool early = MODE == MV_QKV && a.from_embedding && m.tok_off == 0;
     if (MODE == MV_QKV) {
         pos = __ldcg(&m.step->pos) + m.tok_off;
         load_gain<NV>(gr, m.rms_att + (size_t)a.l * m.dim, c4, lane);
-        if (a.from_embedding && m.tok_off == 0)
-            load_act<NV>(xr, m.emb + (size_t)__ldcg(&m.step->tok) * m.dim, c4, lane);
+        if (early) stage_vec(s_x4, m.emb + (size_t)__ldcg(&m.step->tok) * m.dim, c4);
     } else if (MODE == MV_FFN13) {
         load_gain<NV>(gr, m.rms_ffn + (size_t)a.l * m.dim, c4, lane);
     } else if (MODE == MV_CLS) {
@@ -490,24 +516,23 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             xres[q] = (lane == 0 && n_chunks <= NST && i < it1) ? __ldcg(a.res_in + i) : 0.f;
         }
     }
+    if (!early) {
+        const float *src = a.in;
+        if (MODE == MV_QKV && a.from_embedding) src = m.emb + (size_t)__ldcg(&m.step->tok) * m.dim;
+        if (MODE == MV_FFN13 || MODE == MV_CLS) src = m.x;
+        stage_vec(s_x4, src, c4);
+    }
+    __syncthreads();
+    vec_from_smem<NV>(xr, s_x4, c4, lane);
     if (MODE == MV_QKV) {
-        if (a.from_embedding) {
-            if (m.tok_off != 0) load_act<NV>(xr, m.emb + (size_t)__ldcg(&m.step->tok) * m.dim, c4, lane);
-            if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.x, xr, c4, lane);
-        } else {
-            load_act<NV>(xr, a.in, c4, lane);
-        }
+        if (a.from_embedding && blockIdx.x == 0 && warp == 0) store_vec<NV>(m.x, xr, c4, lane);
         rmsnorm_pre<NV>(xr, gr, m.dim);
     } else if (MODE == MV_FFN13) {
-        load_act<NV>(xr, m.x, c4, lane);
         rmsnorm_pre<NV>(xr, gr, m.dim);
     } else if (MODE == MV_CLS) {
-        load_act<NV>(xr, m.x, c4, lane);
         rmsnorm_pre<NV>(xr, gr, m.dim);
         if (blockIdx.x == 0 && warp == 0) store_vec<NV>(m.xn, xr, c4, lane);
         trace_ev(m, tr, tpos, 2 * m.L, 2);
-    } else {
-        load_act<NV>(xr, a.in, c4, lane);
     }
     const bool pos_ok = (MODE != MV_QKV) || (pos >= 0 && pos < m.seq);
     if (!pos_ok) flag_pos_range(m);
@@ -602,8 +627,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             if (tid == 0 && k + NST < n_chunks) {
                 fence_proxy_async_smem();
                 const int kk = k + NST;
-                mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps),
-                               cls_pol);
+                mv_issue<MODE>(m, a, stages + s * stage_floats, &bars[s], it0 + kk * ps, min(it1, it0 + (kk + 1) * ps));
             }
         }
     }
@@ -677,7 +701,8 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
     const int dim = m.dim, c4 = dim >> 2, R = m.ffn_rows;
-    float *w1s = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES);   // [R][dim]
+    float4 *s_x4 = reinterpret_cast<float4 *>(smem_raw + MV_BAR_BYTES);                    // the FFN input
+    float *w1s = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES + vec_smem_bytes(dim));   // [R][dim]
     float *w3s = w1s + (size_t)R * dim;                                 // [R][dim]
     float *w2s = w3s + (size_t)R * dim;                                 // [R][dim]
     __shared__ float s_hb[FF_MAX_ROWS];
@@ -702,7 +727,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
         // per matrix measured 3.6 us/token slower at 110M)
         const size_t off = ((size_t)a.l * m.hidden + j0) * dim;
         const unsigned rb = (unsigned)dim * 4u;
-        const int pk = m.pol_w;
+        constexpr int pk = kPolWeights;
         const uint64_t pol = make_l2_policy(pk);
         mbar_expect_tx(&bars[0], 2u * bytes);
         mbar_expect_tx(&bars[1], bytes);
@@ -717,30 +742,28 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
     load_gain<NV>(gr, m.rms_ffn + (size_t)a.l * dim, c4, lane);
     pdl_wait();
     trace_ev(m, tr, tpos, 2 * a.l + 1, 1);
-    load_act<NV>(xr, a.xin, c4, lane);
-    // the residual this thread adds (CTA 0): issued with the input
+    stage_vec(s_x4, a.xin, c4);
+    __syncthreads();
+    // x is in shared memory: the CTA is done with a.xin and takes its ticket
+    // now; the result is only looked at when the CTA ends
+    unsigned ticket = 0u;
+    if (a.xclear && tid == FF_THREADS - 1) ticket = atomicAdd(&m.tickets[1], 1u);
+    vec_from_smem<NV>(xr, s_x4, c4, lane);
+    // the residual this thread adds (CTA 0)
     constexpr int RV = 2;   // float4 columns per thread: dim <= 4 * RV * FF_THREADS
     float4 res[RV];
 #pragma unroll
     for (int r = 0; r < RV; r++) {
         const int c = tid + r * FF_THREADS;
-        res[r] = (blockIdx.x == 0 && c < c4) ? __ldcg(reinterpret_cast<const float4 *>(a.xin) + c)
-                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        res[r] = (blockIdx.x == 0 && c < c4) ? s_x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     rmsnorm_pre<NV>(xr, gr, dim);
     trace_ev(m, tr, tpos, 2 * a.l + 1, 2);
-    // The input is consumed by rmsnorm; the residual registers are forced
-    // here. Once the barrier below has passed, every thread of the CTA has
-    // done so: the CTA then takes its ticket, looked at when it ends.
-#pragma unroll
-    for (int r = 0; r < RV; r++) asm volatile("" ::"f"(res[r].x), "f"(res[r].y), "f"(res[r].z), "f"(res[r].w));
 
     // A failed wait is recorded in m.err; the CTA then skips its products
     // but still takes part in the ticket.
     bool ok = __syncthreads_and(mbar_wait_bounded(&bars[0], 0u, m.err, ERR_MBAR_TIMEOUT));
     trace_ev(m, tr, tpos, 2 * a.l + 1, 3);
-    unsigned ticket = 0u;
-    if (a.xclear && tid == FF_THREADS - 1) ticket = atomicAdd(&m.tickets[1], 1u);
     if (ok)
         for (int j = warp; j < nj; j += NW) {
             const float h1 = smem_row_dot<NV>(w1s + (size_t)j * dim, xr, c4, lane);
@@ -828,8 +851,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     pdl_trigger();
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);   // [0] q/k/v rows
-    float *stage = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);   // [0] q/k/v rows, [1] wo slice + later K/V rows
+    float4 *s_x4 = reinterpret_cast<float4 *>(smem_raw + MV_BAR_BYTES);   // the layer input x
+    float *stage = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES + vec_smem_bytes(m.dim));
     __shared__ __align__(16) float s_qkv[3 * AT_MAX_HD];        // this head's q, k, v (all CTAs' rows)
     __shared__ __align__(16) float s_part[AC][AT_MAX_HD + 4];   // per-CTA o[hd], max, sum
     __shared__ __align__(16) float s_att[AT_MAX_HD];
@@ -859,10 +883,11 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
         mbar_init_fence();
     }
     __syncthreads();
-    const int pkw = m.pol_w, pkk = m.pol_kv;
+    constexpr int pkw = kPolWeights, pkk = kPolKV;
     const uint64_t polw = make_l2_policy(pkw), polk = make_l2_policy(pkk);
     if (tid == 0) {
         const size_t D = dim, K = m.kvd;
@@ -923,17 +948,18 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     // layer 0 reads the token's embedding row: before the wait when this is
     // the graph's first token, after it otherwise
     const float *xsrc = a.xin ? a.xin : m.emb + (size_t)(m.tok_off == 0 ? __ldcg(&m.step->tok) : 0) * dim;
-    if (!a.xin && m.tok_off == 0) load_act<NV>(xr, xsrc, c4, lane);
+    if (!a.xin && m.tok_off == 0) stage_vec(s_x4, xsrc, c4);
     // every CTA of the cluster runs before any remote store (no memory
     // ordering needed here, so the relaxed form)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
     pdl_wait();
     trace_ev(m, tr, pos, 2 * l, 1);
     if (!a.xin && m.tok_off != 0) xsrc = m.emb + (size_t)__ldcg(&m.step->tok) * dim;
-    if (a.xin || m.tok_off != 0) load_act<NV>(xr, xsrc, c4, lane);
+    if (a.xin || m.tok_off != 0) stage_vec(s_x4, xsrc, c4);
+    __syncthreads();
+    vec_from_smem<NV>(xr, s_x4, c4, lane);
     if (h == 0)
-        for (int i = tid; i < (o1 - o0) / 4; i += AT_THREADS)
-            reinterpret_cast<float4 *>(s_res)[i] = __ldcg(reinterpret_cast<const float4 *>(xsrc + o0) + i);
+        for (int i = tid; i < (o1 - o0) / 4; i += AT_THREADS) reinterpret_cast<float4 *>(s_res)[i] = s_x4[o0 / 4 + i];
     rmsnorm_pre<NV>(xr, gr, dim);
     trace_ev(m, tr, pos, 2 * l, 2);
 
@@ -971,32 +997,31 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     unsigned ticket = 0u;
     if (tid == AT_THREADS - 1) ticket = atomicAdd(&m.tickets[0], 1u);
     // The staging rows are consumed by this CTA's warps: the wo slice (rows
-    // [o0, o1), the hd columns of head h) takes their place, 16 bytes per
-    // thread and copy.
-    {
-        const float *wo_base = m.wo + (size_t)l * dim * dim + (size_t)h * hd;
-        for (int f = tid; f < (o1 - o0) * hd4; f += AT_THREADS) {
-            const int row = f / hd4, c = f - row * hd4;
-            cp_async16_pol(stage + (size_t)row * hd + 4 * c, wo_base + (size_t)(o0 + row) * dim + 4 * c, pkw, polw);
-        }
-    }
-    // K/V rows of the earlier positions past the first round: copied now
-    // into the free part of the staging region (after the wo slice and the
-    // value sums), so later rounds read shared memory; positions beyond its
-    // capacity are read from global memory in their round.
+    // [o0, o1), the hd columns of head h: one bulk copy of hd floats per
+    // row) takes their place, followed by the K/V rows of the earlier
+    // positions past the first round (contiguous in the head-major cache:
+    // one bulk copy each for K and V) in the free part of the region (after
+    // the wo slice and the value sums), so later rounds read shared memory;
+    // positions beyond its capacity are read from global memory in their
+    // round. Warp 0's lanes issue the copies (a few each), so no thread is
+    // held up for long and no per-thread copies occupy the load path.
     float *s_o = stage + (size_t)(dim / AC) * hd;   // value sums [ngrp][hd], after the wo slice
     float *kv2 = s_o + (size_t)ngrp * hd;           // K rows [n2][hd], then V rows [n2][hd]
     const int p2 = t0 + AT_ROUND;
     const int kv2_cap = (a.stage_floats - (dim / AC) * hd - ngrp * hd) / (2 * hd);
     const int n2 = max(0, min(min(t1, pos), p2 + kv2_cap) - p2);
-    if (n2 > 0) {
-        const float *kb = m.kc + (head_base + p2) * hd, *vb = m.vc + (head_base + p2) * hd;
-        for (int f = tid; f < n2 * hd4; f += AT_THREADS) {
-            cp_async16_pol(kv2 + 4 * f, kb + 4 * f, pkk, polk);
-            cp_async16_pol(kv2 + (size_t)n2 * hd + 4 * f, vb + 4 * f, pkk, polk);
-        }
+    if (warp == 0) {
+        fence_proxy_async_smem();   // the warps' reads of the staging rows come before the copies' writes
+        const unsigned row_bytes = (unsigned)hd * 4u;
+        if (lane == 0) mbar_expect_tx(&bars[1], (unsigned)(o1 - o0) * row_bytes + 2u * (unsigned)n2 * row_bytes);
+        const float *wo_base = m.wo + (size_t)l * dim * dim + (size_t)h * hd;
+        for (int row = lane; row < o1 - o0; row += 32)
+            bulk_g2s_pol(stage + (size_t)row * hd, wo_base + (size_t)(o0 + row) * dim, row_bytes, &bars[1], pkw, polw);
+        if (n2 > 0 && lane < 2)
+            bulk_g2s_pol(kv2 + (size_t)lane * n2 * hd, (lane == 0 ? m.kc : m.vc) + (head_base + p2) * hd,
+                         (unsigned)n2 * row_bytes, &bars[1], pkk, polk);
     }
-    cp_async_commit();
+    bool have_b1 = false;   // the wo slice and later K/V rows are resident (bars[1])
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // s_qkv complete
     trace_ev(m, tr, pos, 2 * l, 4);
     // 2. attention over [t0, t1): online softmax in rounds of AT_ROUND
@@ -1011,8 +1036,10 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     for (int rt0 = t0; rt0 < t1; rt0 += AT_ROUND) {
         const int n = min(AT_ROUND, t1 - rt0);
         if (rt0 != t0) {   // later rounds: staged rows from shared memory, the rest from L2 (warmed)
-            cp_async_wait_all();
-            __syncthreads();
+            if (!have_b1) {
+                have_b1 = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
+                bad |= !have_b1;
+            }
             const float4 *kb = reinterpret_cast<const float4 *>(m.kc + (head_base + rt0) * hd);
             const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + rt0) * hd);
             const float4 *ks = reinterpret_cast<const float4 *>(kv2);
@@ -1116,8 +1143,11 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
         s_att[tid] = o * __fdiv_rn(1.0f, L);
     }
-    cp_async_wait_all();
-    __syncthreads();
+    if (!have_b1) {
+        have_b1 = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
+        bad |= !have_b1;
+    }
+    __syncthreads();   // s_att
     // wo rows in quads: lane 8e + k reduces row 4qd + e over float4 columns
     // k, k + 8, ...; lane 0 gathers the quad and adds it at L2.
     const int e8 = lane >> 3, k8 = lane & 7;
@@ -1157,7 +1187,10 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             reinterpret_cast<float4 *>(a.xclear)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (tid == 0) m.tickets[0] = 0u;
     }
-    if (bad && tid == 0) mbar_wait_bounded(&bars[0], 0u, nullptr, 0);   // let the copy land before exiting
+    if (bad && tid == 0) {   // let the copies land before exiting
+        mbar_wait_bounded(&bars[0], 0u, nullptr, 0);
+        mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
+    }
 }
 
 // Host-side launchers --------------------------------------------------------
@@ -1250,7 +1283,7 @@ static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) 
     const int items_max = (a.n_items + grid - 1) / grid;
     int stages = (items_max + a.per_stage - 1) / a.per_stage;
     if (stages > n_stages) stages = n_stages;
-    const size_t smem = (size_t)MV_BAR_BYTES + (size_t)stages * stage_bytes;
+    const size_t smem = (size_t)MV_BAR_BYTES + vec_smem_bytes(a.cols) + (size_t)stages * stage_bytes;
     // Every decode kernel gets the same (maximal) shared-memory carveout, so
     // consecutive kernels co-reside on an SM without reconfiguring L1.
     ensure_kernel_smem((const void *)k_mv<NV, MODE>, smem);
@@ -1270,14 +1303,14 @@ static MvArgs mv_args(int n_items, int cols, int slots, int l) {
 template <int NV>
 static void launch_ffn(const DecodeModel &m, FfnArgs a, int n_sm, cudaStream_t s) {
     const int grid = m.hidden < n_sm ? m.hidden : n_sm;
-    const size_t smem = (size_t)MV_BAR_BYTES + 3 * (size_t)m.ffn_rows * m.dim * 4;
+    const size_t smem = (size_t)MV_BAR_BYTES + vec_smem_bytes(m.dim) + 3 * (size_t)m.ffn_rows * m.dim * 4;
     ensure_kernel_smem((const void *)k_ffn<NV>, smem);
     launch_pdl(k_ffn<NV>, dim3(grid), dim3(FF_THREADS), smem, s, m, a);
 }
 
 template <int NV>
 static void launch_attn_fused(const DecodeModel &m, AttnArgs a, cudaStream_t s) {
-    const size_t smem = (size_t)MV_BAR_BYTES + (size_t)m.attn_stage * 4;
+    const size_t smem = (size_t)MV_BAR_BYTES + vec_smem_bytes(m.dim) + (size_t)m.attn_stage * 4;
     ensure_kernel_smem((const void *)k_attn_fused<NV>, smem);
     a.stage_floats = m.attn_stage;
     launch_cluster_pdl(k_attn_fused<NV>, dim3(m.nh * AC), dim3(AT_THREADS), smem, AC, s, m, a);
@@ -1309,7 +1342,7 @@ int decode_ffn_rows(int dim, int hidden, int n_sm) {
     const int grid = hidden < n_sm ? hidden : n_sm;
     const int rows = (hidden + grid - 1) / grid;
     if (rows > FF_MAX_ROWS || dim / 4 > 2 * FF_THREADS) return 0;
-    if (3 * (size_t)rows * dim * 4 > (size_t)FF_MAX_SMEM) return 0;
+    if (3 * (size_t)rows * dim * 4 + vec_smem_bytes(dim) > (size_t)FF_MAX_SMEM) return 0;
     return rows;
 }
 

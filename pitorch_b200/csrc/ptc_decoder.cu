@@ -38,8 +38,8 @@ struct ptc_decoder {
     int mode;              // current StepState.mode on the device
     cudaGraphExec_t g_host, g_dev;
     cudaGraphExec_t g_devk;  // DEV_TOKENS device-loop tokens per launch (null: not used)
-    size_t trace_n;        // entries of m.trace
-    int trace_on;          // host copy of step->trace_on
+    unsigned long long *trace_buf;  // phase timeline record (m.trace while tracing)
+    size_t trace_n;        // its entries
 };
 
 static void enqueue_kernels(ptc_decoder *d, const DecodeModel &m, cudaStream_t s, int *host_next) {
@@ -68,6 +68,32 @@ static cudaGraphExec_t capture(ptc_decoder *d, bool host_io) {
     PTC_CHECK(cudaGraphInstantiate(&ge, g, 0));
     PTC_CHECK(cudaGraphDestroy(g));
     return ge;
+}
+
+// (Re)capture the host-step graph, the one-position device-loop graph and the
+// DEV_TOKENS-position one from the current d->m.
+static void capture_graphs(ptc_decoder *d) {
+    if (d->g_host) PTC_CHECK(cudaGraphExecDestroy(d->g_host));
+    if (d->g_dev) PTC_CHECK(cudaGraphExecDestroy(d->g_dev));
+    if (d->g_devk) PTC_CHECK(cudaGraphExecDestroy(d->g_devk));
+    d->g_host = capture(d, true);
+    d->g_dev = capture(d, false);
+    d->g_devk = nullptr;
+    const DecodeModel &m = d->m;
+    if (d->has_embed && d->has_head && m.L > 0) {
+        cudaStream_t s = d->stream;
+        cudaGraph_t g;
+        PTC_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        for (int k = 0; k < DEV_TOKENS; k++) {
+            DecodeModel mk = m;
+            mk.tok_off = k;
+            mk.adv = k == DEV_TOKENS - 1;
+            enqueue_kernels(d, mk, s, nullptr);
+        }
+        PTC_CHECK(cudaStreamEndCapture(s, &g));
+        PTC_CHECK(cudaGraphInstantiate(&d->g_devk, g, 0));
+        PTC_CHECK(cudaGraphDestroy(g));
+    }
 }
 
 // A decode kernel whose bounded wait expired left a code in m.err; report it
@@ -159,17 +185,6 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     m.fused_ffn = m.L > 0 && m.ffn_rows > 0 && !no_fuse;
     m.attn_stage = ptc::decode_attn_stage(m.dim, m.nh, m.nkv, m.seq);
     m.fused_attn = m.fused_ffn && m.attn_stage > 0 && !ffn_only;
-    // L2 eviction priorities of the fused kernels' own loads. PTC_L2_POLICY
-    // = "w,cls,kv" with 0 none, 1 evict_first, 2 evict_last, 3 evict_normal
-    // (default: none).
-    if (const char *pe = getenv("PTC_L2_POLICY")) {
-        int a = 0, b = 0, k = 0;
-        if (sscanf(pe, "%d,%d,%d", &a, &b, &k) == 3 && a >= 0 && a <= 3 && b >= 0 && b <= 3 && k >= 0 && k <= 3) {
-            m.pol_w = a;
-            m.pol_cls = b;
-            m.pol_kv = k;
-        }
-    }
     m.tickets = (unsigned *)ptc_alloc(c, 64);
     PTC_CHECK(cudaMemsetAsync(m.tickets, 0, 64, s));
     if (m.fused_attn) {
@@ -183,7 +198,8 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
         m.w2t = w2t;
     }
     d->trace_n = (size_t)2 * ptc::TRACE_POS * (2 * m.L + 1) * ptc::TRACE_EV;
-    m.trace = (unsigned long long *)ptc_alloc(c, d->trace_n * sizeof(unsigned long long));
+    d->trace_buf = (unsigned long long *)ptc_alloc(c, d->trace_n * sizeof(unsigned long long));
+    m.trace = nullptr;
     if (m.fused_ffn) {
         m.xm = (float *)ptc_alloc(c, (size_t)m.dim * 4);
         m.xo = (float *)ptc_alloc(c, (size_t)m.L * m.dim * 4);
@@ -207,22 +223,8 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     size_t stage = (size_t)(m.V > m.dim ? m.V : m.dim) * 4;
     d->stage = (float *)ptc_host_alloc(stage);
 
-    d->g_host = capture(d, true);
-    d->g_dev = capture(d, false);
-    d->g_devk = nullptr;
-    if (has_embed && has_head && m.L > 0) {
-        cudaGraph_t g;
-        PTC_CHECK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-        for (int k = 0; k < DEV_TOKENS; k++) {
-            DecodeModel mk = m;
-            mk.tok_off = k;
-            mk.adv = k == DEV_TOKENS - 1;
-            enqueue_kernels(d, mk, s, nullptr);
-        }
-        PTC_CHECK(cudaStreamEndCapture(s, &g));
-        PTC_CHECK(cudaGraphInstantiate(&d->g_devk, g, 0));
-        PTC_CHECK(cudaGraphDestroy(g));
-    }
+    d->g_host = d->g_dev = d->g_devk = nullptr;
+    capture_graphs(d);
 
     return d;
 }
@@ -234,24 +236,27 @@ extern "C" void ptc_decoder_weights_updated(ptc_decoder *d) {
     ptc::transpose_w2(d->m, (float *)d->m.w2t, d->stream);
 }
 
+// Tracing is a kernel parameter (m.trace non-null), so the untraced kernels
+// pay nothing for it: turning it on or off re-captures the graphs.
 extern "C" size_t ptc_decoder_trace(ptc_decoder *d, int on) {
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
     if (on) {   // earliest stamps start high, latest stamps low
         unsigned long long *h = (unsigned long long *)malloc(d->trace_n * sizeof(unsigned long long));
         for (size_t i = 0; i < d->trace_n; i++) h[i] = (i & 1) ? 0ull : ~0ull;
-        PTC_CHECK(cudaMemcpyAsync(d->m.trace, h, d->trace_n * sizeof(unsigned long long), cudaMemcpyHostToDevice,
-                                  d->stream));
-        PTC_CHECK(cudaStreamSynchronize(d->stream));
+        PTC_CHECK(cudaMemcpy(d->trace_buf, h, d->trace_n * sizeof(unsigned long long), cudaMemcpyHostToDevice));
         free(h);
     }
-    d->trace_on = on ? 1 : 0;
-    PTC_CHECK(cudaMemcpyAsync(&d->m.step->trace_on, &d->trace_on, sizeof(int), cudaMemcpyHostToDevice, d->stream));
-    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    unsigned long long *want = on ? d->trace_buf : nullptr;
+    if (d->m.trace != want) {
+        d->m.trace = want;
+        capture_graphs(d);
+    }
     return d->trace_n;
 }
 
 extern "C" size_t ptc_decoder_read_trace(ptc_decoder *d, unsigned long long *out, size_t n) {
     if (n > d->trace_n) n = d->trace_n;
-    PTC_CHECK(cudaMemcpyAsync(out, d->m.trace, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, d->stream));
+    PTC_CHECK(cudaMemcpyAsync(out, d->trace_buf, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     return n;
 }
@@ -335,7 +340,6 @@ extern "C" void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, in
     st.n_prompt = n_prompt;
     st.mode = 1;
     st.tokens = d->d_tokens;
-    st.trace_on = d->trace_on;
     PTC_CHECK(cudaMemcpyAsync(d->m.step, &st, sizeof(st), cudaMemcpyHostToDevice, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     d->mode = 1;

@@ -797,6 +797,12 @@ extern "C" void ptc_trainer_set_tokens(ptc_trainer *tr, const int *tokens, int T
     PTC_CHECK(cudaMemcpyAsync(tr->tokens, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, tr->s));
 }
 
+extern "C" void ptc_trainer_set_T(ptc_trainer *tr, int T) {
+    if (T < 2 || T > tr->maxT) PTC_FATAL("T=%d outside [2, max_T=%d]", T, tr->maxT);
+    if (T > tr->seq) PTC_FATAL("T=%d exceeds seq_len %d", T, tr->seq);
+    tr->T = T;
+}
+
 extern "C" void ptc_trainer_zero_grads(ptc_trainer *tr) {
     PTC_CHECK(cudaMemsetAsync(tr->g_mem, 0, tr->n_params * 4, tr->s));
 }
