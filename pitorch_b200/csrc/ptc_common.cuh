@@ -177,6 +177,17 @@ __device__ __forceinline__ void red_add_v4(float *dst, float4 v) {
                  : "memory");
 }
 
+// Fire-and-forget 64-bit max at L2, and an add with acquire-release
+// semantics at GPU scope that returns the old value.
+__device__ __forceinline__ void red_max_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Programmatic dependent launch (sm_90+): wait for the producer grid's
 // memory, and let the next grid in the stream start its prologue early.
 __device__ __forceinline__ void pdl_wait() {

@@ -149,8 +149,10 @@ __device__ __forceinline__ void vec_from_smem(float4 (&x)[NV], const float4 *s_x
 // Bytes of the shared-memory copy of an n-float vector (128-byte multiple).
 __host__ __device__ constexpr int vec_smem_bytes(int n) { return (n * 4 + 127) / 128 * 128; }
 
-// Phase timeline stamp by thread 0 of a CTA, only while tracing: the slot of
-// (position, kernel k, event e) keeps the earliest and the latest time.
+// Phase timeline stamp by thread 0 of a CTA, only in the kernels' traced
+// instantiation (template flag TR; the untraced ones carry no trace code):
+// the slot of (position, kernel k, event e) keeps the earliest and the
+// latest time.
 __device__ __forceinline__ void trace_ev(const DecodeModel &m, bool on, int pos, int k, int e) {
     if (!on || threadIdx.x != 0) return;
     const unsigned long long t = globaltimer_ns();
@@ -159,7 +161,6 @@ __device__ __forceinline__ void trace_ev(const DecodeModel &m, bool on, int pos,
     atomicMax(slot + 1, t);
 }
 
-__device__ __forceinline__ bool trace_on(const DecodeModel &m) { return m.trace != nullptr; }
 
 // L2 eviction priority of the decode kernels' own loads: the layer weights
 // and the KV rows are read once per token and marked evict_first, so that
@@ -458,13 +459,16 @@ __device__ __forceinline__ float smem_row_dot(const float *row, const float4 (&x
     return warp_sum(acc);
 }
 
-template <int NV, int MODE>
+template <int NV, int MODE, bool TR>
 __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     pdl_trigger();
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);
-    float4 *s_x4 = reinterpret_cast<float4 *>(smem_raw + MV_BAR_BYTES);   // the input vector
-    float *stages = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES + vec_smem_bytes(a.cols));
+    // the input vector, staged once per CTA (not for the classifier: its x
+    // read queues behind its own 98 MB stream either way, and the 3 KB would
+    // keep it from sharing an SM with the last FFN block)
+    float4 *s_x4 = reinterpret_cast<float4 *>(smem_raw + MV_BAR_BYTES);
+    float *stages = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES + (MODE == MV_CLS ? 0 : vec_smem_bytes(a.cols)));
     __shared__ unsigned long long s_best[MV_THREADS / 32];
     __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -491,7 +495,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     // for layer 0 -- the token's embedding row (set by an earlier launch).
     float4 xr[NV], gr[NV];
     int pos = 0;
-    const bool tr = MODE == MV_CLS && trace_on(m);
+    constexpr bool tr = MODE == MV_CLS && TR;
     const int tpos = tr ? __ldcg(&m.step->pos) + m.tok_off : 0;
     trace_ev(m, tr, tpos, 2 * m.L, 0);
     const bool early = MODE == MV_QKV && a.from_embedding && m.tok_off == 0;
@@ -516,14 +520,18 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
             xres[q] = (lane == 0 && n_chunks <= NST && i < it1) ? __ldcg(a.res_in + i) : 0.f;
         }
     }
-    if (!early) {
-        const float *src = a.in;
-        if (MODE == MV_QKV && a.from_embedding) src = m.emb + (size_t)__ldcg(&m.step->tok) * m.dim;
-        if (MODE == MV_FFN13 || MODE == MV_CLS) src = m.x;
-        stage_vec(s_x4, src, c4);
+    if (MODE == MV_CLS) {
+        load_act<NV>(xr, m.x, c4, lane);
+    } else {
+        if (!early) {
+            const float *src = a.in;
+            if (MODE == MV_QKV && a.from_embedding) src = m.emb + (size_t)__ldcg(&m.step->tok) * m.dim;
+            if (MODE == MV_FFN13) src = m.x;
+            stage_vec(s_x4, src, c4);
+        }
+        __syncthreads();
+        vec_from_smem<NV>(xr, s_x4, c4, lane);
     }
-    __syncthreads();
-    vec_from_smem<NV>(xr, s_x4, c4, lane);
     if (MODE == MV_QKV) {
         if (a.from_embedding && blockIdx.x == 0 && warp == 0) store_vec<NV>(m.x, xr, c4, lane);
         rmsnorm_pre<NV>(xr, gr, m.dim);
@@ -643,22 +651,22 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         if (a.host_next) err_seen = __ldcg(m.err);   // its latency overlaps the atomics below
         unsigned long long b = 0ull;
         for (int w = 0; w < NW; w++) b = s_best[w] > b ? s_best[w] : b;
-        if (b) atomicMax(&st->amax, b);
-        __threadfence();
-        const unsigned ticket = atomicAdd(&st->done, 1u);
+        // the CTA's best key, then its ticket with release semantics (which
+        // orders the max before it) and acquire semantics (so the last CTA
+        // sees every other CTA's max): two global round trips in all
+        if (b) red_max_u64(&st->amax, b);
+        const unsigned ticket = atom_add_acq_rel(&st->done, 1u);
         s_last = (ticket == gridDim.x - 1);
     }
     __syncthreads();
     if (!s_last || tid != 0) return;
-    __threadfence();
-    const unsigned long long key = atomicAdd(&st->amax, 0ull);
+    const unsigned long long key = __ldcg(&st->amax);
     const int next = argmax_key_index(key);
     st->next = next;
     if (a.host_next) {   // straight into the host's pinned word: no copy node after the kernel
         // -1 sends the host to the error word, so a token computed after an
         // expired wait is never returned as valid
         *reinterpret_cast<volatile int *>(a.host_next) = err_seen ? -1 : next;
-        __threadfence_system();
     }
     st->amax = 0ull;
     st->done = 0u;
@@ -670,7 +678,9 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         st->tok = t;
         if (m.adv) st->pos = p + 1;
     }
-    __threadfence();
+    // no fence: the next kernel reads these after griddepcontrol.wait, and
+    // the host after the stream synchronises -- both see a completed grid's
+    // writes
     trace_ev(m, tr, tpos, 2 * m.L, 7);
 }
 
@@ -695,7 +705,7 @@ struct FfnArgs {
     int l;
 };
 
-template <int NV>
+template <int NV, bool TR>
 __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a) {
     pdl_trigger();
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -713,7 +723,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
     const int j1 = (int)((long)m.hidden * (blockIdx.x + 1) / gridDim.x);
     const int nj = j1 - j0;
     const unsigned bytes = (unsigned)nj * (unsigned)dim * 4u;
-    const bool tr = trace_on(m);
+    constexpr bool tr = TR;
     const int tpos = tr ? __ldcg(&m.step->pos) + m.tok_off : 0;
     trace_ev(m, tr, tpos, 2 * a.l + 1, 0);
     if (tid == 0) {
@@ -842,7 +852,7 @@ struct AttnArgs {
     int stage_floats;  // shared staging region (q/k/v rows, then wo slice + value sums)
 };
 
-template <int NV>
+template <int NV, bool TR>
 __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, AttnArgs a) {
     // The next kernel (k_ffn) may start at once: its 18.9 MB (110M) weight
     // stream must be resident by its wait. Releasing it later, after this
@@ -851,7 +861,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     pdl_trigger();
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);   // [0] q/k/v rows, [1] wo slice + later K/V rows
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw);   // [0] q/k/v rows
     float4 *s_x4 = reinterpret_cast<float4 *>(smem_raw + MV_BAR_BYTES);   // the layer input x
     float *stage = reinterpret_cast<float *>(smem_raw + MV_BAR_BYTES + vec_smem_bytes(m.dim));
     __shared__ __align__(16) float s_qkv[3 * AT_MAX_HD];        // this head's q, k, v (all CTAs' rows)
@@ -874,7 +884,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     // still reached, with no K/V write and the error recorded
     const int pos = pos_ok ? pos_raw : 0;
     if (!pos_ok) flag_pos_range(m);
-    const bool tr = trace_on(m);
+    constexpr bool tr = TR;
     trace_ev(m, tr, pos, 2 * l, 0);
     // positions of this CTA: [t0, t1) of [0, pos]
     const int ppc = (pos + AC) / AC;
@@ -883,7 +893,6 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
 
     if (tid == 0) {
         mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
         mbar_init_fence();
     }
     __syncthreads();
@@ -997,31 +1006,34 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     unsigned ticket = 0u;
     if (tid == AT_THREADS - 1) ticket = atomicAdd(&m.tickets[0], 1u);
     // The staging rows are consumed by this CTA's warps: the wo slice (rows
-    // [o0, o1), the hd columns of head h: one bulk copy of hd floats per
-    // row) takes their place, followed by the K/V rows of the earlier
-    // positions past the first round (contiguous in the head-major cache:
-    // one bulk copy each for K and V) in the free part of the region (after
-    // the wo slice and the value sums), so later rounds read shared memory;
-    // positions beyond its capacity are read from global memory in their
-    // round. Warp 0's lanes issue the copies (a few each), so no thread is
-    // held up for long and no per-thread copies occupy the load path.
+    // [o0, o1), the hd columns of head h) takes their place, 16 bytes per
+    // thread and copy, followed by the K/V rows of the earlier positions past
+    // the first round in the free part of the region (after the wo slice and
+    // the value sums), so later rounds read shared memory; positions beyond
+    // its capacity are read from global memory in their round. (The same
+    // copies as bulk copies issued by one warp measured 199 -> 227 us/token:
+    // their issue waits behind the FFN block's bulk copies on the SM's copy
+    // engine, and the cluster barrier waits for that warp.)
     float *s_o = stage + (size_t)(dim / AC) * hd;   // value sums [ngrp][hd], after the wo slice
     float *kv2 = s_o + (size_t)ngrp * hd;           // K rows [n2][hd], then V rows [n2][hd]
     const int p2 = t0 + AT_ROUND;
     const int kv2_cap = (a.stage_floats - (dim / AC) * hd - ngrp * hd) / (2 * hd);
     const int n2 = max(0, min(min(t1, pos), p2 + kv2_cap) - p2);
-    if (warp == 0) {
-        fence_proxy_async_smem();   // the warps' reads of the staging rows come before the copies' writes
-        const unsigned row_bytes = (unsigned)hd * 4u;
-        if (lane == 0) mbar_expect_tx(&bars[1], (unsigned)(o1 - o0) * row_bytes + 2u * (unsigned)n2 * row_bytes);
+    {
         const float *wo_base = m.wo + (size_t)l * dim * dim + (size_t)h * hd;
-        for (int row = lane; row < o1 - o0; row += 32)
-            bulk_g2s_pol(stage + (size_t)row * hd, wo_base + (size_t)(o0 + row) * dim, row_bytes, &bars[1], pkw, polw);
-        if (n2 > 0 && lane < 2)
-            bulk_g2s_pol(kv2 + (size_t)lane * n2 * hd, (lane == 0 ? m.kc : m.vc) + (head_base + p2) * hd,
-                         (unsigned)n2 * row_bytes, &bars[1], pkk, polk);
+        for (int f = tid; f < (o1 - o0) * hd4; f += AT_THREADS) {
+            const int row = f / hd4, c = f - row * hd4;
+            cp_async16_pol(stage + (size_t)row * hd + 4 * c, wo_base + (size_t)(o0 + row) * dim + 4 * c, pkw, polw);
+        }
+        if (n2 > 0) {
+            const float *kb = m.kc + (head_base + p2) * hd, *vb = m.vc + (head_base + p2) * hd;
+            for (int f = tid; f < n2 * hd4; f += AT_THREADS) {
+                cp_async16_pol(kv2 + 4 * f, kb + 4 * f, pkk, polk);
+                cp_async16_pol(kv2 + (size_t)n2 * hd + 4 * f, vb + 4 * f, pkk, polk);
+            }
+        }
+        cp_async_commit();
     }
-    bool have_b1 = false;   // the wo slice and later K/V rows are resident (bars[1])
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // s_qkv complete
     trace_ev(m, tr, pos, 2 * l, 4);
     // 2. attention over [t0, t1): online softmax in rounds of AT_ROUND
@@ -1036,10 +1048,8 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     for (int rt0 = t0; rt0 < t1; rt0 += AT_ROUND) {
         const int n = min(AT_ROUND, t1 - rt0);
         if (rt0 != t0) {   // later rounds: staged rows from shared memory, the rest from L2 (warmed)
-            if (!have_b1) {
-                have_b1 = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
-                bad |= !have_b1;
-            }
+            cp_async_wait_all();
+            __syncthreads();
             const float4 *kb = reinterpret_cast<const float4 *>(m.kc + (head_base + rt0) * hd);
             const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + rt0) * hd);
             const float4 *ks = reinterpret_cast<const float4 *>(kv2);
@@ -1143,11 +1153,8 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
         s_att[tid] = o * __fdiv_rn(1.0f, L);
     }
-    if (!have_b1) {
-        have_b1 = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
-        bad |= !have_b1;
-    }
-    __syncthreads();   // s_att
+    cp_async_wait_all();
+    __syncthreads();   // s_att and the wo slice
     // wo rows in quads: lane 8e + k reduces row 4qd + e over float4 columns
     // k, k + 8, ...; lane 0 gathers the quad and adds it at L2.
     const int e8 = lane >> 3, k8 = lane & 7;
@@ -1187,10 +1194,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             reinterpret_cast<float4 *>(a.xclear)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (tid == 0) m.tickets[0] = 0u;
     }
-    if (bad && tid == 0) {   // let the copies land before exiting
-        mbar_wait_bounded(&bars[0], 0u, nullptr, 0);
-        mbar_wait_bounded(&bars[1], 0u, nullptr, 0);
-    }
+    if (bad && tid == 0) mbar_wait_bounded(&bars[0], 0u, nullptr, 0);   // let the copy land before exiting
 }
 
 // Host-side launchers --------------------------------------------------------
@@ -1283,11 +1287,19 @@ static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) 
     const int items_max = (a.n_items + grid - 1) / grid;
     int stages = (items_max + a.per_stage - 1) / a.per_stage;
     if (stages > n_stages) stages = n_stages;
-    const size_t smem = (size_t)MV_BAR_BYTES + vec_smem_bytes(a.cols) + (size_t)stages * stage_bytes;
+    const size_t smem = (size_t)MV_BAR_BYTES + (MODE == MV_CLS ? 0 : vec_smem_bytes(a.cols)) +
+                        (size_t)stages * stage_bytes;
     // Every decode kernel gets the same (maximal) shared-memory carveout, so
     // consecutive kernels co-reside on an SM without reconfiguring L1.
-    ensure_kernel_smem((const void *)k_mv<NV, MODE>, smem);
-    launch_pdl(k_mv<NV, MODE>, dim3(grid), dim3(MV_THREADS), smem, s, m, a);
+    if constexpr (MODE == MV_CLS) {
+        if (m.trace) {
+            ensure_kernel_smem((const void *)k_mv<NV, MODE, true>, smem);
+            launch_pdl(k_mv<NV, MODE, true>, dim3(grid), dim3(MV_THREADS), smem, s, m, a);
+            return;
+        }
+    }
+    ensure_kernel_smem((const void *)k_mv<NV, MODE, false>, smem);
+    launch_pdl(k_mv<NV, MODE, false>, dim3(grid), dim3(MV_THREADS), smem, s, m, a);
 }
 
 static MvArgs mv_args(int n_items, int cols, int slots, int l) {
@@ -1304,16 +1316,18 @@ template <int NV>
 static void launch_ffn(const DecodeModel &m, FfnArgs a, int n_sm, cudaStream_t s) {
     const int grid = m.hidden < n_sm ? m.hidden : n_sm;
     const size_t smem = (size_t)MV_BAR_BYTES + vec_smem_bytes(m.dim) + 3 * (size_t)m.ffn_rows * m.dim * 4;
-    ensure_kernel_smem((const void *)k_ffn<NV>, smem);
-    launch_pdl(k_ffn<NV>, dim3(grid), dim3(FF_THREADS), smem, s, m, a);
+    auto kern = m.trace ? k_ffn<NV, true> : k_ffn<NV, false>;
+    ensure_kernel_smem((const void *)kern, smem);
+    launch_pdl(kern, dim3(grid), dim3(FF_THREADS), smem, s, m, a);
 }
 
 template <int NV>
 static void launch_attn_fused(const DecodeModel &m, AttnArgs a, cudaStream_t s) {
     const size_t smem = (size_t)MV_BAR_BYTES + vec_smem_bytes(m.dim) + (size_t)m.attn_stage * 4;
-    ensure_kernel_smem((const void *)k_attn_fused<NV>, smem);
+    auto kern = m.trace ? k_attn_fused<NV, true> : k_attn_fused<NV, false>;
+    ensure_kernel_smem((const void *)kern, smem);
     a.stage_floats = m.attn_stage;
-    launch_cluster_pdl(k_attn_fused<NV>, dim3(m.nh * AC), dim3(AT_THREADS), smem, AC, s, m, a);
+    launch_cluster_pdl(kern, dim3(m.nh * AC), dim3(AT_THREADS), smem, AC, s, m, a);
 }
 
 // Staging floats of k_attn_fused for this model, or 0 when the fused
