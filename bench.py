@@ -451,6 +451,30 @@ SWEEP_SHAPES = [(288, 288), (768, 288), (288, 768), (512, 512), (1376, 512), (20
 L2_BYTES = 126 * 1024 * 1024
 
 
+def sweep_references(L, pc, stream, graph_time, hbm, src):
+    """The sweep's two measured references: the L2 read bandwidth (48 MiB,
+    L2-resident, read 20 times per graph replay by ptc_read_probe) and the
+    per-call floor of a chain of dependent matvec launches (8 x 4, 512 per
+    graph). Prints them as one JSON line and returns both."""
+    l2_bytes = 48 << 20
+    probe = L.ptc_alloc(pc, l2_bytes)
+    sink = L.ptc_alloc(pc, 256)
+    L.ptc_memset(pc, probe, 0, l2_bytes)
+    ms = graph_time(lambda: [L.ptc_read_probe(probe, l2_bytes, sink, stream) for _ in range(20)], 10)
+    l2_gbs = 20 * l2_bytes / (ms / 1000.0) / 1e9
+    # per-call floor of dependent matvec launches (PDL chain in a graph)
+    tW, tx, ty = L.ptc_alloc(pc, 8 * 4 * 4), L.ptc_alloc(pc, 64), L.ptc_alloc(pc, 64)
+    L.ptc_memset(pc, tW, 0, 128)
+    L.ptc_memset(pc, tx, 0, 64)
+    floor_us = 1000 * graph_time(lambda: [L.ptc_matvec(tW, tx, ty, 8, 4, stream) for _ in range(512)], 10) / 512
+    print(json.dumps({"metric": "matvec sweep references", "l2_read_gbs": l2_gbs,
+                      "l2_probe": f"ptc_read_probe over {l2_bytes >> 20} MiB, 20 reads per graph replay",
+                      "launch_floor_us": floor_us,
+                      "launch_floor": "8x4 matvec, 512 dependent launches per graph (PDL)",
+                      "hbm_peak_gbs": hbm, "hbm_peak_source": f"{src} hbm_gbs"}), flush=True)
+    return l2_gbs, floor_us
+
+
 def run_sweep(args):
     """The isolated fp32 matvec sweep y = W.x (W rows x cols, W ~ N(0,0.02),
     x ~ N(0,1), seeded) through the C ABI's ptc_matvec. Per shape, one JSON
@@ -461,7 +485,12 @@ def run_sweep(args):
             programmatic dependent launch, as in a decode step);
       hot   the same, always the same W (L2-resident when it fits);
       cpu_baseline  the reference's own smatvec_cpu (oracle/_ref), 1 thread.
-    Algorithmic bytes per call: 4*(rows*cols + rows + cols)."""
+    Algorithmic bytes per call: 4*(rows*cols + rows + cols).
+    Two measured references come first: the L2 read bandwidth (ptc_read_probe
+    over a 48 MiB buffer read back to back, L2-resident) for the hot column,
+    and the per-call floor of a chain of dependent matvec launches (an 8 x 4
+    matvec, whose bytes take no time), so that every shape's attainable time
+    is max(bytes / peak, floor)."""
     import ctypes as C
     import oracle
     import pitorch_b200
@@ -471,6 +500,26 @@ def run_sweep(args):
     stream = L.ptc_stream(pc)
     timer = L.ptc_timer_create(pc)
     hbm, src = peaks()
+
+    def graph_time(calls, reps):
+        """ms per replay of a captured graph of the (callable) enqueues."""
+        L.ptc_capture_begin(pc)
+        calls()
+        g = L.ptc_capture_end(pc)
+        for _ in range(3):
+            L.ptc_graph_launch(g)
+        L.ptc_sync(pc)
+        L.ptc_timer_start(timer)
+        for _ in range(reps):
+            L.ptc_graph_launch(g)
+        L.ptc_timer_stop(timer)
+        ms = L.ptc_timer_ms(timer) / reps
+        L.ptc_graph_destroy(g)
+        return ms
+
+    l2_gbs, floor_us = None, 0.0
+    if not args.sweep_no_refs:
+        l2_gbs, floor_us = sweep_references(L, pc, stream, graph_time, hbm, src)
     shapes = SWEEP_SHAPES
     if args.sweep_shapes:
         shapes = [tuple(int(v) for v in s.split("x")) for s in args.sweep_shapes.split(",")]
@@ -518,8 +567,13 @@ def run_sweep(args):
             L.ptc_graph_destroy(g)
             us_call = 1000 * ms / (reps * n_calls)
             gbs = bytes_call / (us_call * 1e-6) / 1e9
+            peak_mode = hbm if (mode == "cold" or not l2_gbs or wbytes > L2_BYTES // 2) else l2_gbs
+            attain_us = max(bytes_call / (peak_mode * 1e3), floor_us)
             res[mode] = {"GB/s": gbs, "us_per_call": us_call, "calls_per_graph": n_calls,
-                         "frac_of_hbm": gbs / hbm}
+                         "frac_of_hbm": gbs / hbm, "peak": peak_mode,
+                         "peak_kind": "hbm" if peak_mode == hbm else "l2 (measured)",
+                         "frac_of_peak": gbs / peak_mode,
+                         "attainable_us": attain_us, "frac_of_attainable": attain_us / us_call}
         # CPU: the reference's smatvec_cpu on a bounded sample
         n_cpu, t0 = 0, time.perf_counter()
         while time.perf_counter() - t0 < 0.3 or n_cpu < 2:
@@ -618,6 +672,8 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="isolated fp32 matvec sweep (one JSON line per W shape) instead of the decode")
     ap.add_argument("--sweep-shapes", default="", help="e.g. 32000x768,2048x768 (default: the 9 shapes)")
+    ap.add_argument("--sweep-no-refs", action="store_true",
+                    help="skip the sweep's L2 and launch-floor references (for per-shape ncu captures)")
     ap.add_argument("--train", action="store_true", help="stories15M training step (T=256) instead of the decode")
     ap.add_argument("--timeline", action="store_true",
                     help="phase timeline of the decode kernels over 16 positions (ptc_decoder_trace)")

@@ -67,6 +67,20 @@ int pt_dist_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token);
 int pt_dist_generate_greedy(pt_context_t *ctx, pt_dist_t *dist, const int *prompt,
                             int n_prompt, int n_pos, int *out_tokens);
 
+/* GPipe microbatched pipeline training step: the schedule the reference
+ * runs by hand in dev/tests/dist/train_pp/test_train_pp_mb_rank{0,1}.c
+ * (it has no library call for it). n_mb microbatches of T tokens each
+ * (tokens holds n_mb * T ids, microbatch m at tokens + m * T) go forward
+ * through the ring one after another, so neighbouring ranks work on
+ * different microbatches at once; then backward in reverse order with the
+ * gradients accumulated; then ONE SGD update with lr (the reference's test
+ * passes lr / n_mb for the effective step of one microbatch). Every rank
+ * calls it with the same T and n_mb (1 <= n_mb <= 16); only the head rank
+ * reads tokens. The head rank returns the mean loss over the microbatches;
+ * total_ms = 0 on a communication failure. */
+pt_dist_result_t pt_dist_train_step_mb(pt_context_t *ctx, pt_dist_t *dist, const int *tokens, int T, int n_mb,
+                                       float lr);
+
 /* Data-parallel gradient averaging: after it, every rank holds the mean of
  * all ranks' gradients (pitorch/dist/collective/pt_allreduce.c:50-165, a
  * 2-rank GPIO protocol; here ncclAllReduce with ncclAvg on the device

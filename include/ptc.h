@@ -70,6 +70,14 @@ void *ptc_upload_image(ptc_ctx *c, const void *image, size_t bytes, size_t heade
  * and W/x are 16-byte aligned. Asynchronous. */
 void ptc_matvec(const float *W, const float *x, float *y, int rows, int cols, void *stream);
 
+/* Measurement hook (no reference counterpart): stream `bytes` (a multiple
+ * of 16, 16-byte aligned) of DEVICE memory through L2-only loads with
+ * 4 CTAs per SM, on `stream`. Timed over a buffer that fits in L2 and was
+ * just read, it gives the L2 read bandwidth the matvec sweep's hot shapes
+ * are compared with; over a buffer larger than L2, the HBM read bandwidth.
+ * `sink` is a device float the kernel may write. */
+void ptc_read_probe(const void *buf, size_t bytes, float *sink, void *stream);
+
 /* Same contract as pitorch's pt_matvec_fn callback (llama2.h:74-75) and the
  * Pi's matvec_gpu wrapper (pt.c:21-25): HOST pointers, synchronous. W is
  * looked up among images uploaded with ptc_upload_image (and the registered
@@ -109,7 +117,8 @@ ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, const ptc_wei
                                 int has_embed, int has_head);
 void ptc_decoder_destroy(ptc_decoder *d);
 
-/* Zero the KV cache (pt_reset_kv, pitorch/pt.c:273-280). */
+/* Zero the KV cache and the device position (pt_reset_kv,
+ * pitorch/pt.c:273-280). */
 void ptc_decoder_reset(ptc_decoder *d);
 
 /* One position. Input: `token` when has_embed, else the residual stream
@@ -311,6 +320,12 @@ int ptc_mailbox_handle(void *box, void *handle_out);
 void *ptc_mailbox_open(ptc_ctx *c, const void *handle);  /* NULL when the peer cannot be mapped */
 void ptc_mailbox_close(void *peer);
 void ptc_hop_send(ptc_ctx *c, const float *x, const int *pos, void *peer_box, unsigned *sent, int dim);
+/* ptc_hop_send, then *pos += 1 on the device: a layer rank advances its own
+ * position when it passes x on, so its next position's kernels can read
+ * the position before their dependency wait. The kernel after a
+ * ptc_hop_recv may start while the receive still waits (it streams its
+ * weights meanwhile and reads x only after the receive completed). */
+void ptc_hop_send_next(ptc_ctx *c, const float *x, int *pos, void *peer_box, unsigned *sent, int dim);
 void ptc_hop_recv(ptc_ctx *c, const void *box, float *x, int *pos, unsigned *recvd, int dim, int *err,
                   long long timeout_ns);
 

@@ -178,6 +178,7 @@ def declare(L):
     _sig(L, "pt_dist_setup", None, dist, P(pt_shard_info_t), C.c_int, C.c_int)
     _sig(L, "pt_dist_setup_ctx", C.c_int, dist, ctx, P(pt_shard_info_t), C.c_int, C.c_int)
     _sig(L, "pt_dist_transport", C.c_int, dist)
+    _sig(L, "pt_dist_train_step_mb", pt_dist_result_t, ctx, dist, i32p, C.c_int, C.c_int, C.c_float)
     _sig(L, "pt_dist_forward_step", C.c_int, ctx, dist, C.c_int)
     _sig(L, "pt_dist_generate_greedy", C.c_int, ctx, dist, i32p, C.c_int, C.c_int, i32p)
     _sig(L, "pt_dist_train_step", pt_dist_result_t, ctx, dist, i32p, C.c_int, C.c_float)
@@ -219,6 +220,7 @@ def declare(L):
     _sig(L, "ptc_decoder_launches_per_step", C.c_int, vp)
     _sig(L, "ptc_decoder_fetch_next", C.c_int, vp, f32p)
     _sig(L, "ptc_decoder_step", C.c_int, vp, C.c_int, C.c_int, f32p)
+    _sig(L, "ptc_read_probe", None, vp, C.c_size_t, vp, vp)
     _sig(L, "ptc_mailbox_alloc", vp, vp, C.c_int)
     _sig(L, "ptc_mailbox_free", None, vp)
     _sig(L, "ptc_hop_send", None, vp, vp, vp, vp, vp, C.c_int)
@@ -390,6 +392,16 @@ class Pipeline:
                                       C.c_float(lr))
         if r.total_ms == 0:
             raise RuntimeError("pipeline train step failed")
+        return r.loss
+
+    def train_step_mb(self, tokens, n_mb, lr):
+        """GPipe step over n_mb microbatches (tokens: n_mb * T ids)."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        T = len(tokens) // n_mb
+        r = self.L.pt_dist_train_step_mb(C.byref(self.ctx.ctx), C.byref(self.dist), ip(tokens), T, n_mb,
+                                         C.c_float(lr))
+        if r.total_ms == 0:
+            raise RuntimeError("pipeline microbatch step failed")
         return r.loss
 
     def max_over_ranks(self, v):

@@ -51,7 +51,11 @@ typedef struct {
     void *peer_box;       /* the successor's mailbox, mapped */
     unsigned *ctr;        /* device [0] messages sent, [1] messages received */
     int *hop_err;         /* device: a hop wait ran out */
+    ptc_graph *stage_graph;   /* PT_DIST_GRAPH_POS device-loop positions of this rank (hops included) */
 } dist_comm_t;
+
+/* Positions per captured stage graph of the device-loop decode. */
+#define PT_DIST_GRAPH_POS 8
 
 static long now_ms(void) {
     struct timespec t;
@@ -281,6 +285,7 @@ int pt_dist_setup_ctx(pt_dist_t *dist, pt_context_t *ctx, const pt_shard_info_t 
 void pt_dist_free(pt_dist_t *dist) {
     dist_comm_t *c = comm_of(dist);
     if (!c) return;
+    if (c->stage_graph) ptc_graph_destroy(c->stage_graph);
     ptc_mailbox_close(c->peer_box);
     ptc_mailbox_free(c->box);
     if (c->comm) ncclCommDestroy(c->comm);
@@ -377,9 +382,12 @@ static void enqueue_position(pt_dist_t *dist, pt_context_t *ctx, int host_token,
             ptc_hop_recv(pc, c->box, x, NULL, c->ctr + 1, c->dim, c->hop_err, tmo);
             ptc_decoder_enqueue_head(dec);
         } else {
-            ptc_hop_recv(pc, c->box, x, pos_dev, c->ctr + 1, c->dim, c->hop_err, tmo);
+            /* the position is this rank's own (advanced by the send), so the
+             * first layer kernel, which may start while the receive waits,
+             * reads a settled value */
+            ptc_hop_recv(pc, c->box, x, NULL, c->ctr + 1, c->dim, c->hop_err, tmo);
             ptc_decoder_enqueue_layers_devpos(dec, dist->l_start, dist->l_end);
-            ptc_hop_send(pc, x, pos_dev, c->peer_box, c->ctr, c->dim);
+            ptc_hop_send_next(pc, x, pos_dev, c->peer_box, c->ctr, c->dim);
         }
         return;
     }
@@ -437,9 +445,23 @@ int pt_dist_generate_greedy(pt_context_t *ctx, pt_dist_t *dist, const int *promp
     if (!c->comm) return -1;
     ptc_decoder *dec = ctx->dev->dec;
     if (n_pos > ctx->cfg.seq_len) n_pos = ctx->cfg.seq_len;
-    ptc_decoder_reset(dec);
+    ptc_decoder_reset(dec);   /* also position 0 */
     if (dist->has_embed && dist->has_head) ptc_decoder_generate_begin(dec, prompt, n_prompt);
-    for (int p = 0; p < n_pos; p++) enqueue_position(dist, ctx, 0, 0, 1);
+    int p = 0;
+    if (c->p2p) {
+        /* Every position runs the same launches (hops included; position and
+         * token live on the device), so a captured graph of several
+         * positions replays them with one launch. NCCL hops are not
+         * captured. */
+        ptc_ctx *pc = ctx->dev->ctx;
+        if (!c->stage_graph) {
+            ptc_capture_begin(pc);
+            for (int k = 0; k < PT_DIST_GRAPH_POS; k++) enqueue_position(dist, ctx, 0, 0, 1);
+            c->stage_graph = ptc_capture_end(pc);
+        }
+        for (; p + PT_DIST_GRAPH_POS <= n_pos; p += PT_DIST_GRAPH_POS) ptc_graph_launch(c->stage_graph);
+    }
+    for (; p < n_pos; p++) enqueue_position(dist, ctx, 0, 0, 1);
     if (finish(dist, ctx, "dist generate timeout") < 0) return -1;
     if (hop_failed(dist, ctx)) return -1;
     if (dist->has_embed && dist->has_head) {
@@ -496,3 +518,139 @@ pt_dist_result_t pt_dist_train_step(pt_context_t *ctx, pt_dist_t *dist, const in
     return res;
 }
 
+/* ---- GPipe microbatched training (dev/tests/dist/train_pp/test_train_pp_mb_rank0.c,
+ *      _rank1.c: the same fill/drain order, on NCCL instead of GPIO) ---------- */
+
+/* Select microbatch set m and return its buffer of layer l's residual input. */
+static float *set_res(ptc_trainer *tr, int m, int l) {
+    ptc_trainer_select(tr, m);
+    return ptc_trainer_residual(tr, l);
+}
+static float *set_dres(ptc_trainer *tr, int m) {
+    ptc_trainer_select(tr, m);
+    return ptc_trainer_dres_save(tr);
+}
+
+pt_dist_result_t pt_dist_train_step_mb(pt_context_t *ctx, pt_dist_t *dist, const int *tokens, int T, int n_mb,
+                                       float lr) {
+    pt_dist_result_t res = {0.0f, 0};
+    if (join(dist, ctx) < 0) return res;
+    dist_comm_t *c = comm_of(dist);
+    if (!c->comm) return res;
+    ptc_trainer *tr = ctx->dev->trainer;
+    if (!tr) pt_fatal("pt_dist_train_step_mb needs a context initialised with max_T > 0");
+    if (n_mb < 1 || n_mb > 16) pt_fatal("pt_dist_train_step_mb: n_mb=%d outside [1, 16]", n_mb);
+    cudaStream_t s = stream_of(ctx);
+    const long t0 = now_ms();
+    const int M = n_mb, n_local = dist->l_end - dist->l_start;
+    const int nxt = next_rank(dist), prv = prev_rank(dist);
+    const size_t act = (size_t)T * ctx->cfg.dim, act_bytes = act * sizeof(float);
+    const int head = dist->has_embed && dist->has_head;
+    ptc_trainer_set_microbatches(tr, M);
+    ptc_trainer_zero_grads(tr);
+
+    /* forward: the head embeds microbatch m and sends it round the ring while
+     * the layer ranks work on earlier ones; each send of one microbatch is
+     * grouped with the receive of the next, so neighbours never wait on each
+     * other in opposite orders */
+    float loss_sum = 0.0f;
+    if (head) {
+        for (int m = 0; m < M; m++) {
+            ptc_trainer_select(tr, m);
+            ptc_trainer_set_tokens(tr, tokens + (size_t)m * T, T);
+            ptc_trainer_fwd_embed(tr);
+            float *out = ptc_trainer_residual(tr, 0);
+            if (m == 0) {
+                ncclSend(out, act, ncclFloat, nxt, c->comm, s);
+            } else {
+                float *in_prev = set_res(tr, m - 1, 0);   /* x after the last layer, microbatch m - 1 */
+                ncclGroupStart();
+                ncclSend(out, act, ncclFloat, nxt, c->comm, s);
+                ncclRecv(in_prev, act, ncclFloat, prv, c->comm, s);
+                ncclGroupEnd();
+            }
+        }
+        ncclRecv(set_res(tr, M - 1, 0), act, ncclFloat, prv, c->comm, s);
+        if (finish(dist, ctx, "recv fwd act") < 0) return res;
+        for (int m = 0; m < M; m++) {
+            ptc_trainer_select(tr, m);
+            loss_sum += ptc_trainer_fwd_head(tr);
+        }
+    } else {
+        for (int m = 0; m < M; m++) {
+            ptc_trainer_select(tr, m);
+            ptc_trainer_set_T(tr, T);   /* a layer rank gets rows, not tokens */
+            float *in = ptc_trainer_residual(tr, 0);
+            if (m == 0) {
+                ncclRecv(in, act, ncclFloat, prv, c->comm, s);
+            } else {
+                float *out_prev = set_res(tr, m - 1, n_local);
+                ptc_trainer_select(tr, m);
+                ncclGroupStart();
+                ncclSend(out_prev, act, ncclFloat, nxt, c->comm, s);
+                ncclRecv(in, act, ncclFloat, prv, c->comm, s);
+                ncclGroupEnd();
+            }
+            ptc_trainer_fwd_layers(tr, 0, n_local);
+        }
+        ncclSend(set_res(tr, M - 1, n_local), act, ncclFloat, nxt, c->comm, s);
+    }
+
+    /* backward, microbatches M-1 .. 0: d_res goes the other way round; every
+     * microbatch keeps its own d_res buffer while it is in flight */
+    if (head) {
+        for (int i = 0; i < M; i++) {
+            const int m = M - 1 - i;
+            ptc_trainer_select(tr, m);
+            ptc_trainer_bwd_head(tr);
+            float *d_out = ptc_trainer_dres_save(tr);
+            cudaMemcpyAsync(d_out, ptc_trainer_dres(tr), act_bytes, cudaMemcpyDeviceToDevice, s);
+            if (i == 0) {
+                ncclSend(d_out, act, ncclFloat, prv, c->comm, s);
+            } else {
+                float *d_back = set_dres(tr, m + 1);   /* microbatch m + 1 back from rank 0 */
+                ncclGroupStart();
+                ncclSend(d_out, act, ncclFloat, prv, c->comm, s);
+                ncclRecv(d_back, act, ncclFloat, nxt, c->comm, s);
+                ncclGroupEnd();
+                cudaMemcpyAsync(ptc_trainer_dres(tr), d_back, act_bytes, cudaMemcpyDeviceToDevice, s);
+                ptc_trainer_bwd_embed(tr);
+            }
+        }
+        float *d_back = set_dres(tr, 0);
+        ncclRecv(d_back, act, ncclFloat, nxt, c->comm, s);
+        cudaMemcpyAsync(ptc_trainer_dres(tr), d_back, act_bytes, cudaMemcpyDeviceToDevice, s);
+        ptc_trainer_bwd_embed(tr);
+        ptc_trainer_sgd_head(tr, lr);
+    } else {
+        for (int i = 0; i < M; i++) {
+            const int m = M - 1 - i;
+            float *d_in = set_dres(tr, m);
+            if (i == 0) {
+                ncclRecv(d_in, act, ncclFloat, nxt, c->comm, s);
+            } else {
+                float *d_prev = set_dres(tr, m + 1);
+                ptc_trainer_select(tr, m);
+                ncclGroupStart();
+                ncclSend(d_prev, act, ncclFloat, prv, c->comm, s);
+                ncclRecv(d_in, act, ncclFloat, nxt, c->comm, s);
+                ncclGroupEnd();
+            }
+            cudaMemcpyAsync(ptc_trainer_dres(tr), d_in, act_bytes, cudaMemcpyDeviceToDevice, s);
+            ptc_trainer_bwd_layers(tr, 0, n_local);
+            cudaMemcpyAsync(d_in, ptc_trainer_dres(tr), act_bytes, cudaMemcpyDeviceToDevice, s);
+        }
+        ncclSend(set_dres(tr, 0), act, ncclFloat, prv, c->comm, s);
+        ptc_trainer_sgd_layers(tr, lr, 0, n_local);
+    }
+    ptc_trainer_select(tr, 0);
+    if (finish(dist, ctx, "microbatch pipeline step") < 0) return res;
+    ptc_decoder_weights_updated(ctx->dev->dec);
+    long dt = now_ms() - t0;
+    res.total_ms = (unsigned)(dt > 0 ? dt : 1);
+    res.loss = head ? loss_sum / (float)M : 0.0f;
+    if (c->verbose)
+        printf("R%d STEP %d | %d microbatches | loss %.4f | %ums\n", dist->rank, c->step, M, res.loss, res.total_ms);
+    c->step++;
+    return res;
+}

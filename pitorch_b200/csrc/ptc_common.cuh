@@ -221,7 +221,8 @@ __device__ __forceinline__ int argmax_key_index(unsigned long long k) {
 
 // ---------------------------------------------------------------------------
 // Bulk (TMA) global->shared copies completed on an mbarrier. Only the
-// non-multicast form is used, and only on this GPU's own memory.
+// form that writes the issuing CTA's own shared memory is used, and only on
+// this GPU's own memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ unsigned smem_u32(const void *p) {
     return (unsigned)__cvta_generic_to_shared(p);

@@ -273,6 +273,8 @@ extern "C" void ptc_decoder_destroy(ptc_decoder *d) {
 }
 
 extern "C" void ptc_decoder_reset(ptc_decoder *d) {
+    // position 0 (a pipeline layer rank keeps its position on the device)
+    PTC_CHECK(cudaMemsetAsync(&d->m.step->pos, 0, sizeof(int), d->stream));
     size_t kv = (size_t)d->m.L * d->m.seq * d->m.kvd * 4;
     if (kv) {
         PTC_CHECK(cudaMemsetAsync(d->m.kc, 0, kv, d->stream));

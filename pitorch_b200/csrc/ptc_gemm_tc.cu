@@ -4,8 +4,8 @@
 // :475-492).
 //
 // CUTLASS's sm100 "FastFP32" collective (header templates, instantiated here)
-// loads fp32 tiles by TMA in the non-multicast form (cluster 1x1x1, this
-// GPU's own memory), splits each operand element into three bf16 parts in
+// loads fp32 tiles by TMA, each CTA its own (cluster 1x1x1, this GPU's own
+// memory), splits each operand element into three bf16 parts in
 // shared memory and sums all nine partial products with tcgen05.mma into
 // fp32 accumulators in tensor memory, which keeps fp32 accuracy. The epilogue is D = A.B (+ C): store, accumulate or
 // residual add; RoPE products stay on the SIMT kernel.

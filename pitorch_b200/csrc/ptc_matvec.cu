@@ -6,8 +6,11 @@
 // owns a row (or a pair of rows): its 32 lanes stream consecutive 16-byte
 // chunks of the row (fully coalesced 512-byte warp requests, L1 bypassed),
 // multiply by the lane's slice of x held in registers, and reduce with a
-// shuffle tree. Rows wider than 2048 floats, or unaligned operands, use a
-// scalar-load variant with x staged in shared memory.
+// shuffle tree -- the row's K dimension split over the 32 lanes. Matrices
+// of many narrow rows stage x in shared memory once per CTA and keep two
+// passes of rows in flight per warp (k_matvec_pf). Rows wider than 2048
+// floats, or unaligned operands, use a scalar-load variant with x staged in
+// shared memory.
 //
 // The kernel is HBM-bound at 0.5 flop/byte: algorithmic bytes per call are
 // 4 * (rows*cols + rows + cols).
@@ -69,6 +72,70 @@ __global__ void __launch_bounds__(256) k_matvec(const float *__restrict__ W, con
     }
 }
 
+// Many rows of up to 768 floats (1376 x 512, 2048 x 768, 32000 x 288): x
+// staged in shared memory once per CTA (the per-warp reads of x otherwise
+// queue at the few L2 lines that hold it), and each warp requests its next
+// R rows before it reduces the current ones (a register double buffer), so
+// two passes of rows are in flight per warp. Measured against the
+// one-warp-per-row kernel above on the same B200: 2048 x 768 2.70 -> 2.61
+// us, 1376 x 512 2.41 -> 2.30 us, 32000 x 288 10.04 -> 7.21 us per call;
+// for fewer rows, and for the 32000 x 768 classifier, the kernel above is
+// as fast or faster, and the staging's block barrier costs more than it
+// saves.
+template <int NV, int R>
+__global__ void __launch_bounds__(256) k_matvec_pf(const float *__restrict__ W, const float *__restrict__ x,
+                                                   float *__restrict__ y, int rows, int cols) {
+    pdl_trigger();
+    __shared__ __align__(16) float4 s_x[512];   // x, once per CTA (cols <= 2048)
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int gw = (blockIdx.x * blockDim.x + tid) >> 5;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    const int c4 = cols >> 2;
+    float4 w[R][NV], wn[R][NV];
+    auto load_rows = [&](float4 (&dst)[R][NV], int r0) {
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const float4 *row = reinterpret_cast<const float4 *>(W + (size_t)(r0 + k) * cols);
+#pragma unroll
+            for (int v = 0; v < NV; v++) {
+                const int c = lane + 32 * v;
+                dst[k][v] = (r0 + k < rows && c < c4) ? ldg_stream(row + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    };
+    int r0 = gw * R;
+    load_rows(w, r0);
+    pdl_wait();
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    for (int i = tid; i < c4; i += 256) cp_async16(&s_x[i], x4 + i);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    float4 xr[NV];
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const int c = lane + 32 * v;
+        xr[v] = (c < c4) ? s_x[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (; r0 < rows; r0 += nw * R) {
+        const bool more = r0 + nw * R < rows;
+        if (more) load_rows(wn, r0 + nw * R);
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            float a = 0.f;
+#pragma unroll
+            for (int v = 0; v < NV; v++) a = dot4(w[k][v], xr[v], a);
+            a = warp_sum(a);
+            if (lane == 0 && r0 + k < rows) y[r0 + k] = a;
+        }
+        if (more)
+#pragma unroll
+            for (int k = 0; k < R; k++)
+#pragma unroll
+                for (int v = 0; v < NV; v++) w[k][v] = wn[k][v];
+    }
+}
+
 // Any shape / alignment: x staged in shared memory in tiles, one warp per
 // row, scalar coalesced loads.
 __global__ void __launch_bounds__(256) k_matvec_any(const float *__restrict__ W, const float *__restrict__ x,
@@ -92,7 +159,7 @@ __global__ void __launch_bounds__(256) k_matvec_any(const float *__restrict__ W,
     if (r < rows && lane == 0) y[r] = acc;
 }
 
-template <int NV, int R>
+template <int NV, int R, bool PF>
 static void launch_k_matvec(int grid, const float *W, const float *x, float *y, int rows, int cols,
                             cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
@@ -104,15 +171,31 @@ static void launch_k_matvec(int grid, const float *W, const float *x, float *y, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    PTC_CHECK(cudaLaunchKernelEx(&cfg, k_matvec<NV, R>, W, x, y, rows, cols));
+    if constexpr (PF) PTC_CHECK(cudaLaunchKernelEx(&cfg, k_matvec_pf<NV, R>, W, x, y, rows, cols));
+    else PTC_CHECK(cudaLaunchKernelEx(&cfg, k_matvec<NV, R>, W, x, y, rows, cols));
 }
 
+// One warp per row (pair), the row's float4s spread over the lanes: for
+// every shape of the sweep this measured as fast as or faster than splitting
+// a row over 2, 4 or 8 warps with the slice sums added in shared memory
+// (288 x 768: 1.48 us one warp per row, 1.73 us over 4 warps; 288 x 288,
+// 512 x 512, 768 x 288 and 32000 x 288 slower split as well): at these
+// sizes a call is bound by its launch and one memory round trip, which a
+// split does not shorten, and the split adds two block barriers.
 #define MV_CASE(NVV)                                                                        \
     case NVV:                                                                               \
-        if (rows >= 4096)                                                                   \
-            launch_k_matvec<NVV, 2>(grid2, W, x, y, rows, cols, s);                         \
-        else                                                                                \
-            launch_k_matvec<NVV, 1>(grid1, W, x, y, rows, cols, s);                         \
+        if constexpr (NVV <= 3) {                                                           \
+            if (rows >= 4096) launch_k_matvec<NVV, 2, true>(grid2, W, x, y, rows, cols, s);  \
+            else if (rows >= 1024) launch_k_matvec<NVV, 1, true>(grid1, W, x, y, rows, cols, s); \
+            else launch_k_matvec<NVV, 1, false>(grid1, W, x, y, rows, cols, s);             \
+        } else if constexpr (NVV <= 6) {                                                    \
+            if (rows >= 4096) launch_k_matvec<NVV, 2, false>(grid2, W, x, y, rows, cols, s); \
+            else if (rows >= 1024) launch_k_matvec<NVV, 1, true>(grid1, W, x, y, rows, cols, s); \
+            else launch_k_matvec<NVV, 1, false>(grid1, W, x, y, rows, cols, s);             \
+        } else {                                                                            \
+            if (rows >= 4096) launch_k_matvec<NVV, 2, false>(grid2, W, x, y, rows, cols, s); \
+            else launch_k_matvec<NVV, 1, false>(grid1, W, x, y, rows, cols, s);             \
+        }                                                                                   \
         break;
 
 void launch_matvec(const float *W, const float *x, float *y, int rows, int cols, cudaStream_t s) {
@@ -147,10 +230,36 @@ void launch_matvec(const float *W, const float *x, float *y, int rows, int cols,
     PTC_CHECK(cudaGetLastError());
 }
 
+// Read bandwidth probe: every thread streams float4s of buf (grid-stride,
+// L2-only loads) and folds them into one value, written so the loads are
+// not removed. Over a buffer that fits in L2 and was just read, this is the
+// L2 read bandwidth; over one larger than L2, HBM.
+__global__ void __launch_bounds__(256) k_read_probe(const float4 *__restrict__ buf, size_t n4, float *sink) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += 4 * stride) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = (i + k * stride < n4) ? __ldcg(buf + i + k * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 4; k++) { a.x += v[k].x; a.y += v[k].y; a.z += v[k].z; a.w += v[k].w; }
+    }
+    const float t = a.x + a.y + a.z + a.w;
+    if (t == 123456.789f) *sink = t;   // practically never: keeps the loads live
+}
+
 }  // namespace ptc
 
 extern "C" void ptc_matvec(const float *W, const float *x, float *y, int rows, int cols, void *stream) {
     ptc::launch_matvec(W, x, y, rows, cols, (cudaStream_t)stream);
+}
+
+extern "C" void ptc_read_probe(const void *buf, size_t bytes, float *sink, void *stream) {
+    int dev = 0, n_sm = 148;
+    PTC_CHECK(cudaGetDevice(&dev));
+    PTC_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    ptc::k_read_probe<<<4 * n_sm, 256, 0, (cudaStream_t)stream>>>((const float4 *)buf, bytes / 16, sink);
+    PTC_CHECK(cudaGetLastError());
 }
 
 // ---------------------------------------------------------------------------

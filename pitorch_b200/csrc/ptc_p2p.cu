@@ -35,8 +35,11 @@ __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__global__ void k_hop_send(const float *__restrict__ x, const int *__restrict__ pos, unsigned char *peer,
-                           unsigned *sent, int dim) {
+// advance != 0: after publishing, the sender moves its own position on by
+// one (a layer rank keeps its position itself, so that the kernels of its
+// next position can read it before their dependency wait).
+__global__ void k_hop_send(const float *__restrict__ x, int *pos, unsigned char *peer, unsigned *sent, int dim,
+                           int advance) {
     MailboxHeader *h = reinterpret_cast<MailboxHeader *>(peer);
     float *px = reinterpret_cast<float *>(peer + sizeof(MailboxHeader));
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
@@ -50,11 +53,16 @@ __global__ void k_hop_send(const float *__restrict__ x, const int *__restrict__ 
         const unsigned s = *sent + 1;
         *sent = s;
         st_release_sys(&h->seq, s);
+        if (advance) *pos = *pos + 1;
     }
 }
 
+// The kernel after a receive may start at once (programmatic dependent
+// launch): it streams its weights while this one waits, and reads x only
+// after its griddepcontrol.wait, i.e. after this kernel has completed.
 __global__ void k_hop_recv(const unsigned char *box, float *__restrict__ x, int *pos, unsigned *recvd, int dim,
                            int *err, unsigned long long timeout_ns) {
+    pdl_trigger();
     const MailboxHeader *h = reinterpret_cast<const MailboxHeader *>(box);
     const float *bx = reinterpret_cast<const float *>(box + sizeof(MailboxHeader));
     __shared__ int s_ok;
@@ -123,13 +131,21 @@ extern "C" void ptc_mailbox_close(void *peer) {
 }
 
 extern "C" void ptc_hop_send(ptc_ctx *c, const float *x, const int *pos, void *peer_box, unsigned *sent, int dim) {
-    ptc::k_hop_send<<<1, 256, 0, ptc_ctx_stream(c)>>>(x, pos, (unsigned char *)peer_box, sent, dim);
+    ptc::k_hop_send<<<1, 256, 0, ptc_ctx_stream(c)>>>(x, (int *)pos, (unsigned char *)peer_box, sent, dim, 0);
+    PTC_CHECK(cudaGetLastError());
+}
+
+extern "C" void ptc_hop_send_next(ptc_ctx *c, const float *x, int *pos, void *peer_box, unsigned *sent, int dim) {
+    ptc::k_hop_send<<<1, 256, 0, ptc_ctx_stream(c)>>>(x, pos, (unsigned char *)peer_box, sent, dim, 1);
     PTC_CHECK(cudaGetLastError());
 }
 
 extern "C" void ptc_hop_recv(ptc_ctx *c, const void *box, float *x, int *pos, unsigned *recvd, int dim, int *err,
                              long long timeout_ns) {
-    ptc::k_hop_recv<<<1, 256, 0, ptc_ctx_stream(c)>>>((const unsigned char *)box, x, pos, recvd, dim, err,
-                                                      (unsigned long long)timeout_ns);
-    PTC_CHECK(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(256);
+    cfg.stream = ptc_ctx_stream(c);
+    PTC_CHECK(cudaLaunchKernelEx(&cfg, ptc::k_hop_recv, (const unsigned char *)box, x, pos, recvd, dim, err,
+                                 (unsigned long long)timeout_ns));
 }

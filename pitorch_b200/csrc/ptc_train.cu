@@ -617,6 +617,17 @@ static void load_set(ptc_trainer *tr, int i) {
     tr->loss = a.loss; tr->T = a.T;
 }
 
+// Every pass needs the selected activation set's sequence length. A set that
+// has had neither tokens nor a length (ptc_trainer_set_tokens /
+// ptc_trainer_set_T) has T = 0, and its kernels would index row T - 1 = -1:
+// refuse on the host instead. (A pipeline schedule's layer rank selecting
+// microbatch 1 without giving it a length did exactly that.)
+static void require_T(const ptc_trainer *tr, const char *pass) {
+    if (tr->T < 2 || tr->T > tr->maxT)
+        PTC_FATAL("%s on microbatch set %d with T=%d: set the tokens or the length first (max_T=%d)", pass, tr->cur,
+                  tr->T, tr->maxT);
+}
+
 static int blocks_for(size_t n, int threads, int n_sm) {
     size_t b = (n + threads - 1) / threads;
     size_t cap = (size_t)n_sm * 8;
@@ -755,7 +766,7 @@ extern "C" void ptc_trainer_set_microbatches(ptc_trainer *tr, int n) {
         a.loss_rows = A(T);
         a.loss = A(1);
         a.dres_save = A(T * D);
-        a.T = tr->T;
+        a.T = 0;   // no length until its tokens or length are set
     }
     if (n > tr->n_sets) tr->n_sets = n;
 }
@@ -810,6 +821,7 @@ extern "C" void ptc_trainer_zero_grads(ptc_trainer *tr) {
 // pt_forward_train_embed (pt_train.c:946-952)
 extern "C" void ptc_trainer_fwd_embed(ptc_trainer *tr) {
     if (!tr->has_embed) PTC_FATAL("trainer has no embedding");
+    require_T(tr, "forward embedding");
     const int n = tr->T * tr->D;
     ptc::k_tr_embed<<<blocks_for(n, 256, tr->n_sm), 256, 0, tr->s>>>(tr->res, tr->w.token_embedding,
                                                                        tr->tokens, tr->T, tr->D);
@@ -830,6 +842,8 @@ static bool attn_blocked(ptc_trainer *tr, int T) {
 }
 
 extern "C" void ptc_trainer_fwd_layers(ptc_trainer *tr, int l0, int l1) {
+    require_T(tr, "forward layers");
+    if (l0 < 0 || l1 > tr->L || l0 > l1) PTC_FATAL("layer range [%d, %d) outside [0, %d)", l0, l1, tr->L);
     const int T = tr->T, D = tr->D, H = tr->H, K = tr->K, nh = tr->nh;
     cudaStream_t s = tr->s;
     for (int l = l0; l < l1; l++) {
@@ -890,6 +904,7 @@ static void fwd_head_enqueue(ptc_trainer *tr) {
 }
 
 extern "C" float ptc_trainer_fwd_head(ptc_trainer *tr) {
+    require_T(tr, "forward head");
     fwd_head_enqueue(tr);
     PTC_CHECK(cudaStreamSynchronize(tr->s));
     return *tr->loss_host;
@@ -897,6 +912,7 @@ extern "C" float ptc_trainer_fwd_head(ptc_trainer *tr) {
 
 // pt_backward_head (pt_train.c:1103-1171)
 extern "C" void ptc_trainer_bwd_head(ptc_trainer *tr) {
+    require_T(tr, "backward head");
     const int T = tr->T, D = tr->D, V = tr->V, n = T - 1;
     cudaStream_t s = tr->s;
     PTC_CHECK(cudaMemsetAsync(tr->d_res, 0, (size_t)T * D * 4, s));
@@ -915,6 +931,8 @@ extern "C" void ptc_trainer_bwd_head(ptc_trainer *tr) {
 
 // pt_backward_layers_range (pt_train.c:1173-1377)
 extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
+    require_T(tr, "backward layers");
+    if (l0 < 0 || l1 > tr->L || l0 > l1) PTC_FATAL("layer range [%d, %d) outside [0, %d)", l0, l1, tr->L);
     const int T = tr->T, D = tr->D, H = tr->H, K = tr->K, nh = tr->nh, n = T - 1;
     cudaStream_t s = tr->s;
     for (int l = l1 - 1; l >= l0; l--) {
@@ -976,6 +994,7 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
 // pt_backward_embed (pt_train.c:1379-1383)
 extern "C" void ptc_trainer_bwd_embed(ptc_trainer *tr) {
     if (!tr->has_embed) PTC_FATAL("trainer has no embedding");
+    require_T(tr, "backward embedding");
     const int n = tr->T - 1;
     ptc::k_tr_embed_bwd<<<blocks_for((size_t)n * tr->D, 256, tr->n_sm), 256, 0, tr->s>>>(
         tr->g_emb, tr->d_res, tr->tokens, n, tr->D);

@@ -26,6 +26,11 @@ import numpy as np
 
 
 def run(args, rank, world):
+    # NCCL's communicator set-up lines ("... nRanks N ...") show how many
+    # ranks the run had; only the set-up subsystem, printed before the
+    # bench's JSON line
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     import ctypes as C
 
     import pitorch_b200
@@ -69,6 +74,10 @@ def run(args, rank, world):
     if pipe.is_head:
         same = bool(np.array_equal(toks, host_toks))
     same = pipe.max_over_ranks(0.0 if same else 1.0) == 0.0
+    # the head rank's stream against the reference's 1024-position fixture
+    par = _bench.stream_parity(toks, seq) if pipe.is_head else {}
+    matched = pipe.max_over_ranks(float(par.get("matched_positions", 0)))
+    par_ok = pipe.max_over_ranks(1.0 if par.get("equal_up_to_first_near_tie") else 0.0) == 1.0
 
     dim, hidden, nl, nh, nkv, V, _ = cfg
     # kernels per position over all ranks: the layer kernels of every layer
@@ -111,6 +120,9 @@ def run(args, rank, world):
                               "frac": step_gbs / hbm, "peak_source": f"{src} hbm_gbs",
                               "basis": "serial: each token's weights and KV stream once, stage after stage"},
             "clocks": clk.summary(),
+            "parity": {"fixture": "tests/golden/decode_stories110M_long.npz (reference host C)",
+                       "compared": "the head rank's token stream of the last timed step",
+                       "matched_positions": int(matched), "equal_up_to_first_near_tie": bool(par_ok)},
         }
         print(json.dumps(line), flush=True)
     L.ptc_timer_destroy(timer)

@@ -52,11 +52,19 @@ def _worker(rank, world, port, task, q):
             host = pipe.decode_greedy(g["prompt"], n)
             q.put((rank, pipe.is_head, dev.tolist(), host.tolist()))
             pipe.close()
-        else:
+        elif kind == "train":
             g = golden(f"train_{name}.npz")
             T = int(g["T"])
             pipe = api.Pipeline(blob, rank, world, device=rank, max_T=T)
             losses = [pipe.train_step(g["tokens"], float(g["lr"])) for _ in range(3)]
+            q.put((rank, pipe.is_head, losses, None))
+            pipe.close()
+        else:   # "train_mb": GPipe over 4 microbatches of the same tokens, lr / 4
+            g = golden(f"train_{name}.npz")
+            T, M = int(g["T"]), 4
+            pipe = api.Pipeline(blob, rank, world, device=rank, max_T=T)
+            toks = np.tile(np.asarray(g["tokens"], dtype=np.int32), M)
+            losses = [pipe.train_step_mb(toks, M, float(g["lr"]) / M) for _ in range(3)]
             q.put((rank, pipe.is_head, losses, None))
             pipe.close()
     except Exception as e:  # report instead of hanging the parent
@@ -115,3 +123,19 @@ def test_pipeline_training_matches_single_gpu(ptlib, world):
     ref = g["losses"][:3].astype(np.float64)
     assert np.all(np.abs(losses - ref) <= 1e-4 * np.abs(ref)), (losses, ref)
 
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_pipeline_microbatch_training_matches_single_gpu(ptlib, world):
+    """GPipe (pt_dist_train_step_mb, the schedule of the reference's
+    dev/tests/dist/train_pp/test_train_pp_mb_rank{0,1}.c): 4 microbatches of
+    the fixture's tokens with lr / 4 accumulate to the same update as one
+    pt_train_step with lr, so the losses of 3 steps equal the reference's
+    single-step losses within 1e-4."""
+    if n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = run_ranks(world, ("stories15M", "train_mb"))
+    g = golden("train_stories15M.npz")
+    head = [o for o in out if o[1]]
+    losses = np.array(head[0][2], dtype=np.float64)
+    ref = g["losses"][:3].astype(np.float64)
+    assert np.all(np.abs(losses - ref) <= 1e-4 * np.abs(ref)), (losses, ref)

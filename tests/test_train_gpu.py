@@ -6,6 +6,7 @@ the north star; gradients and updated weights at max|d| / max|ref| <= 1e-4
 per tensor against the oracle (pinned bitwise to the reference build).
 """
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -219,3 +220,27 @@ def test_microbatch_sets_match_accumulation(ptlib):
     got = np.array(got)
     assert np.all(np.abs(got - ref) <= 1e-4 * np.abs(ref)), (got, ref)
     assert ref[2] < ref[0]
+
+
+def test_microbatch_set_without_length_is_refused(ptlib):
+    """A microbatch set that has neither tokens nor a length has T = 0; a
+    pass on it is refused on the host with a message (its kernels would
+    index row T - 1 = -1). Checked in a child process, which aborts before
+    any kernel of the pass is launched."""
+    import subprocess
+    import sys
+    code = (
+        "import ctypes as C, pitorch_b200\n"
+        "from pitorch_b200 import api, synth\n"
+        "L = pitorch_b200.lib()\n"
+        "ctx = api.Context(synth.make_blob('tiny'), max_T=16)\n"
+        "tr = L.pt_ptc_trainer(C.byref(ctx.ctx))\n"
+        "L.ptc_trainer_set_microbatches(tr, 2)\n"
+        "L.ptc_trainer_select(tr, 1)\n"
+        "L.ptc_trainer_fwd_layers(tr, 0, 1)\n"
+        "L.ptc_trainer_sync(tr)\n"
+        "print('NOT REFUSED')\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0 and "NOT REFUSED" not in r.stdout, (r.returncode, r.stdout[-500:])
+    assert "set the tokens or the length first" in r.stderr, r.stderr[-1000:]
