@@ -87,6 +87,9 @@ pt_dist_result_t pt_dist_train_step_mb(pt_context_t *ctx, pt_dist_t *dist, const
  * gradients of ctx). Returns 0 or -1 on timeout. */
 int pt_dist_allreduce_grads_avg(pt_context_t *ctx, pt_dist_t *dist);
 
+/* Ranks in the NCCL communicator of a joined ring (ncclCommCount), or -1. */
+int pt_dist_comm_size(const pt_dist_t *dist);
+
 /* Largest value of `v` over all ranks (for max-over-ranks timing). */
 float pt_dist_max_float(pt_context_t *ctx, pt_dist_t *dist, float v);
 

@@ -178,6 +178,7 @@ def declare(L):
     _sig(L, "pt_dist_setup", None, dist, P(pt_shard_info_t), C.c_int, C.c_int)
     _sig(L, "pt_dist_setup_ctx", C.c_int, dist, ctx, P(pt_shard_info_t), C.c_int, C.c_int)
     _sig(L, "pt_dist_transport", C.c_int, dist)
+    _sig(L, "pt_dist_comm_size", C.c_int, dist)
     _sig(L, "pt_dist_train_step_mb", pt_dist_result_t, ctx, dist, i32p, C.c_int, C.c_int, C.c_float)
     _sig(L, "pt_dist_forward_step", C.c_int, ctx, dist, C.c_int)
     _sig(L, "pt_dist_generate_greedy", C.c_int, ctx, dist, i32p, C.c_int, C.c_int, i32p)

@@ -299,6 +299,13 @@ void pt_dist_set_verbose(pt_dist_t *dist, int verbose) {
 
 void pt_dist_reset_links(pt_dist_t *dist) { (void)dist; }
 
+int pt_dist_comm_size(const pt_dist_t *dist) {
+    const dist_comm_t *c = (const dist_comm_t *)dist->comm;
+    int n = -1;
+    if (!c || !c->comm || ncclCommCount(c->comm, &n) != ncclSuccess) return -1;
+    return n;
+}
+
 int pt_dist_transport(const pt_dist_t *dist) {
     const dist_comm_t *c = (const dist_comm_t *)dist->comm;
     return c ? c->p2p : -1;

@@ -76,22 +76,22 @@ __global__ void __launch_bounds__(256) k_matvec(const float *__restrict__ W, con
 // staged in shared memory once per CTA (the per-warp reads of x otherwise
 // queue at the few L2 lines that hold it), and each warp requests its next
 // R rows before it reduces the current ones (a register double buffer), so
-// two passes of rows are in flight per warp. Measured against the
-// one-warp-per-row kernel above on the same B200: 2048 x 768 2.70 -> 2.61
-// us, 1376 x 512 2.41 -> 2.30 us, 32000 x 288 10.04 -> 7.21 us per call;
-// for fewer rows, and for the 32000 x 768 classifier, the kernel above is
-// as fast or faster, and the staging's block barrier costs more than it
-// saves.
+// two passes of rows are in flight per warp. The two-row form is held to 64
+// registers so that 4 CTAs fit per SM (at 71 registers, 3: 8.2 instead of
+// 7.6 us at 32000 x 288). Measured against the one-warp-per-row kernel above
+// on the same B200: 32000 x 288 9.97 -> 7.6 us, 1376 x 512 2.30-2.40 ->
+// 2.19 us, 2048 x 768 2.62 -> 2.60 us per call; for fewer rows, and for the
+// 32000 x 768 classifier, the kernel above is as fast or faster (there the
+// staging's block barrier costs more than it saves).
 template <int NV, int R>
-__global__ void __launch_bounds__(256) k_matvec_pf(const float *__restrict__ W, const float *__restrict__ x,
+__global__ void __launch_bounds__(256, R == 2 ? 4 : 1) k_matvec_pf(const float *__restrict__ W, const float *__restrict__ x,
                                                    float *__restrict__ y, int rows, int cols) {
     pdl_trigger();
     __shared__ __align__(16) float4 s_x[512];   // x, once per CTA (cols <= 2048)
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int gw = (blockIdx.x * blockDim.x + tid) >> 5;
-    const int nw = (gridDim.x * blockDim.x) >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int c4 = cols >> 2;
-    float4 w[R][NV], wn[R][NV];
+    const int ng = gridDim.x * 8;               // warps (row groups) in the grid
+    float4 w[R][NV];
     auto load_rows = [&](float4 (&dst)[R][NV], int r0) {
 #pragma unroll
         for (int k = 0; k < R; k++) {
@@ -103,36 +103,42 @@ __global__ void __launch_bounds__(256) k_matvec_pf(const float *__restrict__ W, 
             }
         }
     };
-    int r0 = gw * R;
+    int r0 = (blockIdx.x * 8 + warp) * R;
     load_rows(w, r0);
     pdl_wait();
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    float4 xr[NV];
     for (int i = tid; i < c4; i += 256) cp_async16(&s_x[i], x4 + i);
     cp_async_commit();
     cp_async_wait_all();
     __syncthreads();
-    float4 xr[NV];
 #pragma unroll
     for (int v = 0; v < NV; v++) {
         const int c = lane + 32 * v;
         xr[v] = (c < c4) ? s_x[c] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (; r0 < rows; r0 += nw * R) {
-        const bool more = r0 + nw * R < rows;
-        if (more) load_rows(wn, r0 + nw * R);
+    // passes counted by the CTA's first row; the next pass's rows are
+    // requested before the current ones are reduced (rows past the end read
+    // as zeros)
+    for (int rb = blockIdx.x * 8 * R; rb < rows; rb += ng * R, r0 += ng * R) {
+        float4 wn[R][NV];
+        if (rb + ng * R < rows) load_rows(reinterpret_cast<float4 (&)[R][NV]>(wn), r0 + ng * R);
+        float acc[R];
 #pragma unroll
         for (int k = 0; k < R; k++) {
             float a = 0.f;
 #pragma unroll
             for (int v = 0; v < NV; v++) a = dot4(w[k][v], xr[v], a);
-            a = warp_sum(a);
-            if (lane == 0 && r0 + k < rows) y[r0 + k] = a;
+            acc[k] = warp_sum(a);
         }
-        if (more)
+        if (lane == 0)
 #pragma unroll
             for (int k = 0; k < R; k++)
+                if (r0 + k < rows) y[r0 + k] = acc[k];
 #pragma unroll
-                for (int v = 0; v < NV; v++) w[k][v] = wn[k][v];
+        for (int k = 0; k < R; k++)
+#pragma unroll
+            for (int v = 0; v < NV; v++) w[k][v] = reinterpret_cast<float4 (&)[R][NV]>(wn)[k][v];
     }
 }
 

@@ -20,6 +20,7 @@ bytes stream once, stage after stage).
 """
 import json
 import os
+import sys
 import time
 
 import numpy as np
@@ -29,8 +30,8 @@ def run(args, rank, world):
     # NCCL's communicator set-up lines ("... nRanks N ...") show how many
     # ranks the run had; only the set-up subsystem, printed before the
     # bench's JSON line
-    os.environ.setdefault("NCCL_DEBUG", "INFO")
-    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
     import ctypes as C
 
     import pitorch_b200
@@ -46,6 +47,10 @@ def run(args, rank, world):
     import bench as _bench   # the single-GPU bench's clock sampler and byte model
     pipe = api.Pipeline(blob, rank, world, device=local)
     del blob
+    # the communicator's own rank count, as NCCL reports it
+    print(f"pitorch_b200: rank {rank}: NCCL communicator with {L.pt_dist_comm_size(C.byref(pipe.dist))} ranks, "
+          f"hop transport {'NVLink peer stores' if L.pt_dist_transport(C.byref(pipe.dist)) == 1 else 'NCCL'}",
+          file=sys.stderr, flush=True)
     pc = pipe.ctx.ptc_ctx()
     timer = L.ptc_timer_create(pc)
 
