@@ -107,11 +107,12 @@ class ClockSampler:
 # capture of the 16-position bench case (positions 0-15, so the attention
 # block's KV share is that of those positions, not of the mean position):
 # dram__bytes_read.sum + dram__bytes_write.sum.
-TRAFFIC = {"attention block": 9518848, "ffn block": 18914048, "classifier": 102196000}
-TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:'k_attn_fused|k_ffn' -s 40 -c 2 "
-                  "-o k_attn_ffn_110M python bench.py --positions 16 --steps 1 --warmup 1 --no-cpu-baseline "
-                  "(profiles/k_attn_fused_k_ffn_110M.md; the attention block at a position < 16, so its "
-                  "KV bytes are those of that position)")
+TRAFFIC = {"attention block": 9518592, "ffn block": 18916608, "classifier": 102142208}
+TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:'k_attn_fused|k_ffn' -s 44 -c 2 "
+                  "-o layer python bench.py --positions 16 --steps 1 --warmup 1 --no-cpu-baseline "
+                  "(profiles/k_attn_fused_k_ffn_110M.md: layer 10 of position 1, so the attention block's "
+                  "KV bytes are those of that position; the classifier from "
+                  "profiles/k_mv_cls_110M.md)")
 
 
 def decode_bytes_per_token(cfg, pos):
