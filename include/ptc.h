@@ -180,6 +180,32 @@ int ptc_decoder_launches_per_step(ptc_decoder *d);
  * the context stream finished, 1 = still running after timeout_ms. */
 int ptc_wait_deadline(ptc_ctx *c, int timeout_ms);
 
+/* Pipeline links of a layer-range decoder (no reference counterpart: the
+ * reference passes [pos | x] between boards over GPIO, pt_dist_pipeline.c:
+ * 287-357). in_box is this rank's mailbox (ptc_mailbox_alloc; the previous
+ * stage writes it), out_box the next stage's mailbox mapped from its owner
+ * (ptc_mailbox_open), sent a device counter of the messages this rank has
+ * sent on its link (shared with ptc_hop_send), err a device error word
+ * (1: a wait ran out after timeout_ns on the GPU, 2: a message for another
+ * position) and timeout_ns the bound of each wait. With links set, the
+ * decoder captures stage graphs in which a layer rank's first attention
+ * block and the embedding+head rank's classifier take x from in_box
+ * themselves (no receive kernel), and in device-loop mode the classifier's
+ * last CTA sends the next token's embedding row to out_box (no embedding or
+ * send kernel). in_box NULL removes the links. Synchronises the decoder's
+ * stream and re-captures its graphs. */
+void ptc_decoder_set_links(ptc_decoder *d, const void *in_box, void *out_box, unsigned *sent, int *err,
+                           long long timeout_ns);
+/* Enqueue n positions of this rank's pipeline stage in link form (graphs of
+ * 8 positions, then single ones). The positions start at the device
+ * position (ptc_decoder_reset: 0); the embedding+head rank must also have
+ * begun a device-loop decode (ptc_decoder_generate_begin) and sent the first
+ * position's embedding row (ptc_hop_send); every rank enqueues the same n. */
+void ptc_decoder_enqueue_stage(ptc_decoder *d, int n);
+/* The number of positions of the device-loop decode just begun (default:
+ * seq_len): an embedding+head stage's classifier sends no input past it. */
+void ptc_decoder_set_stop(ptc_decoder *d, int n_pos);
+
 /* Weights were updated in place (training): refresh derived device copies. */
 void ptc_decoder_weights_updated(ptc_decoder *d);
 /* Phase timeline of the decode kernels (profiling; no reference
@@ -320,12 +346,9 @@ int ptc_mailbox_handle(void *box, void *handle_out);
 void *ptc_mailbox_open(ptc_ctx *c, const void *handle);  /* NULL when the peer cannot be mapped */
 void ptc_mailbox_close(void *peer);
 void ptc_hop_send(ptc_ctx *c, const float *x, const int *pos, void *peer_box, unsigned *sent, int dim);
-/* ptc_hop_send, then *pos += 1 on the device: a layer rank advances its own
- * position when it passes x on, so its next position's kernels can read
- * the position before their dependency wait. The kernel after a
- * ptc_hop_recv may start while the receive still waits (it streams its
- * weights meanwhile and reads x only after the receive completed). */
-void ptc_hop_send_next(ptc_ctx *c, const float *x, int *pos, void *peer_box, unsigned *sent, int dim);
+/* The kernel after a ptc_hop_recv may start while the receive still waits
+ * (it streams its weights meanwhile and reads x only after the receive
+ * completed). */
 void ptc_hop_recv(ptc_ctx *c, const void *box, float *x, int *pos, unsigned *recvd, int dim, int *err,
                   long long timeout_ns);
 

@@ -51,11 +51,7 @@ typedef struct {
     void *peer_box;       /* the successor's mailbox, mapped */
     unsigned *ctr;        /* device [0] messages sent, [1] messages received */
     int *hop_err;         /* device: a hop wait ran out */
-    ptc_graph *stage_graph;   /* PT_DIST_GRAPH_POS device-loop positions of this rank (hops included) */
 } dist_comm_t;
-
-/* Positions per captured stage graph of the device-loop decode. */
-#define PT_DIST_GRAPH_POS 8
 
 static long now_ms(void) {
     struct timespec t;
@@ -172,6 +168,7 @@ static void fail(const pt_dist_t *d, const char *what) {
 
 static dist_comm_t *comm_of(pt_dist_t *d) { return (dist_comm_t *)d->comm; }
 static int finish(pt_dist_t *dist, pt_context_t *ctx, const char *what);
+static long long hop_timeout_ns(const pt_dist_t *dist);
 static int next_rank(const pt_dist_t *d) { return (d->rank + 1) % d->world_size; }
 static int prev_rank(const pt_dist_t *d) { return (d->rank + d->world_size - 1) % d->world_size; }
 
@@ -216,10 +213,22 @@ static int setup_p2p(pt_dist_t *dist, pt_context_t *ctx) {
     cudaMemsetAsync(c->ctr, 0, 2 * sizeof(unsigned), s);
     cudaMemsetAsync(c->hop_err, 0, sizeof(int), s);
     c->p2p = 1;
-    return finish(dist, ctx, "mailbox setup timeout");
+    if (finish(dist, ctx, "mailbox setup timeout") < 0) return -1;
+    /* the decoder takes its input from the mailbox and sends its output
+     * itself: no receive kernels, and on the head rank no embedding or send
+     * kernel per position */
+    ptc_decoder_set_links(ctx->dev->dec, c->box, c->peer_box, c->ctr, c->hop_err, hop_timeout_ns(dist));
+    return 0;
 }
 
 /* A decode hop wait that ran out on the GPU (after the stream finished). */
+static long long hop_timeout_ns(const pt_dist_t *dist) {
+    /* the GPU-side bound of one wait: the dist timeout, at most 60 s (the
+     * host's deadline still bounds the whole call) */
+    const int ms = timeout_of(dist) < 60000 ? timeout_of(dist) : 60000;
+    return (long long)ms * 1000000LL;
+}
+
 static int hop_failed(pt_dist_t *dist, pt_context_t *ctx) {
     dist_comm_t *c = comm_of(dist);
     if (!c->p2p) return 0;
@@ -285,7 +294,6 @@ int pt_dist_setup_ctx(pt_dist_t *dist, pt_context_t *ctx, const pt_shard_info_t 
 void pt_dist_free(pt_dist_t *dist) {
     dist_comm_t *c = comm_of(dist);
     if (!c) return;
-    if (c->stage_graph) ptc_graph_destroy(c->stage_graph);
     ptc_mailbox_close(c->peer_box);
     ptc_mailbox_free(c->box);
     if (c->comm) ncclCommDestroy(c->comm);
@@ -374,28 +382,17 @@ static void enqueue_position(pt_dist_t *dist, pt_context_t *ctx, int host_token,
     float *x = ptc_decoder_x_dev(dec);
     int *pos_dev = ptc_decoder_pos_dev(dec);
     if (c->p2p) {
-        ptc_ctx *pc = ctx->dev->ctx;
-        /* GPU-side bound of one hop wait: the dist timeout, at most 60 s (the
-         * host's deadline still bounds the whole call) */
-        const long long tmo = (long long)(timeout_of(dist) < 60000 ? timeout_of(dist) : 60000) * 1000000LL;
+        /* link form: the decoder's stage graph of one position (its first
+         * kernel waits for this rank's mailbox; a layer rank's last one
+         * sends on). The head rank first sends the position's embedding row
+         * itself: in host-driven steps the token is the caller's. */
+        (void)devloop;
         if (dist->has_embed && dist->has_head) {
-            if (devloop) {
-                ptc_decoder_enqueue_embed_dev(dec);
-            } else {
-                cudaMemcpyAsync(pos_dev, &host_pos, 4, cudaMemcpyHostToDevice, s);
-                ptc_decoder_enqueue_embed(dec, host_token);
-            }
-            ptc_hop_send(pc, x, pos_dev, c->peer_box, c->ctr, c->dim);
-            ptc_hop_recv(pc, c->box, x, NULL, c->ctr + 1, c->dim, c->hop_err, tmo);
-            ptc_decoder_enqueue_head(dec);
-        } else {
-            /* the position is this rank's own (advanced by the send), so the
-             * first layer kernel, which may start while the receive waits,
-             * reads a settled value */
-            ptc_hop_recv(pc, c->box, x, NULL, c->ctr + 1, c->dim, c->hop_err, tmo);
-            ptc_decoder_enqueue_layers_devpos(dec, dist->l_start, dist->l_end);
-            ptc_hop_send_next(pc, x, pos_dev, c->peer_box, c->ctr, c->dim);
+            cudaMemcpyAsync(pos_dev, &host_pos, 4, cudaMemcpyHostToDevice, s);
+            ptc_decoder_enqueue_embed(dec, host_token);
+            ptc_hop_send(ctx->dev->ctx, x, pos_dev, c->peer_box, c->ctr, c->dim);
         }
+        ptc_decoder_enqueue_stage(dec, 1);
         return;
     }
     if (dist->has_embed && dist->has_head) {
@@ -454,21 +451,20 @@ int pt_dist_generate_greedy(pt_context_t *ctx, pt_dist_t *dist, const int *promp
     if (n_pos > ctx->cfg.seq_len) n_pos = ctx->cfg.seq_len;
     ptc_decoder_reset(dec);   /* also position 0 */
     if (dist->has_embed && dist->has_head) ptc_decoder_generate_begin(dec, prompt, n_prompt);
-    int p = 0;
     if (c->p2p) {
-        /* Every position runs the same launches (hops included; position and
-         * token live on the device), so a captured graph of several
-         * positions replays them with one launch. NCCL hops are not
-         * captured. */
-        ptc_ctx *pc = ctx->dev->ctx;
-        if (!c->stage_graph) {
-            ptc_capture_begin(pc);
-            for (int k = 0; k < PT_DIST_GRAPH_POS; k++) enqueue_position(dist, ctx, 0, 0, 1);
-            c->stage_graph = ptc_capture_end(pc);
+        /* Link form: the head rank sends position 0's embedding row; from
+         * then on every position's input travels inside the decode kernels
+         * (the classifier sends the next embedding row, the layer ranks
+         * send their outputs), replayed from the decoders' stage graphs. */
+        if (dist->has_embed && dist->has_head) {
+            ptc_decoder_set_stop(dec, n_pos);
+            const float *row = ctx->dev->dw.token_embedding + (size_t)prompt[0] * ctx->cfg.dim;
+            ptc_hop_send(ctx->dev->ctx, row, ptc_decoder_pos_dev(dec), c->peer_box, c->ctr, c->dim);
         }
-        for (; p + PT_DIST_GRAPH_POS <= n_pos; p += PT_DIST_GRAPH_POS) ptc_graph_launch(c->stage_graph);
+        ptc_decoder_enqueue_stage(dec, n_pos);
+    } else {
+        for (int p = 0; p < n_pos; p++) enqueue_position(dist, ctx, 0, 0, 1);
     }
-    for (; p < n_pos; p++) enqueue_position(dist, ctx, 0, 0, 1);
     if (finish(dist, ctx, "dist generate timeout") < 0) return -1;
     if (hop_failed(dist, ctx)) return -1;
     if (dist->has_embed && dist->has_head) {

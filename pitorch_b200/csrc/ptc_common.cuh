@@ -203,6 +203,25 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 
+// A pipeline link's mailbox in the receiving rank's memory: the message of
+// one position ([pos | x], pitorch/dist/pt_dist_pipeline.c:287-302) and the
+// number of messages delivered so far, published last with release
+// semantics at system scope.
+struct MailboxHeader {
+    int pos;
+    unsigned seq;   // messages delivered into this mailbox
+    int pad[2];     // x starts 16-byte aligned
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Order-preserving map of a float to uint32 (larger float -> larger key).
 __device__ __forceinline__ uint32_t float_key(float f) {
     uint32_t u = __float_as_uint(f);

@@ -20,6 +20,12 @@ struct StepState {
     unsigned pad1;
     unsigned long long amax;  // packed (value, index) running argmax
     int *tokens;              // device-loop mode: token stream [seq]
+    int stop;                 // device-loop mode: positions of this decode (the last is stop - 1)
+    // Pipeline stage: messages taken from this rank's mailbox so far (the
+    // sender's count of the same link). Kept across decodes: the fields
+    // above it are rewritten when a decode begins, this one never.
+    unsigned recvd;
+    unsigned pad2;
 };
 
 // Everything the decode kernels need for one model replica.
@@ -70,6 +76,18 @@ struct DecodeModel {
     // earliest and the latest %globaltimer over the kernel's CTAs at
     // trace[2 * (((p % TRACE_POS) * (2L + 1) + k) * TRACE_EV + e)] (+1).
     unsigned long long *trace;
+    // Pipeline links (ptc_decoder_set_links; null on a single GPU). While
+    // link_mode is set (the decoder's stage graphs), the first layer's
+    // attention block -- or, on the embedding+head rank, the classifier --
+    // takes x from in_box, waiting on the GPU for the message of its
+    // position; in device-loop mode the classifier's last CTA sends the next
+    // token's embedding row to out_box itself.
+    const unsigned char *in_box;   // this rank's mailbox (MailboxHeader, then x)
+    unsigned char *out_box;        // the next stage's mailbox (peer memory)
+    unsigned *link_sent;           // messages this rank has sent on its out link
+    int *link_err;                 // 1: a mailbox wait expired, 2: a message for another position
+    unsigned long long link_timeout_ns;
+    int link_mode;
 };
 
 constexpr int TRACE_POS = 16;

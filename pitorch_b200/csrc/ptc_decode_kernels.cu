@@ -146,6 +146,37 @@ __device__ __forceinline__ void vec_from_smem(float4 (&x)[NV], const float4 *s_x
     }
 }
 
+// The same from a pipeline mailbox, written by another GPU: volatile loads.
+__device__ __forceinline__ void stage_vec_cv(float4 *s_x4, const float *src, int c4) {
+    const float4 *src4 = reinterpret_cast<const float4 *>(src);
+    for (int i = threadIdx.x; i < c4; i += blockDim.x) s_x4[i] = __ldcv(src4 + i);
+}
+
+// Thread 0 of a CTA: wait for the message `want` (the link's message count)
+// of position `pos` in this rank's mailbox, polling its sequence word with
+// acquire semantics and giving up after m.link_timeout_ns of %globaltimer.
+// After an expired wait, or a message for another position, the link error
+// word is set (the host turns it into the reference's -1) and later waits on
+// the broken link return at once; the kernel then computes on whatever the
+// mailbox holds, and reaches all of its barriers.
+__device__ __forceinline__ void link_poll(const DecodeModel &m, unsigned want, int pos) {
+    const MailboxHeader *h = reinterpret_cast<const MailboxHeader *>(m.in_box);
+    if (*reinterpret_cast<volatile int *>(m.link_err)) return;
+    const unsigned long long t0 = globaltimer_ns();
+    while ((int)(ld_acquire_sys(&h->seq) - want) < 0) {
+        if (globaltimer_ns() - t0 > m.link_timeout_ns) {
+            atomicExch(m.link_err, 1);
+            return;
+        }
+        __nanosleep(64);
+    }
+    if (__ldcv(&h->pos) != pos) atomicExch(m.link_err, 2);
+}
+
+__device__ __forceinline__ const float *mailbox_x(const unsigned char *box) {
+    return reinterpret_cast<const float *>(box + sizeof(MailboxHeader));
+}
+
 // Bytes of the shared-memory copy of an n-float vector (128-byte multiple).
 __host__ __device__ constexpr int vec_smem_bytes(int n) { return (n * 4 + 127) / 128 * 128; }
 
@@ -415,6 +446,8 @@ struct MvArgs {
     int l;             // layer
     int from_embedding;
     int *host_next;    // MV_CLS: pinned host word that also receives the argmax (null: none)
+    int recv;          // MV_CLS: x from this rank's mailbox (pipeline head rank)
+    int send_next;     // MV_CLS, device loop: the next token's embedding row to the next stage
 };
 
 template <int MODE>
@@ -496,7 +529,10 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     float4 xr[NV], gr[NV];
     int pos = 0;
     constexpr bool tr = MODE == MV_CLS && TR;
-    const int tpos = tr ? __ldcg(&m.step->pos) + m.tok_off : 0;
+    const int tpos = (tr || (MODE == MV_CLS && a.recv)) ? __ldcg(&m.step->pos) + m.tok_off : 0;
+    // the link's message for this position (read before the wait: only the
+    // last kernel of a graph moves the count on)
+    const unsigned want = (MODE == MV_CLS && a.recv) ? __ldcg(&m.step->recvd) + m.tok_off + 1 : 0u;
     trace_ev(m, tr, tpos, 2 * m.L, 0);
     const bool early = MODE == MV_QKV && a.from_embedding && m.tok_off == 0;
     if (MODE == MV_QKV) {
@@ -521,7 +557,18 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         }
     }
     if (MODE == MV_CLS) {
-        load_act<NV>(xr, m.x, c4, lane);
+        if (a.recv) {   // pipeline head rank: x is the last layer rank's message
+            if (tid == 0) link_poll(m, want, tpos);
+            __syncthreads();
+            const float4 *b4 = reinterpret_cast<const float4 *>(mailbox_x(m.in_box));
+#pragma unroll
+            for (int v = 0; v < NV; v++) {
+                const int c = lane + 32 * v;
+                xr[v] = (c < c4) ? __ldcv(b4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        } else {
+            load_act<NV>(xr, m.x, c4, lane);
+        }
     } else {
         if (!early) {
             const float *src = a.in;
@@ -659,29 +706,86 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         s_last = (ticket == gridDim.x - 1);
     }
     __syncthreads();
-    if (!s_last || tid != 0) return;
-    const unsigned long long key = __ldcg(&st->amax);
-    const int next = argmax_key_index(key);
-    st->next = next;
-    if (a.host_next) {   // straight into the host's pinned word: no copy node after the kernel
-        // -1 sends the host to the error word, so a token computed after an
-        // expired wait is never returned as valid
-        *reinterpret_cast<volatile int *>(a.host_next) = err_seen ? -1 : next;
+    if (!s_last) return;
+    __shared__ int s_send_tok, s_send_pos;
+    if (tid == 0) {
+        const unsigned long long key = __ldcg(&st->amax);
+        const int next = argmax_key_index(key);
+        st->next = next;
+        if (a.host_next) {   // straight into the host's pinned word: no copy node after the kernel
+            // -1 sends the host to the error word, so a token computed after an
+            // expired wait is never returned as valid
+            *reinterpret_cast<volatile int *>(a.host_next) = err_seen ? -1 : next;
+        }
+        st->amax = 0ull;
+        st->done = 0u;
+        const int p = st->pos + m.tok_off;
+        int send_tok = -1;
+        if (st->mode == 1 && p < m.seq) {
+            int t = next;
+            if (p + 1 < st->n_prompt) t = st->tokens[p + 1];
+            else st->tokens[p + 1] = next;
+            st->tok = t;
+            if (m.adv) st->pos = p + 1;
+            if (a.send_next && p + 1 < st->stop) send_tok = t;
+        }
+        if (a.recv && m.adv) st->recvd = st->recvd + m.tok_off + 1;
+        s_send_tok = send_tok;
+        s_send_pos = p + 1;
     }
-    st->amax = 0ull;
-    st->done = 0u;
-    const int p = st->pos + m.tok_off;
-    if (st->mode == 1 && p < m.seq) {
-        int t = next;
-        if (p + 1 < st->n_prompt) t = st->tokens[p + 1];
-        else st->tokens[p + 1] = next;
-        st->tok = t;
-        if (m.adv) st->pos = p + 1;
+    __syncthreads();
+    if (s_send_tok >= 0) {
+        // Pipeline head rank: the next position's input -- the embedding row
+        // of the token just chosen -- goes straight into the first layer
+        // rank's mailbox (peer stores over NVLink), published after a
+        // system-scope fence; no embedding or send kernel follows.
+        MailboxHeader *oh = reinterpret_cast<MailboxHeader *>(m.out_box);
+        float4 *ox = reinterpret_cast<float4 *>(m.out_box + sizeof(MailboxHeader));
+        const float4 *er = reinterpret_cast<const float4 *>(m.emb + (size_t)s_send_tok * m.dim);
+        for (int i = tid; i < c4; i += MV_THREADS) ox[i] = __ldg(er + i);
+        if (tid == 0) oh->pos = s_send_pos;
+        __threadfence_system();
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned sq = *m.link_sent + 1;
+            *m.link_sent = sq;
+            st_release_sys(&oh->seq, sq);
+        }
     }
-    // no fence: the next kernel reads these after griddepcontrol.wait, and
-    // the host after the stream synchronises -- both see a completed grid's
-    // writes
+    // no fence for the step state: the next kernel reads it after
+    // griddepcontrol.wait, and the host after the stream synchronises --
+    // both see a completed grid's writes
     trace_ev(m, tr, tpos, 2 * m.L, 7);
+}
+
+// A pipeline layer rank's output: x (m.x, complete -- this kernel is
+// launched without programmatic overlap, after the last layer's kernels)
+// into the next stage's mailbox with peer stores, published after a
+// system-scope fence. The last position of a stage graph (adv) then moves
+// the rank's own position and message count on.
+__global__ void k_stage_send(DecodeModel m) {
+    const int pos = __ldcg(&m.step->pos) + m.tok_off;
+    MailboxHeader *oh = reinterpret_cast<MailboxHeader *>(m.out_box);
+    float4 *ox = reinterpret_cast<float4 *>(m.out_box + sizeof(MailboxHeader));
+    const float4 *x4 = reinterpret_cast<const float4 *>(m.x);
+    for (int i = threadIdx.x; i < m.dim / 4; i += blockDim.x) ox[i] = __ldcg(x4 + i);
+    if (threadIdx.x == 0) oh->pos = pos;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned sq = *m.link_sent + 1;
+        *m.link_sent = sq;
+        st_release_sys(&oh->seq, sq);
+        if (m.adv) {
+            m.step->pos = pos + 1;
+            m.step->recvd = m.step->recvd + m.tok_off + 1;
+        }
+    }
+}
+
+void launch_stage_send(const DecodeModel &m, cudaStream_t s) {
+    k_stage_send<<<1, 256, 0, s>>>(m);
+    PTC_CHECK(cudaGetLastError());
 }
 
 // ---------------------------------------------------------------------------
@@ -850,6 +954,7 @@ struct AttnArgs {
     float *xclear;     // cleared once every CTA has read the input
     int l;
     int stage_floats;  // shared staging region (q/k/v rows, then wo slice + value sums)
+    int recv;          // x from this rank's mailbox (a pipeline layer rank's first layer)
 };
 
 template <int NV, bool TR>
@@ -886,6 +991,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     if (!pos_ok) flag_pos_range(m);
     constexpr bool tr = TR;
     trace_ev(m, tr, pos, 2 * l, 0);
+    // the link's message for this position (read before the wait: only the
+    // last kernel of a graph moves the count on)
+    const unsigned want = a.recv ? __ldcg(&m.step->recvd) + m.tok_off + 1 : 0u;
     // positions of this CTA: [t0, t1) of [0, pos]
     const int ppc = (pos + AC) / AC;
     const int t0 = min(r * ppc, pos + 1), t1 = min(t0 + ppc, pos + 1);
@@ -963,8 +1071,14 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
     pdl_wait();
     trace_ev(m, tr, pos, 2 * l, 1);
-    if (!a.xin && m.tok_off != 0) xsrc = m.emb + (size_t)__ldcg(&m.step->tok) * dim;
-    if (a.xin || m.tok_off != 0) stage_vec(s_x4, xsrc, c4);
+    if (a.recv) {   // pipeline layer rank: x is the previous stage's message
+        if (tid == 0) link_poll(m, want, pos);
+        __syncthreads();
+        stage_vec_cv(s_x4, mailbox_x(m.in_box), c4);
+    } else {
+        if (!a.xin && m.tok_off != 0) xsrc = m.emb + (size_t)__ldcg(&m.step->tok) * dim;
+        if (a.xin || m.tok_off != 0) stage_vec(s_x4, xsrc, c4);
+    }
     __syncthreads();
     vec_from_smem<NV>(xr, s_x4, c4, lane);
     if (h == 0)
@@ -1365,7 +1479,7 @@ int decode_ffn_rows(int dim, int hidden, int n_sm) {
 // Fused FFN: wo writes xm = x_in + wo.att and clears x_in behind it, k_ffn
 // accumulates xm + w2.hb into x_out, which is zero on entry.
 static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float *x_in, float *x_out, int n_sm,
-                         cudaStream_t s) {
+                         cudaStream_t s, bool recv = false) {
     const int nvd = nv_of(m.dim), nvh = nv_of(m.hidden);
     if (m.fused_attn) {
         // two kernels: attention block -> xm, FFN block -> x_out; each clears
@@ -1376,6 +1490,7 @@ static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float
         at.xout = m.xm;
         at.xclear = x_in;
         at.l = l;
+        at.recv = recv ? 1 : 0;
         PTC_NV_SWITCH(nvd, (launch_attn_fused<NV>(m, at, s)));
         FfnArgs f;
         f.xin = m.xm;
@@ -1385,6 +1500,7 @@ static void launch_layer(const DecodeModel &m, int l, bool from_embedding, float
         PTC_NV_SWITCH(nvd, (launch_ffn<NV>(m, f, n_sm, s)));
         return;
     }
+    if (recv) PTC_FATAL("pipeline links need the fused attention block (PTC_DECODE_FUSED unset)");
     MvArgs a = mv_args((m.dim + 2 * m.kvd) / 2, m.dim, 2, l);
     a.from_embedding = from_embedding ? 1 : 0;
     a.in = x_in;
@@ -1463,7 +1579,7 @@ void launch_layers(const DecodeModel &m, int l0, int l1, bool from_embedding, in
             x_in = (l == l0) ? m.x : m.xo + (size_t)(l - 1) * m.dim;
             x_out = (l == l1 - 1) ? m.x : m.xo + (size_t)l * m.dim;
         }
-        launch_layer(m, l, from_embedding && l == 0, x_in, x_out, n_sm, s);
+        launch_layer(m, l, from_embedding && l == 0, x_in, x_out, n_sm, s, m.link_mode && l == l0);
     }
 }
 
@@ -1471,6 +1587,8 @@ void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s, int *host_next)
     MvArgs a = mv_args(m.V, m.dim, 1, 0);
     a.W = m.wcls;
     a.host_next = host_next;
+    a.recv = m.link_mode ? 1 : 0;
+    a.send_next = m.link_mode ? 1 : 0;
     PTC_NV_SWITCH(nv_of(m.dim), (launch_mv<NV, MV_CLS>(m, a, n_sm, s)));
 }
 

@@ -9,6 +9,7 @@
 //   device graphs:  kernels only, for one position and for DEV_TOKENS
 //                   positions; position and token advance on the device, so
 //                   a whole greedy decode is a chain of graph launches.
+#include <stddef.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -40,7 +41,44 @@ struct ptc_decoder {
     cudaGraphExec_t g_devk;  // DEV_TOKENS device-loop tokens per launch (null: not used)
     unsigned long long *trace_buf;  // phase timeline record (m.trace while tracing)
     size_t trace_n;        // its entries
+    // pipeline stage graphs (ptc_decoder_set_links): STAGE_POS positions and one
+    cudaGraphExec_t g_stage, g_stage1;
 };
+
+// Positions per captured pipeline stage graph.
+constexpr int STAGE_POS = 8;
+
+// The kernels of `n` positions of this rank's pipeline stage, in link form:
+// a layer rank's layers (the first attention block waits for its mailbox)
+// and the send of its output; the embedding+head rank's classifier (waits for
+// its mailbox, sends the next embedding row). The k-th position decodes
+// step->pos + k and expects message step->recvd + k + 1; only the last one
+// moves both on.
+static void enqueue_stage_kernels(ptc_decoder *d, int n, cudaStream_t s) {
+    for (int k = 0; k < n; k++) {
+        DecodeModel mk = d->m;
+        mk.link_mode = 1;
+        mk.tok_off = k;
+        mk.adv = k == n - 1;
+        if (mk.L > 0) {
+            ptc::launch_layers(mk, 0, mk.L, false, d->n_sm, s);
+            ptc::launch_stage_send(mk, s);
+        } else {
+            ptc::launch_head(mk, d->n_sm, s);
+        }
+    }
+}
+
+static cudaGraphExec_t capture_stage(ptc_decoder *d, int n) {
+    cudaGraph_t g;
+    PTC_CHECK(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal));
+    enqueue_stage_kernels(d, n, d->stream);
+    PTC_CHECK(cudaStreamEndCapture(d->stream, &g));
+    cudaGraphExec_t ge;
+    PTC_CHECK(cudaGraphInstantiate(&ge, g, 0));
+    PTC_CHECK(cudaGraphDestroy(g));
+    return ge;
+}
 
 static void enqueue_kernels(ptc_decoder *d, const DecodeModel &m, cudaStream_t s, int *host_next) {
     if (d->has_embed && m.L == 0) ptc::launch_embed(m, s);
@@ -76,6 +114,13 @@ static void capture_graphs(ptc_decoder *d) {
     if (d->g_host) PTC_CHECK(cudaGraphExecDestroy(d->g_host));
     if (d->g_dev) PTC_CHECK(cudaGraphExecDestroy(d->g_dev));
     if (d->g_devk) PTC_CHECK(cudaGraphExecDestroy(d->g_devk));
+    if (d->g_stage) PTC_CHECK(cudaGraphExecDestroy(d->g_stage));
+    if (d->g_stage1) PTC_CHECK(cudaGraphExecDestroy(d->g_stage1));
+    d->g_stage = d->g_stage1 = nullptr;
+    if (d->m.in_box) {   // a pipeline stage: its link-form graphs
+        d->g_stage = capture_stage(d, STAGE_POS);
+        d->g_stage1 = capture_stage(d, 1);
+    }
     d->g_host = capture(d, true);
     d->g_dev = capture(d, false);
     d->g_devk = nullptr;
@@ -224,6 +269,7 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     d->stage = (float *)ptc_host_alloc(stage);
 
     d->g_host = d->g_dev = d->g_devk = nullptr;
+    d->g_stage = d->g_stage1 = nullptr;
     capture_graphs(d);
 
     return d;
@@ -267,6 +313,8 @@ extern "C" void ptc_decoder_destroy(ptc_decoder *d) {
     cudaGraphExecDestroy(d->g_host);
     cudaGraphExecDestroy(d->g_dev);
     if (d->g_devk) cudaGraphExecDestroy(d->g_devk);
+    if (d->g_stage) cudaGraphExecDestroy(d->g_stage);
+    if (d->g_stage1) cudaGraphExecDestroy(d->g_stage1);
     ptc_host_free(d->io);
     ptc_host_free(d->stage);
     delete d;  // device buffers belong to the context arena
@@ -342,7 +390,9 @@ extern "C" void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, in
     st.n_prompt = n_prompt;
     st.mode = 1;
     st.tokens = d->d_tokens;
-    PTC_CHECK(cudaMemcpyAsync(d->m.step, &st, sizeof(st), cudaMemcpyHostToDevice, d->stream));
+    st.stop = d->m.seq;
+    // everything before the link's message count, which outlives decodes
+    PTC_CHECK(cudaMemcpyAsync(d->m.step, &st, offsetof(StepState, recvd), cudaMemcpyHostToDevice, d->stream));
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     d->mode = 1;
 }
@@ -442,4 +492,33 @@ extern "C" int ptc_decoder_launches_per_step(ptc_decoder *d) {
 extern "C" void ptc_decoder_enqueue_embed_dev(ptc_decoder *d) {
     if (!d->has_embed) PTC_FATAL("decoder has no embedding");
     ptc::launch_embed(d->m, d->stream);
+}
+
+extern "C" void ptc_decoder_set_links(ptc_decoder *d, const void *in_box, void *out_box, unsigned *sent, int *err,
+                                      long long timeout_ns) {
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    if (in_box && (!out_box || !sent || !err)) PTC_FATAL("pipeline links need out_box, sent and err");
+    if (in_box && d->m.L > 0 && !d->m.fused_attn)
+        PTC_FATAL("pipeline links need the fused attention block (two kernels per layer)");
+    if (in_box && d->m.L == 0 && !(d->has_embed && d->has_head))
+        PTC_FATAL("a pipeline stage without layers must hold the embedding and the classifier");
+    d->m.in_box = (const unsigned char *)in_box;
+    d->m.out_box = (unsigned char *)out_box;
+    d->m.link_sent = sent;
+    d->m.link_err = err;
+    d->m.link_timeout_ns = (unsigned long long)(timeout_ns > 0 ? timeout_ns : 0);
+    capture_graphs(d);
+}
+
+extern "C" void ptc_decoder_set_stop(ptc_decoder *d, int n_pos) {
+    if (n_pos < 1 || n_pos > d->m.seq) PTC_FATAL("decode length %d outside [1, %d]", n_pos, d->m.seq);
+    PTC_CHECK(cudaMemcpyAsync(&d->m.step->stop, &n_pos, sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+}
+
+extern "C" void ptc_decoder_enqueue_stage(ptc_decoder *d, int n) {
+    if (!d->m.in_box) PTC_FATAL("ptc_decoder_enqueue_stage without pipeline links");
+    int i = 0;
+    for (; i + STAGE_POS <= n; i += STAGE_POS) PTC_CHECK(cudaGraphLaunch(d->g_stage, d->stream));
+    for (; i < n; i++) PTC_CHECK(cudaGraphLaunch(d->g_stage1, d->stream));
 }

@@ -34,6 +34,8 @@ void transpose_w2(const DecodeModel &m, float *w2t, cudaStream_t s);
 // host_next: pinned host word that also receives the argmax (or null).
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s, int *host_next = nullptr);
 void launch_embed(const DecodeModel &m, cudaStream_t s);
+// A pipeline layer rank's output x into the next stage's mailbox.
+void launch_stage_send(const DecodeModel &m, cudaStream_t s);
 int decode_attn_limits_ok(int hd, int chunk, int n_chunks);
 void launch_matvec(const float *W, const float *x, float *y, int rows, int cols, cudaStream_t s);
 }  // namespace ptc

@@ -18,28 +18,10 @@
 
 namespace ptc {
 
-struct MailboxHeader {
-    int pos;
-    unsigned seq;   // number of messages delivered into this mailbox
-    int pad[2];     // x starts 16-byte aligned
-};
-
 static size_t mailbox_bytes(int dim) { return sizeof(MailboxHeader) + (size_t)dim * 4; }
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// advance != 0: after publishing, the sender moves its own position on by
-// one (a layer rank keeps its position itself, so that the kernels of its
-// next position can read it before their dependency wait).
-__global__ void k_hop_send(const float *__restrict__ x, int *pos, unsigned char *peer, unsigned *sent, int dim,
-                           int advance) {
+__global__ void k_hop_send(const float *__restrict__ x, const int *__restrict__ pos, unsigned char *peer,
+                           unsigned *sent, int dim) {
     MailboxHeader *h = reinterpret_cast<MailboxHeader *>(peer);
     float *px = reinterpret_cast<float *>(peer + sizeof(MailboxHeader));
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
@@ -53,7 +35,6 @@ __global__ void k_hop_send(const float *__restrict__ x, int *pos, unsigned char 
         const unsigned s = *sent + 1;
         *sent = s;
         st_release_sys(&h->seq, s);
-        if (advance) *pos = *pos + 1;
     }
 }
 
@@ -131,12 +112,7 @@ extern "C" void ptc_mailbox_close(void *peer) {
 }
 
 extern "C" void ptc_hop_send(ptc_ctx *c, const float *x, const int *pos, void *peer_box, unsigned *sent, int dim) {
-    ptc::k_hop_send<<<1, 256, 0, ptc_ctx_stream(c)>>>(x, (int *)pos, (unsigned char *)peer_box, sent, dim, 0);
-    PTC_CHECK(cudaGetLastError());
-}
-
-extern "C" void ptc_hop_send_next(ptc_ctx *c, const float *x, int *pos, void *peer_box, unsigned *sent, int dim) {
-    ptc::k_hop_send<<<1, 256, 0, ptc_ctx_stream(c)>>>(x, pos, (unsigned char *)peer_box, sent, dim, 1);
+    ptc::k_hop_send<<<1, 256, 0, ptc_ctx_stream(c)>>>(x, pos, (unsigned char *)peer_box, sent, dim);
     PTC_CHECK(cudaGetLastError());
 }
 
