@@ -358,11 +358,14 @@ def run_single(args):
 
 
 ATTN_PHASES = [("release after the previous kernel's end", None, 1),
-               ("x read + rmsnorm", 1, 2), ("q/k/v rows resident", 2, 3), ("q/k/v exchange (cluster)", 3, 4),
+               ("x read + rmsnorm", 1, 2), ("q/k/v rows resident", 2, 3),
+               ("q/k/v row pairs + RoPE + stores to the cluster", 3, 8),
+               ("ticket + wo / K/V copy issue", 8, 9), ("q/k/v cluster barrier wait", 9, 4),
                ("attention rounds", 4, 5), ("partial exchange (cluster)", 5, 6),
-               ("merge + wo rows + reductions", 6, 7)]
+               ("merge of the partials", 6, 10), ("wo slice resident", 10, 11),
+               ("wo rows + reductions", 11, 7)]
 FFN_PHASES = [("release after the previous kernel's end", None, 1), ("x read + rmsnorm", 1, 2),
-              ("w1/w3 rows resident", 2, 3), ("silu(h1)*h3 + w2t rows resident", 3, 4),
+              ("w1/w3 rows resident", 2, 3), ("h1, h3 rows + silu", 3, 8), ("w2t rows resident", 8, 4),
               ("w2t product + reductions", 4, 7)]
 CLS_PHASES = [("release after the previous kernel's end", None, 1), ("x read + rmsnorm", 1, 2),
               ("32000 rows + logits", 2, 6), ("argmax + step state (last CTA)", 6, 7)]
@@ -400,7 +403,7 @@ def run_timeline(args):
     L.ptc_decoder_read_trace(dec, buf, n)
     L.ptc_decoder_trace(dec, 0)
     ctx.close()
-    t = np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(16, 2 * nl + 1, 8, 2)
+    t = np.frombuffer(buf, dtype=np.uint64).astype(np.float64).reshape(16, 2 * nl + 1, 12, 2)
     last = t[..., 1]    # latest CTA per event (ns)
     first = t[..., 0]
     order = [(start + i) % 16 for i in range(16)]

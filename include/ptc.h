@@ -213,8 +213,8 @@ void ptc_decoder_weights_updated(ptc_decoder *d);
  * clears the record and makes the attention block, the FFN block and the
  * classifier stamp %globaltimer (ns) at fixed points of their work; 0 stops
  * it. For position p (recorded modulo 16), kernel k (2l: attention block of
- * layer l, 2l+1: FFN block of layer l, 2L: classifier) and event e < 8,
- * entries 2i and 2i+1 with i = ((p % 16) * (2L + 1) + k) * 8 + e hold the
+ * layer l, 2l+1: FFN block of layer l, 2L: classifier) and event e < 12,
+ * entries 2i and 2i+1 with i = ((p % 16) * (2L + 1) + k) * 12 + e hold the
  * earliest and the latest stamp over the kernel's CTAs (an event a kernel
  * does not have keeps ~0 / 0). Tracing is a parameter of the kernels, so
  * turning it on or off synchronises the decoder's stream and re-captures

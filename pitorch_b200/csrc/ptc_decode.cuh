@@ -91,7 +91,7 @@ struct DecodeModel {
 };
 
 constexpr int TRACE_POS = 16;
-constexpr int TRACE_EV = 8;
+constexpr int TRACE_EV = 12;
 
 // Decode matvec staging: each CTA streams its contiguous block of weight rows
 // through a ring of shared-memory stages filled by bulk (TMA) copies.

@@ -884,6 +884,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1) k_ffn(DecodeModel m, FfnArgs a)
             const float h3 = smem_row_dot<NV>(w3s + (size_t)j * dim, xr, c4, lane);
             if (lane == 0) s_hb[j] = silu_mul(h1, h3);
         }
+    trace_ev(m, tr, tpos, 2 * a.l + 1, 8);
     if (ok) ok = mbar_wait_bounded(&bars[1], 0u, m.err, ERR_MBAR_TIMEOUT);
     ok = __syncthreads_and(ok);   // also publishes s_hb
     trace_ev(m, tr, tpos, 2 * a.l + 1, 4);
@@ -1109,6 +1110,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             }
         }
     }
+    trace_ev(m, tr, pos, 2 * l, 8);
     // This CTA's q/k/v values are in every CTA's s_qkv: arrive (release) on
     // the cluster barrier now and wait for it only before reading s_qkv, so
     // the copies below are issued while the barrier completes.
@@ -1148,6 +1150,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
         cp_async_commit();
     }
+    trace_ev(m, tr, pos, 2 * l, 9);
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // s_qkv complete
     trace_ev(m, tr, pos, 2 * l, 4);
     // 2. attention over [t0, t1): online softmax in rounds of AT_ROUND
@@ -1267,8 +1270,10 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
         }
         s_att[tid] = o * __fdiv_rn(1.0f, L);
     }
+    trace_ev(m, tr, pos, 2 * l, 10);
     cp_async_wait_all();
     __syncthreads();   // s_att and the wo slice
+    trace_ev(m, tr, pos, 2 * l, 11);
     // wo rows in quads: lane 8e + k reduces row 4qd + e over float4 columns
     // k, k + 8, ...; lane 0 gathers the quad and adds it at L2.
     const int e8 = lane >> 3, k8 = lane & 7;

@@ -205,9 +205,10 @@ def test_phase_timeline_records_every_kernel(ptlib):
     assert ptlib.ptc_decoder_read_trace(dec, buf, n) == n
     ptlib.ptc_decoder_trace(dec, 0)
     L = ctx.cfg.n_layers
-    t = np.frombuffer(buf, dtype=np.uint64).reshape(16, 2 * L + 1, 8, 2)
+    t = np.frombuffer(buf, dtype=np.uint64).reshape(16, 2 * L + 1, 12, 2)
     NONE = np.uint64(0xFFFFFFFFFFFFFFFF)
-    events = {"attn": [0, 1, 2, 3, 4, 5, 6, 7], "ffn": [0, 1, 2, 3, 4, 7], "cls": [0, 1, 2, 6, 7]}
+    # each kernel's points in the order its CTAs pass them
+    events = {"attn": [0, 1, 2, 3, 8, 9, 4, 5, 6, 10, 11, 7], "ffn": [0, 1, 2, 3, 8, 4, 7], "cls": [0, 1, 2, 6, 7]}
     for p in range(16):
         for k in range(2 * L + 1):
             kind = "cls" if k == 2 * L else ("attn" if k % 2 == 0 else "ffn")
