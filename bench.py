@@ -12,6 +12,11 @@ larger than the 126 MB L2, so every token streams its weights from HBM).
          (host token in, host token out), timed with CUDA events around the
          whole loop.
 
+After the decode's timed region the N = 1 line also carries the isolated
+matvec sweep (`matvec_sweep`, cold column of the 9 shapes; --sweep prints the
+full per-shape lines) and the stories15M training step (`train`; --train
+prints it alone). --no-extras leaves both out.
+
 N > 1 (torchrun): the layer pipeline over N GPUs (pt_dist_forward_step), the
 last rank holding embedding + classifier as in the pitorch ring.
 
@@ -353,6 +358,13 @@ def run_single(args):
     }
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(blob, cfg)
+    if not args.no_extras:
+        # the path's two other measured workloads, after the decode's timed
+        # region: the isolated matvec sweep (cold column) and the training step
+        sw = MatvecSweep()
+        line["matvec_sweep"] = sw.summary(3, 3)
+        sw.close()
+        line["train"] = train_line(3, 10, not args.no_cpu_baseline)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -479,10 +491,9 @@ def sweep_references(L, pc, stream, graph_time, hbm, src):
     return l2_gbs, floor_us
 
 
-def run_sweep(args):
+class MatvecSweep:
     """The isolated fp32 matvec sweep y = W.x (W rows x cols, W ~ N(0,0.02),
-    x ~ N(0,1), seeded) through the C ABI's ptc_matvec. Per shape, one JSON
-    line:
+    x ~ N(0,1), seeded) through the C ABI's ptc_matvec. Per shape:
       cold  back-to-back calls, each on a different copy of W, the copies
             together >= 2x L2 so every call streams W from HBM; the calls are
             one CUDA graph, timed with CUDA events (launches overlap through
@@ -495,40 +506,40 @@ def run_sweep(args):
     and the per-call floor of a chain of dependent matvec launches (an 8 x 4
     matvec, whose bytes take no time), so that every shape's attainable time
     is max(bytes / peak, floor)."""
-    import ctypes as C
-    import oracle
-    import pitorch_b200
-    from pitorch_b200 import api
-    L = pitorch_b200.lib()
-    pc = L.ptc_create(0, 0)
-    stream = L.ptc_stream(pc)
-    timer = L.ptc_timer_create(pc)
-    hbm, src = peaks()
 
-    def graph_time(calls, reps):
+    def __init__(self, refs=True):
+        import pitorch_b200
+        self.L = L = pitorch_b200.lib()
+        self.pc = L.ptc_create(0, 0)
+        self.stream = L.ptc_stream(self.pc)
+        self.timer = L.ptc_timer_create(self.pc)
+        self.hbm, self.src = peaks()
+        self.l2_gbs, self.floor_us = None, 0.0
+        if refs:
+            self.l2_gbs, self.floor_us = sweep_references(L, self.pc, self.stream, self.graph_time,
+                                                          self.hbm, self.src)
+
+    def graph_time(self, calls, reps):
         """ms per replay of a captured graph of the (callable) enqueues."""
+        L, pc = self.L, self.pc
         L.ptc_capture_begin(pc)
         calls()
         g = L.ptc_capture_end(pc)
         for _ in range(3):
             L.ptc_graph_launch(g)
         L.ptc_sync(pc)
-        L.ptc_timer_start(timer)
+        L.ptc_timer_start(self.timer)
         for _ in range(reps):
             L.ptc_graph_launch(g)
-        L.ptc_timer_stop(timer)
-        ms = L.ptc_timer_ms(timer) / reps
+        L.ptc_timer_stop(self.timer)
+        ms = L.ptc_timer_ms(self.timer) / reps
         L.ptc_graph_destroy(g)
         return ms
 
-    l2_gbs, floor_us = None, 0.0
-    if not args.sweep_no_refs:
-        l2_gbs, floor_us = sweep_references(L, pc, stream, graph_time, hbm, src)
-    shapes = SWEEP_SHAPES
-    if args.sweep_shapes:
-        shapes = [tuple(int(v) for v in s.split("x")) for s in args.sweep_shapes.split(",")]
-    impl = "reference" if oracle.ref_available() else "port"
-    for rows, cols in shapes:
+    def shape(self, rows, cols, warmup, steps, modes=("cold", "hot"), cpu_s=0.3):
+        """One shape's JSON record (see the class docstring)."""
+        import oracle
+        L, pc, stream, hbm = self.L, self.pc, self.stream, self.hbm
         rng = np.random.default_rng(1000 + rows + cols)
         W = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
         x = rng.standard_normal(cols).astype(np.float32)
@@ -550,7 +561,7 @@ def run_sweep(args):
         err = float(np.abs(y - ref).max() / np.abs(ref).max())
         bytes_call = 4 * (rows * cols + rows + cols)
         res = {}
-        for mode in ("cold", "hot"):
+        for mode in modes:
             n_calls = n_copies if mode == "cold" else max(64, n_copies)
             while n_calls * bytes_call < 1.5e9 and n_calls < 4096:   # >= ~0.25 ms of work per replay
                 n_calls *= 2
@@ -559,45 +570,80 @@ def run_sweep(args):
                 Wi = dW + (i % n_copies) * wbytes if mode == "cold" else dW
                 L.ptc_matvec(Wi, dx, dy, rows, cols, stream)
             g = L.ptc_capture_end(pc)
-            for _ in range(max(3, args.warmup)):
+            for _ in range(max(3, warmup)):
                 L.ptc_graph_launch(g)
             L.ptc_sync(pc)
-            reps = max(3, args.steps)
-            L.ptc_timer_start(timer)
+            reps = max(3, steps)
+            L.ptc_timer_start(self.timer)
             for _ in range(reps):
                 L.ptc_graph_launch(g)
-            L.ptc_timer_stop(timer)
-            ms = L.ptc_timer_ms(timer)
+            L.ptc_timer_stop(self.timer)
+            ms = L.ptc_timer_ms(self.timer)
             L.ptc_graph_destroy(g)
             us_call = 1000 * ms / (reps * n_calls)
             gbs = bytes_call / (us_call * 1e-6) / 1e9
-            peak_mode = hbm if (mode == "cold" or not l2_gbs or wbytes > L2_BYTES // 2) else l2_gbs
-            attain_us = max(bytes_call / (peak_mode * 1e3), floor_us)
+            peak_mode = hbm if (mode == "cold" or not self.l2_gbs or wbytes > L2_BYTES // 2) else self.l2_gbs
+            attain_us = max(bytes_call / (peak_mode * 1e3), self.floor_us)
             res[mode] = {"GB/s": gbs, "us_per_call": us_call, "calls_per_graph": n_calls,
                          "frac_of_hbm": gbs / hbm, "peak": peak_mode,
                          "peak_kind": "hbm" if peak_mode == hbm else "l2 (measured)",
                          "frac_of_peak": gbs / peak_mode,
                          "attainable_us": attain_us, "frac_of_attainable": attain_us / us_call}
-        # CPU: the reference's smatvec_cpu on a bounded sample
-        n_cpu, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < 0.3 or n_cpu < 2:
-            oracle.matvec(W, x, impl=impl)
-            n_cpu += 1
-        cpu_us = 1e6 * (time.perf_counter() - t0) / n_cpu
-        line = {
-            "metric": "fp32 matvec GB/s", "shape": f"{rows}x{cols}", "unit": "GB/s", "n_gpus": 1,
-            "value": res["cold"]["GB/s"], "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-            "bytes_per_call": bytes_call, "cold": res["cold"], "hot": res["hot"],
-            "cold_copies": n_copies, "l2_policy": f"cold: {n_copies} copies of W = "
-                                                  f"{n_copies * wbytes / 2**20:.0f} MiB >= 2x L2",
-            "peak": hbm, "peak_source": f"{src} hbm_gbs", "parity_rel_err": err,
-            "cpu_baseline": {"value": bytes_call / (cpu_us * 1e-6) / 1e9, "unit": "GB/s", "cores": 1,
-                             "kind": impl, "us_per_call": cpu_us,
-                             "sample": f"{n_cpu} calls of smatvec_cpu on the same W, x"},
-        }
+        rec = {"shape": f"{rows}x{cols}", "bytes_per_call": bytes_call, "parity_rel_err": err,
+               "cold_copies": n_copies, "w_bytes": wbytes, **res}
+        if cpu_s > 0:
+            # CPU: the reference's smatvec_cpu on a bounded sample
+            impl = "reference" if oracle.ref_available() else "port"
+            n_cpu, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < cpu_s or n_cpu < 2:
+                oracle.matvec(W, x, impl=impl)
+                n_cpu += 1
+            cpu_us = 1e6 * (time.perf_counter() - t0) / n_cpu
+            rec["cpu_baseline"] = {"value": bytes_call / (cpu_us * 1e-6) / 1e9, "unit": "GB/s", "cores": 1,
+                                   "kind": impl, "us_per_call": cpu_us,
+                                   "sample": f"{n_cpu} calls of smatvec_cpu on the same W, x"}
+        return rec
+
+    def summary(self, warmup, steps):
+        """The cold column of all 9 shapes in compact form, for the decode
+        line (so every default bench run carries the matvec sweep)."""
+        out = {"l2_read_gbs": self.l2_gbs, "launch_floor_us": self.floor_us,
+               "peak": self.hbm, "peak_source": f"{self.src} hbm_gbs",
+               "timing": "cold: one CUDA graph of back-to-back calls on copies of W >= 2x L2, CUDA events",
+               "shapes": {}}
+        for rows, cols in SWEEP_SHAPES:
+            r = self.shape(rows, cols, warmup, steps, modes=("cold",), cpu_s=0.0)
+            c = r["cold"]
+            out["shapes"][r["shape"]] = {"GB/s": round(c["GB/s"], 1), "us_per_call": round(c["us_per_call"], 3),
+                                         "frac_of_hbm": round(c["frac_of_hbm"], 3),
+                                         "attainable_us": round(c["attainable_us"], 3),
+                                         "frac_of_attainable": round(c["frac_of_attainable"], 3),
+                                         "parity_rel_err": r["parity_rel_err"]}
+        return out
+
+    def close(self):
+        self.L.ptc_timer_destroy(self.timer)
+        self.L.ptc_destroy(self.pc)
+
+
+def run_sweep(args):
+    """One JSON line per shape of the isolated matvec sweep (MatvecSweep)."""
+    sw = MatvecSweep(refs=not args.sweep_no_refs)
+    shapes = SWEEP_SHAPES
+    if args.sweep_shapes:
+        shapes = [tuple(int(v) for v in s.split("x")) for s in args.sweep_shapes.split(",")]
+    for rows, cols in shapes:
+        r = sw.shape(rows, cols, args.warmup, args.steps)
+        line = {"metric": "fp32 matvec GB/s", "shape": r["shape"], "unit": "GB/s", "n_gpus": 1,
+                "value": r["cold"]["GB/s"], "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                "bytes_per_call": r["bytes_per_call"], "cold": r["cold"], "hot": r["hot"],
+                "cold_copies": r["cold_copies"],
+                "l2_policy": f"cold: {r['cold_copies']} copies of W = "
+                             f"{r['cold_copies'] * r['w_bytes'] / 2**20:.0f} MiB >= 2x L2",
+                "peak": sw.hbm, "peak_source": f"{sw.src} hbm_gbs", "parity_rel_err": r["parity_rel_err"],
+                "cpu_baseline": r["cpu_baseline"]}
         print(json.dumps(line), flush=True)
-    L.ptc_timer_destroy(timer)
-    L.ptc_destroy(pc)
+    sw.close()
     return 0
 
 
@@ -617,6 +663,14 @@ def run_train(args):
     """Training throughput: pt_train_step on the stories15M shape, T = 256
     seeded tokens, lr 1e-3 (the reference's training benchmark settings), timed with CUDA
     events around K whole steps (each returns its loss to the host)."""
+    print(json.dumps(train_line(args.warmup, args.steps, not args.no_cpu_baseline)), flush=True)
+    return 0
+
+
+def train_line(warmup, steps, cpu):
+    """The training measurement of run_train as a dict, with the GEMM
+    launches of the timed steps by path (ptc_gemm_counters)."""
+    import ctypes as C
     import oracle
     import pitorch_b200
     from pitorch_b200 import api
@@ -629,21 +683,24 @@ def run_train(args):
     pc = ctx.ptc_ctx()
     timer = L.ptc_timer_create(pc)
     losses = []
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         losses.append(ctx.train_step(tokens, lr))
     L.ptc_sync(pc)
+    cnt0, cnt1 = (C.c_longlong * 4)(), (C.c_longlong * 4)()
+    L.ptc_gemm_counters(cnt0)
     with ClockSampler(0) as clk:
         L.ptc_timer_start(timer)
-        for _ in range(args.steps):
+        for _ in range(steps):
             losses.append(ctx.train_step(tokens, lr))
         L.ptc_timer_stop(timer)
-        ms = L.ptc_timer_ms(timer) / args.steps
+        ms = L.ptc_timer_ms(timer) / steps
+    L.ptc_gemm_counters(cnt1)
     L.ptc_timer_destroy(timer)
     ctx.close()
     flops = train_flops(cfg, T)
     line = {
         "metric": "stories15M train step tokens/s (T=256)", "value": T / (ms / 1000.0), "unit": "tokens/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,0.02) weights, seeded uniform tokens)",
         "config": {"workload": "pt_train_step: forward, cross-entropy, backward, SGD", "model": model,
@@ -651,7 +708,10 @@ def run_train(args):
         "achieved_gflops": flops / (ms / 1000.0) / 1e9, "flops_per_step": flops,
         "losses_first": losses[:3], "clocks": clk.summary(),
     }
-    if not args.no_cpu_baseline:
+    per = [(cnt1[k] - cnt0[k]) / steps for k in range(4)]
+    line["gemm_launches_per_step"] = {"tensor_core": per[0], "simt": per[1], "splitk_reduce": per[2],
+                                      "simt_cluster_reduced": per[3]}
+    if cpu:
         impl = "reference" if oracle.ref_available() else "port"
         m = oracle.Model(blob, max_T=T, impl=impl)
         t0 = time.perf_counter()
@@ -659,9 +719,8 @@ def run_train(args):
         dt = time.perf_counter() - t0
         line["cpu_baseline"] = {"value": T / dt, "unit": "tokens/s", "cores": 1, "kind": impl,
                                 "s_per_step": dt, "sample": "one pt_train_step at T=256 on the same weights"}
-        line["loss_rel_err_step0"] = abs(losses[0] - ref_loss) / abs(ref_loss) if args.warmup else None
-    print(json.dumps(line), flush=True)
-    return 0
+        line["loss_rel_err_step0"] = abs(losses[0] - ref_loss) / abs(ref_loss) if warmup else None
+    return line
 
 
 def main():
@@ -671,6 +730,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode line only: skip the matvec sweep and training step it carries")
     ap.add_argument("--positions", type=int, default=0,
                     help="decode positions per step (default: the model's seq_len, 1024)")
     ap.add_argument("--sweep", action="store_true",
