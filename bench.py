@@ -732,6 +732,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode line only: skip the matvec sweep and training step it carries")
+    ap.add_argument("--no-vocab-parallel", action="store_true",
+                    help="N > 1: skip the second measurement with the classifier split over all ranks")
     ap.add_argument("--positions", type=int, default=0,
                     help="decode positions per step (default: the model's seq_len, 1024)")
     ap.add_argument("--sweep", action="store_true",

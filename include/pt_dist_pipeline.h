@@ -90,6 +90,22 @@ int pt_dist_allreduce_grads_avg(pt_context_t *ctx, pt_dist_t *dist);
 /* Ranks in the NCCL communicator of a joined ring (ncclCommCount), or -1. */
 int pt_dist_comm_size(const pt_dist_t *dist);
 
+/* Vocab-parallel classifier (no reference counterpart: the reference's head
+ * rank computes every vocab row, pitorch/model/llama2.c:194-198). After it,
+ * every rank computes the logits of its 1/world share of the classifier rows
+ * on the final residual, and the argmax is combined across ranks on the GPU
+ * (ptc_decoder_set_vocab_parallel); token streams are unchanged. Collective:
+ * every rank calls it once, after pt_dist_setup_ctx (or with a pt_dist_setup
+ * ring, which it joins). Needs the NVLink hop transport and the reference's
+ * shard layout (layers on ranks 0..world-2, embedding + classifier on the
+ * last). Returns 0, or -1 with nothing changed when that does not hold or a
+ * transfer timed out. Afterwards, in host-driven steps (pt_dist_forward_step)
+ * every rank must set ctx->sync_logits alike: with it set, the head gathers
+ * the other ranks' logits. */
+int pt_dist_vocab_parallel(pt_context_t *ctx, pt_dist_t *dist);
+/* 1 once pt_dist_vocab_parallel succeeded on this ring, else 0. */
+int pt_dist_is_vocab_parallel(const pt_dist_t *dist);
+
 /* Largest value of `v` over all ranks (for max-over-ranks timing). */
 float pt_dist_max_float(pt_context_t *ctx, pt_dist_t *dist, float v);
 

@@ -206,6 +206,39 @@ void ptc_decoder_enqueue_stage(ptc_decoder *d, int n);
  * seq_len): an embedding+head stage's classifier sends no input past it. */
 void ptc_decoder_set_stop(ptc_decoder *d, int n_pos);
 
+/* Vocab-parallel classifier (no reference counterpart: the reference's head
+ * rank computes all vocab rows, pitorch/model/llama2.c:194-198, inside its
+ * ring, pitorch/dist/pt_dist_pipeline.c:290-333). Every rank of a pipeline
+ * computes the logits of its own rows of the classifier on the final
+ * residual and sends its argmax key to the combining ranks -- rank 0, which
+ * then reads the next token's embedding row itself, and the head rank, which
+ * keeps the token stream -- and these take the max over all ranks' keys.
+ * Needs pipeline links (ptc_decoder_set_links). `box` is this rank's
+ * classifier mailbox, ptc_mailbox_alloc(c, dim + 4 * ranks): the final
+ * residual x[dim], then one 16-byte key slot per rank. NULL turns the split
+ * off. Synchronises the decoder's stream and re-captures its graphs. */
+#define PTC_VP_MAX_RANKS 8
+typedef struct {
+    int row0, rows;          /* this rank's classifier rows [row0, row0 + rows) */
+    int ranks, rank;         /* ranks sharing the classifier; this rank's key slot */
+    int combine;             /* 1: collect every rank's key and select the token */
+    int x_local;             /* 1: this rank ran the last layer (its rows read its own residual) */
+    int embed_local;         /* 1: layer 0 reads the token's embedding row (no input message) */
+    const float *cls_rows;   /* device rows [row0, row0 + rows), dim floats each */
+    const float *rms_final;  /* device final rmsnorm gain [dim] */
+    const float *embedding;  /* device [vocab][dim] token embedding (embed_local), else NULL */
+    const void *box;         /* this rank's classifier mailbox */
+    void *x_out[PTC_VP_MAX_RANKS];  /* x_local: the other ranks' classifier mailboxes (mapped) */
+    int n_x_out;
+    void *key_out[2];        /* the combining ranks' classifier mailboxes other than this rank's */
+    int n_key_out;
+    unsigned *sent;          /* device counters: [0] residuals sent, [1] keys sent; zero at the start */
+} ptc_vocab_split;
+void ptc_decoder_set_vocab_parallel(ptc_decoder *d, const ptc_vocab_split *vp);
+/* Host-driven step input of a pipeline rank: mode 0, position pos, and the
+ * input token copied from device memory (tok_dev; NULL keeps the token). */
+void ptc_decoder_set_input(ptc_decoder *d, int pos, const int *tok_dev);
+
 /* Weights were updated in place (training): refresh derived device copies. */
 void ptc_decoder_weights_updated(ptc_decoder *d);
 /* Phase timeline of the decode kernels (profiling; no reference

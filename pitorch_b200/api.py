@@ -179,6 +179,8 @@ def declare(L):
     _sig(L, "pt_dist_setup_ctx", C.c_int, dist, ctx, P(pt_shard_info_t), C.c_int, C.c_int)
     _sig(L, "pt_dist_transport", C.c_int, dist)
     _sig(L, "pt_dist_comm_size", C.c_int, dist)
+    _sig(L, "pt_dist_vocab_parallel", C.c_int, ctx, dist)
+    _sig(L, "pt_dist_is_vocab_parallel", C.c_int, dist)
     _sig(L, "pt_dist_train_step_mb", pt_dist_result_t, ctx, dist, i32p, C.c_int, C.c_int, C.c_float)
     _sig(L, "pt_dist_forward_step", C.c_int, ctx, dist, C.c_int)
     _sig(L, "pt_dist_generate_greedy", C.c_int, ctx, dist, i32p, C.c_int, C.c_int, i32p)
@@ -360,6 +362,12 @@ class Pipeline:
     def is_head(self):
         return bool(self.dist.has_embed and self.dist.has_head)
 
+    def vocab_parallel(self):
+        """Split the classifier over all ranks (pt_dist_vocab_parallel; every
+        rank calls it)."""
+        if self.L.pt_dist_vocab_parallel(C.byref(self.ctx.ctx), C.byref(self.dist)) != 0:
+            raise RuntimeError(f"rank {self.rank}: vocab-parallel classifier set-up failed")
+
     def generate_greedy(self, prompt, n_pos):
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.zeros(n_pos, dtype=np.int32)
@@ -372,20 +380,25 @@ class Pipeline:
     def forward_step(self, token):
         return self.L.pt_dist_forward_step(C.byref(self.ctx.ctx), C.byref(self.dist), int(token))
 
-    def decode_greedy(self, prompt, n_pos):
-        """Host-driven pipeline decode through pt_dist_forward_step."""
+    def decode_greedy(self, prompt, n_pos, logit_rows=()):
+        """Host-driven pipeline decode through pt_dist_forward_step. On the
+        head rank, logit_rows selects positions whose host logits are kept
+        (returned as a dict after the tokens when given)."""
         self.ctx.reset_kv()
         toks = np.zeros(n_pos, dtype=np.int32)
+        kept = {}
         tok = int(prompt[0])
         for p in range(n_pos):
             nxt = self.forward_step(tok)
             if nxt < 0:
                 raise RuntimeError("pipeline step failed")
             if self.is_head:
+                if p in logit_rows:
+                    kept[p] = self.ctx.logits()
                 nxt = int(prompt[p + 1]) if p + 1 < len(prompt) else nxt
                 toks[p] = nxt
                 tok = nxt
-        return toks
+        return (toks, kept) if logit_rows else toks
 
     def train_step(self, tokens, lr):
         tokens = np.ascontiguousarray(tokens, dtype=np.int32)

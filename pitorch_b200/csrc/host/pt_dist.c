@@ -51,6 +51,12 @@ typedef struct {
     void *peer_box;       /* the successor's mailbox, mapped */
     unsigned *ctr;        /* device [0] messages sent, [1] messages received */
     int *hop_err;         /* device: a hop wait ran out */
+    /* vocab-parallel classifier (pt_dist_vocab_parallel) */
+    int vp;
+    void *vp_box;                      /* this rank's classifier mailbox */
+    void *vp_peer[PTC_VP_MAX_RANKS];   /* other ranks' classifier mailboxes, mapped where needed */
+    unsigned *vp_sent;                 /* device [0] residuals sent, [1] keys sent */
+    int *tokmsg;                       /* device: the head's input token of a host-driven step */
 } dist_comm_t;
 
 static long now_ms(void) {
@@ -172,6 +178,34 @@ static long long hop_timeout_ns(const pt_dist_t *dist);
 static int next_rank(const pt_dist_t *d) { return (d->rank + 1) % d->world_size; }
 static int prev_rank(const pt_dist_t *d) { return (d->rank + d->world_size - 1) % d->world_size; }
 
+/* All-gather the IPC handle of this rank's mailbox `box` (NULL: none) into
+ * hh[world][PTC_MAILBOX_HANDLE_BYTES]. Returns 0, or -1 on a timeout. */
+static int gather_handles(pt_dist_t *dist, pt_context_t *ctx, void *box, unsigned char *hh) {
+    dist_comm_t *c = comm_of(dist);
+    ptc_ctx *pc = ctx->dev->ctx;
+    cudaStream_t s = (cudaStream_t)ptc_stream(pc);
+    const int W = dist->world_size, H = PTC_MAILBOX_HANDLE_BYTES;
+    unsigned char *dh = (unsigned char *)ptc_alloc(pc, (size_t)W * H);
+    memset(hh, 0, (size_t)W * H);
+    if (box) ptc_mailbox_handle(box, hh + (size_t)dist->rank * H);
+    cudaMemcpyAsync(dh + (size_t)dist->rank * H, hh + (size_t)dist->rank * H, H, cudaMemcpyHostToDevice, s);
+    ncclAllGather(dh + (size_t)dist->rank * H, dh, H, ncclUint8, c->comm, s);
+    cudaMemcpyAsync(hh, dh, (size_t)W * H, cudaMemcpyDeviceToHost, s);
+    return finish(dist, ctx, "mailbox exchange timeout");
+}
+
+/* 1 when every rank's `ok` is non-zero (a min all-reduce), -1 on a timeout. */
+static int agree(pt_dist_t *dist, pt_context_t *ctx, int ok, const char *what) {
+    dist_comm_t *c = comm_of(dist);
+    cudaStream_t s = (cudaStream_t)ptc_stream(ctx->dev->ctx);
+    float v = ok ? 1.f : 0.f;
+    cudaMemcpyAsync(c->scal, &v, 4, cudaMemcpyHostToDevice, s);
+    ncclAllReduce(c->scal, c->scal, 1, ncclFloat, ncclMin, c->comm, s);
+    cudaMemcpyAsync(&v, c->scal, 4, cudaMemcpyDeviceToHost, s);
+    if (finish(dist, ctx, what) < 0) return -1;
+    return v < 1.f ? 0 : 1;
+}
+
 /* Decode hops over NVLink: allocate this rank's mailbox, all-gather the IPC
  * handles, map the successor's mailbox, and agree on the transport (every
  * rank must use the same one). PT_DIST_P2P=0 keeps NCCL send/recv. Returns
@@ -183,26 +217,20 @@ static int setup_p2p(pt_dist_t *dist, pt_context_t *ctx) {
     ptc_ctx *pc = ctx->dev->ctx;
     cudaStream_t s = (cudaStream_t)ptc_stream(pc);
     const int W = dist->world_size, H = PTC_MAILBOX_HANDLE_BYTES;
-    unsigned char *dh = (unsigned char *)ptc_alloc(pc, (size_t)W * H);
     unsigned char *hh = (unsigned char *)calloc((size_t)W, H);
     c->box = ptc_mailbox_alloc(pc, c->dim);
-    int ok = c->box && ptc_mailbox_handle(c->box, hh + (size_t)dist->rank * H) == 0;
-    cudaMemcpyAsync(dh + (size_t)dist->rank * H, hh + (size_t)dist->rank * H, H, cudaMemcpyHostToDevice, s);
-    ncclAllGather(dh + (size_t)dist->rank * H, dh, H, ncclUint8, c->comm, s);
-    cudaMemcpyAsync(hh, dh, (size_t)W * H, cudaMemcpyDeviceToHost, s);
-    if (finish(dist, ctx, "mailbox exchange timeout") < 0) {
+    unsigned char probe[PTC_MAILBOX_HANDLE_BYTES];
+    int ok = c->box && ptc_mailbox_handle(c->box, probe) == 0;
+    if (gather_handles(dist, ctx, ok ? c->box : NULL, hh) < 0) {
         free(hh);
         return -1;
     }
     if (ok) c->peer_box = ptc_mailbox_open(pc, hh + (size_t)next_rank(dist) * H);
     free(hh);
     ok = ok && c->peer_box;
-    float v = ok ? 1.f : 0.f;
-    cudaMemcpyAsync(c->scal, &v, 4, cudaMemcpyHostToDevice, s);
-    ncclAllReduce(c->scal, c->scal, 1, ncclFloat, ncclMin, c->comm, s);
-    cudaMemcpyAsync(&v, c->scal, 4, cudaMemcpyDeviceToHost, s);
-    if (finish(dist, ctx, "mailbox agreement timeout") < 0) return -1;
-    if (v < 1.f) {   /* somebody could not map its successor: NCCL hops everywhere */
+    const int all = agree(dist, ctx, ok, "mailbox agreement timeout");
+    if (all < 0) return -1;
+    if (!all) {   /* somebody could not map its successor: NCCL hops everywhere */
         ptc_mailbox_close(c->peer_box);
         ptc_mailbox_free(c->box);
         c->peer_box = c->box = NULL;
@@ -294,6 +322,8 @@ int pt_dist_setup_ctx(pt_dist_t *dist, pt_context_t *ctx, const pt_shard_info_t 
 void pt_dist_free(pt_dist_t *dist) {
     dist_comm_t *c = comm_of(dist);
     if (!c) return;
+    for (int q = 0; q < PTC_VP_MAX_RANKS; q++) ptc_mailbox_close(c->vp_peer[q]);
+    ptc_mailbox_free(c->vp_box);
     ptc_mailbox_close(c->peer_box);
     ptc_mailbox_free(c->box);
     if (c->comm) ncclCommDestroy(c->comm);
@@ -419,6 +449,172 @@ static void enqueue_position(pt_dist_t *dist, pt_context_t *ctx, int host_token,
     }
 }
 
+/* ---- vocab-parallel classifier --------------------------------------------- */
+
+/* First classifier row of rank q's share: rank q computes rows
+ * [vp_row(q), vp_row(q + 1)). */
+static long vp_row(const pt_context_t *ctx, const pt_dist_t *d, int q) {
+    return (long)ctx->dev->cfg.vocab_size * q / d->world_size;
+}
+
+static int is_head(const pt_dist_t *d) { return d->has_embed && d->has_head; }
+
+/* Every rank computes the logits of its share of the classifier rows (the
+ * reference's head rank computes them all, pitorch/model/llama2.c:194-198);
+ * the last layer rank sends the final residual to every rank, and each rank
+ * sends its argmax key to rank 0 (which embeds the next token itself) and to
+ * the head rank (which keeps the token stream). The head sends every rank
+ * its rows and the final rmsnorm gain once, and rank 0 the embedding table,
+ * over NCCL; the decode hops stay peer stores over NVLink. */
+int pt_dist_vocab_parallel(pt_context_t *ctx, pt_dist_t *dist) {
+    if (join(dist, ctx) < 0) return -1;
+    dist_comm_t *c = comm_of(dist);
+    if (!c->comm) return -1;
+    if (c->vp) return 0;
+    const int W = dist->world_size, r = dist->rank, head = W - 1, last = W - 2;
+    const struct pt_device *dv = ctx->dev;
+    const int dim = dv->cfg.dim, V = dv->cfg.vocab_size, n_local = dv->cfg.n_layers;
+    /* the reference's layout: layers on ranks 0..W-2, embedding + classifier on the last */
+    int ok = c->p2p && W >= 2 && W <= PTC_VP_MAX_RANKS && V >= W && (r == head) == (is_head(dist) != 0) &&
+             (r == head ? n_local == 0 : n_local > 0);
+    int all = agree(dist, ctx, ok, "vocab-parallel agreement timeout");
+    if (all <= 0) {
+        if (all == 0 && r == 0)
+            fprintf(stderr, "R%d: vocab-parallel classifier needs the NVLink hop transport, 2..%d ranks and the "
+                            "layers-then-head layout\n", r, PTC_VP_MAX_RANKS);
+        return -1;
+    }
+    ptc_ctx *pc = dv->ctx;
+    cudaStream_t s = stream_of(ctx);
+    const long r0 = vp_row(ctx, dist, r), nr = vp_row(ctx, dist, r + 1) - r0;
+    const float *rows, *gain, *table = NULL;
+    ncclGroupStart();
+    if (r == head) {
+        rows = dv->dw.wcls + (size_t)r0 * dim;
+        gain = dv->dw.rms_final_weight;
+        for (int q = 0; q < head; q++) {
+            const long q0 = vp_row(ctx, dist, q), qn = vp_row(ctx, dist, q + 1) - q0;
+            ncclSend(gain, (size_t)dim, ncclFloat, q, c->comm, s);
+            ncclSend(dv->dw.wcls + (size_t)q0 * dim, (size_t)qn * dim, ncclFloat, q, c->comm, s);
+            if (q == 0) ncclSend(dv->dw.token_embedding, (size_t)V * dim, ncclFloat, 0, c->comm, s);
+        }
+    } else {
+        float *g = (float *)ptc_alloc(pc, (size_t)dim * 4);
+        float *w = (float *)ptc_alloc(pc, (size_t)nr * dim * 4);
+        ncclRecv(g, (size_t)dim, ncclFloat, head, c->comm, s);
+        ncclRecv(w, (size_t)nr * dim, ncclFloat, head, c->comm, s);
+        if (r == 0) {
+            float *t = (float *)ptc_alloc(pc, (size_t)V * dim * 4);
+            ncclRecv(t, (size_t)V * dim, ncclFloat, head, c->comm, s);
+            table = t;
+        }
+        rows = w;
+        gain = g;
+    }
+    ncclGroupEnd();
+    if (finish(dist, ctx, "vocab-parallel weights timeout") < 0) return -1;
+
+    /* mailboxes: every rank's, mapped by the ranks that write it */
+    const int H = PTC_MAILBOX_HANDLE_BYTES;
+    unsigned char *hh = (unsigned char *)calloc((size_t)W, H);
+    c->vp_box = ptc_mailbox_alloc(pc, dim + 4 * W);
+    if (gather_handles(dist, ctx, c->vp_box, hh) < 0) {
+        free(hh);
+        return -1;
+    }
+    ok = c->vp_box != NULL;
+    for (int q = 0; q < W && ok; q++) {
+        const int need = q != r && (q == 0 || q == head || r == last);
+        if (need) ok = (c->vp_peer[q] = ptc_mailbox_open(pc, hh + (size_t)q * H)) != NULL;
+    }
+    free(hh);
+    all = agree(dist, ctx, ok, "vocab-parallel mailbox timeout");
+    if (all <= 0) {
+        for (int q = 0; q < W; q++) {
+            ptc_mailbox_close(c->vp_peer[q]);
+            c->vp_peer[q] = NULL;
+        }
+        ptc_mailbox_free(c->vp_box);
+        c->vp_box = NULL;
+        return -1;
+    }
+    c->vp_sent = (unsigned *)ptc_alloc(pc, 2 * sizeof(unsigned));
+    c->tokmsg = (int *)ptc_alloc(pc, 16);
+    cudaMemsetAsync(c->vp_sent, 0, 2 * sizeof(unsigned), s);
+    if (finish(dist, ctx, "vocab-parallel setup timeout") < 0) return -1;
+
+    ptc_vocab_split vp;
+    memset(&vp, 0, sizeof(vp));
+    vp.row0 = (int)r0;
+    vp.rows = (int)nr;
+    vp.ranks = W;
+    vp.rank = r;
+    vp.combine = r == 0 || r == head;
+    vp.x_local = r == last;
+    vp.embed_local = r == 0;
+    vp.cls_rows = rows;
+    vp.rms_final = gain;
+    vp.embedding = table;
+    vp.box = c->vp_box;
+    if (r == last)
+        for (int q = 0; q < W; q++)
+            if (q != r) vp.x_out[vp.n_x_out++] = c->vp_peer[q];
+    if (r != 0) vp.key_out[vp.n_key_out++] = c->vp_peer[0];
+    if (r != head) vp.key_out[vp.n_key_out++] = c->vp_peer[head];
+    vp.sent = c->vp_sent;
+    ptc_decoder_set_vocab_parallel(dv->dec, &vp);
+    c->vp = 1;
+    return 0;
+}
+
+int pt_dist_is_vocab_parallel(const pt_dist_t *dist) {
+    const dist_comm_t *c = (const dist_comm_t *)dist->comm;
+    return c && c->vp;
+}
+
+/* The head rank's logits of a host-driven step: every rank's share of the
+ * rows, gathered over NCCL (each rank wrote its rows at their global index). */
+static void vp_gather_logits(pt_dist_t *dist, pt_context_t *ctx) {
+    dist_comm_t *c = comm_of(dist);
+    cudaStream_t s = stream_of(ctx);
+    float *lg = ptc_decoder_logits_dev(ctx->dev->dec);
+    const int head = dist->world_size - 1;
+    ncclGroupStart();
+    if (dist->rank == head) {
+        for (int q = 0; q < head; q++) {
+            const long q0 = vp_row(ctx, dist, q), qn = vp_row(ctx, dist, q + 1) - q0;
+            ncclRecv(lg + q0, (size_t)qn, ncclFloat, q, c->comm, s);
+        }
+    } else {
+        const long r0 = vp_row(ctx, dist, dist->rank), nr = vp_row(ctx, dist, dist->rank + 1) - r0;
+        ncclSend(lg + r0, (size_t)nr, ncclFloat, head, c->comm, s);
+    }
+    ncclGroupEnd();
+}
+
+/* One host-driven position with the vocab-parallel classifier: the head's
+ * token goes to every rank (an NCCL broadcast; rank 0 embeds it), every rank
+ * replays its one-position stage graph, and the head gathers the logits when
+ * the caller keeps host logits. */
+static int vp_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token) {
+    dist_comm_t *c = comm_of(dist);
+    ptc_decoder *dec = ctx->dev->dec;
+    cudaStream_t s = stream_of(ctx);
+    const int head = dist->world_size - 1;
+    if (dist->rank == head) cudaMemcpyAsync(c->tokmsg, &token, sizeof(int), cudaMemcpyHostToDevice, s);
+    ncclBroadcast(c->tokmsg, c->tokmsg, 1, ncclInt, head, c->comm, s);
+    if (dist->rank == 0) ptc_decoder_set_input(dec, ctx->pos, c->tokmsg);
+    else if (dist->rank == head) ptc_decoder_set_input(dec, ctx->pos, NULL);
+    ptc_decoder_enqueue_stage(dec, 1);
+    if (ctx->sync_logits) vp_gather_logits(dist, ctx);
+    if (finish(dist, ctx, "dist forward timeout") < 0) return -1;
+    if (hop_failed(dist, ctx)) return -1;
+    int next = 0;
+    if (dist->rank == head) next = ptc_decoder_fetch_next(dec, ctx->sync_logits ? ctx->state.logits : NULL);
+    ctx->pos++;
+    return next;
+}
+
 /* pt_dist_pipeline.c:284-372 */
 int pt_dist_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token) {
     if (join(dist, ctx) < 0) return -1;
@@ -428,13 +624,17 @@ int pt_dist_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token) {
     if (dist->has_embed && dist->has_head && (token < 0 || token >= ctx->cfg.vocab_size))
         pt_fatal("token %d outside [0, %d)", token, ctx->cfg.vocab_size);
     long t0 = now_ms();
-    enqueue_position(dist, ctx, token, ctx->pos, 0);
     int next = 0;
-    if (finish(dist, ctx, "dist forward recv timeout") < 0) return -1;
-    if (hop_failed(dist, ctx)) return -1;
-    if (dist->has_embed && dist->has_head) {
-        next = ptc_decoder_fetch_next(ctx->dev->dec, ctx->sync_logits ? ctx->state.logits : NULL);
-        ctx->pos++;
+    if (c->vp) {
+        if ((next = vp_forward_step(ctx, dist, token)) < 0) return -1;
+    } else {
+        enqueue_position(dist, ctx, token, ctx->pos, 0);
+        if (finish(dist, ctx, "dist forward recv timeout") < 0) return -1;
+        if (hop_failed(dist, ctx)) return -1;
+        if (dist->has_embed && dist->has_head) {
+            next = ptc_decoder_fetch_next(ctx->dev->dec, ctx->sync_logits ? ctx->state.logits : NULL);
+            ctx->pos++;
+        }
     }
     if (c->verbose)
         printf("R%d pos %d -> %d | %ldms\n", dist->rank, c->step, next, now_ms() - t0);
@@ -451,7 +651,11 @@ int pt_dist_generate_greedy(pt_context_t *ctx, pt_dist_t *dist, const int *promp
     if (n_pos > ctx->cfg.seq_len) n_pos = ctx->cfg.seq_len;
     ptc_decoder_reset(dec);   /* also position 0 */
     if (dist->has_embed && dist->has_head) ptc_decoder_generate_begin(dec, prompt, n_prompt);
-    if (c->p2p) {
+    if (c->vp) {
+        /* vocab-parallel: rank 0 selects tokens too (it embeds them) */
+        if (dist->rank == 0) ptc_decoder_generate_begin(dec, prompt, n_prompt);
+        ptc_decoder_enqueue_stage(dec, n_pos);
+    } else if (c->p2p) {
         /* Link form: the head rank sends position 0's embedding row; from
          * then on every position's input travels inside the decode kernels
          * (the classifier sends the next embedding row, the layer ranks
@@ -471,6 +675,7 @@ int pt_dist_generate_greedy(pt_context_t *ctx, pt_dist_t *dist, const int *promp
         ptc_decoder_read_tokens(dec, out_tokens, n_pos);
         ctx->pos = n_pos;
     }
+    if (c->vp) ctx->pos = n_pos;
     return 0;
 }
 

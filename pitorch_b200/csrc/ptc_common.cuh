@@ -213,6 +213,16 @@ struct MailboxHeader {
     int pad[2];     // x starts 16-byte aligned
 };
 
+// One rank's classifier result in a vocab-parallel decode: the packed argmax
+// key of its rows for position `pos`, published by `seq` (release, system
+// scope) like a mailbox message. A combining rank's mailbox carries one slot
+// per rank after its x.
+struct KeySlot {
+    unsigned long long key;
+    unsigned seq;
+    int pos;
+};
+
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

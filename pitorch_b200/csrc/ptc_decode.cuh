@@ -3,6 +3,9 @@
 
 #include <stdint.h>
 
+#include "../../include/ptc.h"
+#include "ptc_common.cuh"
+
 namespace ptc {
 
 // Per-step control block, resident in device memory. The decode kernels read
@@ -25,6 +28,11 @@ struct StepState {
     // sender's count of the same link). Kept across decodes: the fields
     // above it are rewritten when a decode begins, this one never.
     unsigned recvd;
+    // Vocab-parallel classifier: final residuals taken from this rank's
+    // classifier mailbox, and key rounds collected from the other ranks
+    // (kept across decodes like recvd).
+    unsigned cls_recvd;
+    unsigned key_recvd;
     unsigned pad2;
 };
 
@@ -88,6 +96,24 @@ struct DecodeModel {
     int *link_err;                 // 1: a mailbox wait expired, 2: a message for another position
     unsigned long long link_timeout_ns;
     int link_mode;
+    int link_recv;   // link form: the first layer takes x from in_box (else the token's embedding row)
+    // Vocab-parallel classifier (ptc_decoder_set_vocab_parallel; vp_rows 0:
+    // off). Every rank of the pipeline computes the logits of its rows
+    // [vp_row0, vp_row0 + vp_rows) of the classifier on the final residual
+    // and sends its argmax key to the combining ranks, which take the max
+    // over all ranks' keys as the step's token.
+    int vp_row0, vp_rows;
+    int vp_ranks, vp_rank;
+    int vp_combine;          // this rank collects the keys (rank 0 and the head rank)
+    int vp_x_local;          // this rank ran the last layer: its slice reads m.x
+    const float *vp_W;       // the classifier rows of this rank (row vp_row0 first)
+    const unsigned char *cls_box;    // this rank's classifier mailbox: MailboxHeader, x[dim], KeySlot[vp_ranks]
+    unsigned char *cls_out[PTC_VP_MAX_RANKS];  // the last layer rank: mailboxes the final x goes to
+    int n_cls_out;
+    KeySlot *key_out[2];     // the combining ranks' key slots (slot vp_rank is this rank's)
+    int n_key_out;
+    unsigned *cls_sent;      // final residuals this rank has sent
+    unsigned *key_sent;      // keys this rank has sent (once per position, to every combining rank)
 };
 
 constexpr int TRACE_POS = 16;

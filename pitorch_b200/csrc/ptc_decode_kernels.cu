@@ -159,8 +159,8 @@ __device__ __forceinline__ void stage_vec_cv(float4 *s_x4, const float *src, int
 // word is set (the host turns it into the reference's -1) and later waits on
 // the broken link return at once; the kernel then computes on whatever the
 // mailbox holds, and reaches all of its barriers.
-__device__ __forceinline__ void link_poll(const DecodeModel &m, unsigned want, int pos) {
-    const MailboxHeader *h = reinterpret_cast<const MailboxHeader *>(m.in_box);
+__device__ __forceinline__ void box_poll(const DecodeModel &m, const unsigned char *box, unsigned want, int pos) {
+    const MailboxHeader *h = reinterpret_cast<const MailboxHeader *>(box);
     if (*reinterpret_cast<volatile int *>(m.link_err)) return;
     const unsigned long long t0 = globaltimer_ns();
     while ((int)(ld_acquire_sys(&h->seq) - want) < 0) {
@@ -173,8 +173,52 @@ __device__ __forceinline__ void link_poll(const DecodeModel &m, unsigned want, i
     if (__ldcv(&h->pos) != pos) atomicExch(m.link_err, 2);
 }
 
+__device__ __forceinline__ void link_poll(const DecodeModel &m, unsigned want, int pos) {
+    box_poll(m, m.in_box, want, pos);
+}
+
 __device__ __forceinline__ const float *mailbox_x(const unsigned char *box) {
     return reinterpret_cast<const float *>(box + sizeof(MailboxHeader));
+}
+
+// Vocab-parallel classifier, thread 0 of the last CTA: send this rank's key
+// for position p to the combining ranks (peer stores of the slot, then its
+// sequence number with release semantics at system scope); a combining rank
+// then waits for every other rank's key of p -- bounded like box_poll -- and
+// returns the max over all ranks' keys, i.e. the argmax over the whole
+// vocabulary with the single-GPU tie order (keys carry global row indices).
+__device__ __forceinline__ unsigned long long vp_exchange(const DecodeModel &m, unsigned long long key, int p) {
+    if (m.n_key_out) {
+        const unsigned sq = *m.key_sent + 1;
+        *m.key_sent = sq;
+        for (int j = 0; j < m.n_key_out; j++) {
+            KeySlot *ks = m.key_out[j] + m.vp_rank;
+            ks->key = key;
+            ks->pos = p;
+        }
+        __threadfence_system();
+        for (int j = 0; j < m.n_key_out; j++) st_release_sys(&(m.key_out[j] + m.vp_rank)->seq, sq);
+    }
+    if (!m.vp_combine) return key;
+    const KeySlot *slots = reinterpret_cast<const KeySlot *>(m.cls_box + sizeof(MailboxHeader) + (size_t)m.dim * 4);
+    const unsigned want = m.step->key_recvd + m.tok_off + 1;
+    if (*reinterpret_cast<volatile int *>(m.link_err)) return key;
+    const unsigned long long t0 = globaltimer_ns();
+    for (int q = 0; q < m.vp_ranks; q++) {
+        if (q == m.vp_rank) continue;
+        const KeySlot *ks = slots + q;
+        while ((int)(ld_acquire_sys(&ks->seq) - want) < 0) {
+            if (globaltimer_ns() - t0 > m.link_timeout_ns) {
+                atomicExch(m.link_err, 1);
+                return key;
+            }
+            __nanosleep(32);
+        }
+        if (__ldcv(&ks->pos) != p) atomicExch(m.link_err, 2);
+        const unsigned long long kq = __ldcv(&ks->key);
+        key = kq > key ? kq : key;
+    }
+    return key;
 }
 
 // Bytes of the shared-memory copy of an n-float vector (128-byte multiple).
@@ -448,6 +492,10 @@ struct MvArgs {
     int *host_next;    // MV_CLS: pinned host word that also receives the argmax (null: none)
     int recv;          // MV_CLS: x from this rank's mailbox (pipeline head rank)
     int send_next;     // MV_CLS, device loop: the next token's embedding row to the next stage
+    int vp;            // MV_CLS: this rank's rows of a vocab-parallel classifier (link form)
+    int row0;          // MV_CLS: global index of the first row (vocab-parallel slice)
+    int vp_cls;        // MV_CLS: x from this rank's classifier mailbox (vocab-parallel)
+    int adv_recvd;     // MV_CLS, last position of a graph: this stage's layers took one message per position
 };
 
 template <int MODE>
@@ -529,10 +577,12 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     float4 xr[NV], gr[NV];
     int pos = 0;
     constexpr bool tr = MODE == MV_CLS && TR;
-    const int tpos = (tr || (MODE == MV_CLS && a.recv)) ? __ldcg(&m.step->pos) + m.tok_off : 0;
+    const int tpos = (tr || (MODE == MV_CLS && (a.recv || a.vp_cls))) ? __ldcg(&m.step->pos) + m.tok_off : 0;
     // the link's message for this position (read before the wait: only the
     // last kernel of a graph moves the count on)
-    const unsigned want = (MODE == MV_CLS && a.recv) ? __ldcg(&m.step->recvd) + m.tok_off + 1 : 0u;
+    const unsigned want = (MODE == MV_CLS && a.recv)     ? __ldcg(&m.step->recvd) + m.tok_off + 1
+                          : (MODE == MV_CLS && a.vp_cls) ? __ldcg(&m.step->cls_recvd) + m.tok_off + 1
+                                                         : 0u;
     trace_ev(m, tr, tpos, 2 * m.L, 0);
     const bool early = MODE == MV_QKV && a.from_embedding && m.tok_off == 0;
     if (MODE == MV_QKV) {
@@ -557,10 +607,11 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         }
     }
     if (MODE == MV_CLS) {
-        if (a.recv) {   // pipeline head rank: x is the last layer rank's message
-            if (tid == 0) link_poll(m, want, tpos);
+        if (a.recv || a.vp_cls) {   // pipeline: x is the last layer rank's message
+            const unsigned char *box = a.recv ? m.in_box : m.cls_box;
+            if (tid == 0) box_poll(m, box, want, tpos);
             __syncthreads();
-            const float4 *b4 = reinterpret_cast<const float4 *>(mailbox_x(m.in_box));
+            const float4 *b4 = reinterpret_cast<const float4 *>(mailbox_x(box));
 #pragma unroll
             for (int v = 0; v < NV; v++) {
                 const int c = lane + 32 * v;
@@ -636,8 +687,8 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
         } else {
             const float v = smem_row_dot<NV>(stage + (size_t)li * a.cols, xr, c4, lane);
             if (lane == 0) {
-                m.logits[i] = v;
-                const unsigned long long key = argmax_key(v, i);
+                m.logits[a.row0 + i] = v;
+                const unsigned long long key = argmax_key(v, a.row0 + i);
                 if (key > best) best = key;
             }
         }
@@ -709,27 +760,39 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
     if (!s_last) return;
     __shared__ int s_send_tok, s_send_pos;
     if (tid == 0) {
-        const unsigned long long key = __ldcg(&st->amax);
-        const int next = argmax_key_index(key);
-        st->next = next;
-        if (a.host_next) {   // straight into the host's pinned word: no copy node after the kernel
-            // -1 sends the host to the error word, so a token computed after an
-            // expired wait is never returned as valid
-            *reinterpret_cast<volatile int *>(a.host_next) = err_seen ? -1 : next;
-        }
+        unsigned long long key = __ldcg(&st->amax);
+        const int p = st->pos + m.tok_off;
         st->amax = 0ull;
         st->done = 0u;
-        const int p = st->pos + m.tok_off;
+        // vocab-parallel: this rank's key out, and on a combining rank the
+        // max over every rank's key in
+        if (a.vp) key = vp_exchange(m, key, p);
         int send_tok = -1;
-        if (st->mode == 1 && p < m.seq) {
-            int t = next;
-            if (p + 1 < st->n_prompt) t = st->tokens[p + 1];
-            else st->tokens[p + 1] = next;
-            st->tok = t;
-            if (m.adv) st->pos = p + 1;
-            if (a.send_next && p + 1 < st->stop) send_tok = t;
+        if (!a.vp || m.vp_combine) {
+            const int next = argmax_key_index(key);
+            st->next = next;
+            if (a.host_next) {   // straight into the host's pinned word: no copy node after the kernel
+                // -1 sends the host to the error word, so a token computed after an
+                // expired wait is never returned as valid
+                *reinterpret_cast<volatile int *>(a.host_next) = err_seen ? -1 : next;
+            }
+            if (st->mode == 1 && p < m.seq) {
+                int t = next;
+                if (p + 1 < st->n_prompt) t = st->tokens[p + 1];
+                else st->tokens[p + 1] = next;
+                st->tok = t;
+                if (m.adv) st->pos = p + 1;
+                if (a.send_next && p + 1 < st->stop) send_tok = t;
+            }
         }
-        if (a.recv && m.adv) st->recvd = st->recvd + m.tok_off + 1;
+        if (m.adv) {
+            // every rank of a vocab-parallel split keeps its own position; the
+            // message counts move on by the positions of this graph
+            if (a.vp) st->pos = p + 1;
+            if (a.recv || a.adv_recvd) st->recvd = st->recvd + m.tok_off + 1;
+            if (a.vp_cls) st->cls_recvd = st->cls_recvd + m.tok_off + 1;
+            if (a.vp && m.vp_combine) st->key_recvd = st->key_recvd + m.tok_off + 1;
+        }
         s_send_tok = send_tok;
         s_send_pos = p + 1;
     }
@@ -763,20 +826,30 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
 // into the next stage's mailbox with peer stores, published after a
 // system-scope fence. The last position of a stage graph (adv) then moves
 // the rank's own position and message count on.
+// With the vocab-parallel classifier the last layer rank sends its output to
+// every other rank's classifier mailbox instead (the ranks' own classifiers
+// then move the positions and counts on).
 __global__ void k_stage_send(DecodeModel m) {
     const int pos = __ldcg(&m.step->pos) + m.tok_off;
-    MailboxHeader *oh = reinterpret_cast<MailboxHeader *>(m.out_box);
-    float4 *ox = reinterpret_cast<float4 *>(m.out_box + sizeof(MailboxHeader));
+    const bool bcast = m.vp_rows && m.n_cls_out;   // (stage graphs only: link form)
+    const int n_out = bcast ? m.n_cls_out : 1;
     const float4 *x4 = reinterpret_cast<const float4 *>(m.x);
-    for (int i = threadIdx.x; i < m.dim / 4; i += blockDim.x) ox[i] = __ldcg(x4 + i);
-    if (threadIdx.x == 0) oh->pos = pos;
+    for (int i = threadIdx.x; i < m.dim / 4; i += blockDim.x) {
+        const float4 v = __ldcg(x4 + i);
+        for (int j = 0; j < n_out; j++)
+            reinterpret_cast<float4 *>((bcast ? m.cls_out[j] : m.out_box) + sizeof(MailboxHeader))[i] = v;
+    }
+    if (threadIdx.x < n_out)
+        reinterpret_cast<MailboxHeader *>(bcast ? m.cls_out[threadIdx.x] : m.out_box)->pos = pos;
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-        const unsigned sq = *m.link_sent + 1;
-        *m.link_sent = sq;
-        st_release_sys(&oh->seq, sq);
-        if (m.adv) {
+        unsigned *ctr = bcast ? m.cls_sent : m.link_sent;
+        const unsigned sq = *ctr + 1;
+        *ctr = sq;
+        for (int j = 0; j < n_out; j++)
+            st_release_sys(&reinterpret_cast<MailboxHeader *>(bcast ? m.cls_out[j] : m.out_box)->seq, sq);
+        if (m.adv && !m.vp_rows) {
             m.step->pos = pos + 1;
             m.step->recvd = m.step->recvd + m.tok_off + 1;
         }
@@ -1584,16 +1657,21 @@ void launch_layers(const DecodeModel &m, int l0, int l1, bool from_embedding, in
             x_in = (l == l0) ? m.x : m.xo + (size_t)(l - 1) * m.dim;
             x_out = (l == l1 - 1) ? m.x : m.xo + (size_t)l * m.dim;
         }
-        launch_layer(m, l, from_embedding && l == 0, x_in, x_out, n_sm, s, m.link_mode && l == l0);
+        launch_layer(m, l, from_embedding && l == 0, x_in, x_out, n_sm, s, m.link_mode && m.link_recv && l == l0);
     }
 }
 
 void launch_head(const DecodeModel &m, int n_sm, cudaStream_t s, int *host_next) {
-    MvArgs a = mv_args(m.V, m.dim, 1, 0);
-    a.W = m.wcls;
+    const bool vp = m.link_mode && m.vp_rows > 0;
+    MvArgs a = mv_args(vp ? m.vp_rows : m.V, m.dim, 1, 0);
+    a.W = vp ? m.vp_W : m.wcls;
+    a.row0 = vp ? m.vp_row0 : 0;
     a.host_next = host_next;
-    a.recv = m.link_mode ? 1 : 0;
-    a.send_next = m.link_mode ? 1 : 0;
+    a.recv = m.link_mode && !vp ? 1 : 0;
+    a.send_next = m.link_mode && !vp ? 1 : 0;
+    a.vp = vp ? 1 : 0;
+    a.vp_cls = vp && !m.vp_x_local ? 1 : 0;
+    a.adv_recvd = vp && m.L > 0 && m.link_recv ? 1 : 0;
     PTC_NV_SWITCH(nv_of(m.dim), (launch_mv<NV, MV_CLS>(m, a, n_sm, s)));
 }
 

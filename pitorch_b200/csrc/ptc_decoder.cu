@@ -53,7 +53,11 @@ constexpr int STAGE_POS = 8;
 // and the send of its output; the embedding+head rank's classifier (waits for
 // its mailbox, sends the next embedding row). The k-th position decodes
 // step->pos + k and expects message step->recvd + k + 1; only the last one
-// moves both on.
+// moves both on. With the vocab-parallel classifier every rank also runs its
+// classifier rows after its layers (rank 0's first layer reads the token's
+// embedding row instead of a message, the last layer rank sends its output
+// to every rank's classifier mailbox), and the classifiers move the
+// positions and counts on.
 static void enqueue_stage_kernels(ptc_decoder *d, int n, cudaStream_t s) {
     for (int k = 0; k < n; k++) {
         DecodeModel mk = d->m;
@@ -61,8 +65,9 @@ static void enqueue_stage_kernels(ptc_decoder *d, int n, cudaStream_t s) {
         mk.tok_off = k;
         mk.adv = k == n - 1;
         if (mk.L > 0) {
-            ptc::launch_layers(mk, 0, mk.L, false, d->n_sm, s);
+            ptc::launch_layers(mk, 0, mk.L, mk.vp_rows > 0 && !mk.link_recv, d->n_sm, s);
             ptc::launch_stage_send(mk, s);
+            if (mk.vp_rows > 0) ptc::launch_head(mk, d->n_sm, s);
         } else {
             ptc::launch_head(mk, d->n_sm, s);
         }
@@ -164,6 +169,7 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
     ptc_decoder *d = new ptc_decoder();
     memset(&d->m, 0, sizeof(d->m));
     d->m.adv = 1;   // every single-token launch advances the device position
+    d->m.link_recv = 1;   // a linked layer rank takes its input from its mailbox
     d->ctx = c;
     d->stream = ptc_ctx_stream(c);
     d->has_embed = has_embed;
@@ -378,7 +384,9 @@ extern "C" float *ptc_decoder_x_dev(ptc_decoder *d) { return d->m.x; }
 extern "C" float *ptc_decoder_logits_dev(ptc_decoder *d) { return d->m.logits; }
 
 extern "C" void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, int n_prompt) {
-    if (!d->has_embed || !d->has_head) PTC_FATAL("device-loop decode needs embedding and head");
+    // (a combining rank of a vocab-parallel classifier selects tokens too)
+    if ((!d->has_embed || !d->has_head) && !(d->m.vp_rows > 0 && d->m.vp_combine))
+        PTC_FATAL("device-loop decode needs embedding and head");
     if (n_prompt < 1 || n_prompt > d->m.seq) PTC_FATAL("prompt length %d outside [1, %d]", n_prompt, d->m.seq);
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= d->m.V) PTC_FATAL("prompt token %d outside [0, %d)", prompt[i], d->m.V);
@@ -486,7 +494,7 @@ extern "C" void ptc_decoder_enqueue_kernel(ptc_decoder *d, int kind, int l, int 
 extern "C" int ptc_decoder_launches_per_step(ptc_decoder *d) {
     const ptc::DecodeModel &m = d->m;
     const int per_layer = m.fused_attn ? 2 : m.fused_ffn ? 4 : 5;
-    return per_layer * m.L + (d->has_head ? 1 : 0) + (d->has_embed && m.L == 0 ? 1 : 0);
+    return per_layer * m.L + (d->has_head || m.vp_rows > 0 ? 1 : 0) + (d->has_embed && m.L == 0 ? 1 : 0);
 }
 
 extern "C" void ptc_decoder_enqueue_embed_dev(ptc_decoder *d) {
@@ -508,6 +516,57 @@ extern "C" void ptc_decoder_set_links(ptc_decoder *d, const void *in_box, void *
     d->m.link_err = err;
     d->m.link_timeout_ns = (unsigned long long)(timeout_ns > 0 ? timeout_ns : 0);
     capture_graphs(d);
+}
+
+extern "C" void ptc_decoder_set_vocab_parallel(ptc_decoder *d, const ptc_vocab_split *vp) {
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+    DecodeModel &m = d->m;
+    if (!vp) {
+        m.vp_rows = 0;
+        m.n_cls_out = m.n_key_out = 0;
+        m.link_recv = 1;
+        capture_graphs(d);
+        return;
+    }
+    if (!m.in_box) PTC_FATAL("the vocab-parallel classifier needs pipeline links (ptc_decoder_set_links)");
+    if (vp->ranks < 2 || vp->ranks > PTC_VP_MAX_RANKS || vp->rank < 0 || vp->rank >= vp->ranks)
+        PTC_FATAL("vocab-parallel rank %d of %d (2 to %d ranks)", vp->rank, vp->ranks, PTC_VP_MAX_RANKS);
+    if (vp->rows < 1 || vp->row0 < 0 || vp->row0 + vp->rows > m.V)
+        PTC_FATAL("vocab-parallel rows [%d, %d) outside [0, %d)", vp->row0, vp->row0 + vp->rows, m.V);
+    if (!vp->cls_rows || !vp->rms_final || !vp->box || !vp->sent) PTC_FATAL("vocab-parallel split without weights or mailbox");
+    if (vp->embed_local && (!vp->embedding || m.L == 0))
+        PTC_FATAL("a vocab-parallel rank that embeds needs the table and the first layers");
+    if (vp->n_x_out < 0 || vp->n_x_out > PTC_VP_MAX_RANKS || vp->n_key_out < 0 || vp->n_key_out > 2)
+        PTC_FATAL("vocab-parallel targets: %d residual, %d key", vp->n_x_out, vp->n_key_out);
+    if (vp->x_local != (vp->n_x_out > 0)) PTC_FATAL("the last layer rank (x_local) sends the final residual");
+    m.vp_row0 = vp->row0;
+    m.vp_rows = vp->rows;
+    m.vp_ranks = vp->ranks;
+    m.vp_rank = vp->rank;
+    m.vp_combine = vp->combine ? 1 : 0;
+    m.vp_x_local = vp->x_local ? 1 : 0;
+    m.vp_W = vp->cls_rows;
+    m.rms_final = vp->rms_final;
+    if (vp->embed_local) m.emb = vp->embedding;
+    m.link_recv = vp->embed_local ? 0 : 1;
+    m.cls_box = (const unsigned char *)vp->box;
+    m.n_cls_out = vp->n_x_out;
+    for (int j = 0; j < vp->n_x_out; j++) m.cls_out[j] = (unsigned char *)vp->x_out[j];
+    m.n_key_out = vp->n_key_out;
+    for (int j = 0; j < vp->n_key_out; j++)
+        m.key_out[j] = reinterpret_cast<ptc::KeySlot *>((unsigned char *)vp->key_out[j] + sizeof(ptc::MailboxHeader) +
+                                                        (size_t)m.dim * 4);
+    m.cls_sent = vp->sent;
+    m.key_sent = vp->sent + 1;
+    capture_graphs(d);
+}
+
+extern "C" void ptc_decoder_set_input(ptc_decoder *d, int pos, const int *tok_dev) {
+    if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
+    set_mode(d, 0);
+    put_step_int(d, &d->m.step->pos, pos);
+    if (tok_dev)
+        PTC_CHECK(cudaMemcpyAsync(&d->m.step->tok, tok_dev, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
 }
 
 extern "C" void ptc_decoder_set_stop(ptc_decoder *d, int n_pos) {

@@ -12,6 +12,11 @@ the others split the 12 layers), joins the ring (NCCL over NVLink) and runs
   e2e    pt_dist_forward_step per position (host token in, host token out
          on the head rank), the reference's per-token API.
 
+After those, the same two measurements with the vocab-parallel classifier
+(pt_dist_vocab_parallel: every rank computes 1/N of the classifier rows and
+the argmax is combined on the GPUs; a departure from the reference's ring
+topology, reported separately under "vocab_parallel").
+
 Batch-1 decode cannot overlap positions (each token depends on the previous
 argmax), so the pipeline splits weights across GPUs without adding
 throughput; every N runs the same full decode (fixed total work: "strong"
@@ -32,6 +37,7 @@ def run(args, rank, world):
     # bench's JSON line
     os.environ["NCCL_DEBUG"] = "INFO"
     os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")   # stdout carries only the JSON line
     import ctypes as C
 
     import pitorch_b200
@@ -54,35 +60,37 @@ def run(args, rank, world):
     pc = pipe.ctx.ptc_ctx()
     timer = L.ptc_timer_create(pc)
 
-    for _ in range(args.warmup):
-        pipe.generate_greedy(prompt, seq)
-    ms = 0.0
-    toks = None
-    with _bench.ClockSampler(local) as clk:
+    def measure():
+        """Device-loop decodes (timed, max over ranks), one host-driven decode
+        (e2e), and the head's stream against the reference fixture."""
+        for _ in range(args.warmup):
+            pipe.generate_greedy(prompt, seq)
+        ms = 0.0
+        toks = None
         for _ in range(args.steps):
             L.ptc_sync(pc)
             L.ptc_timer_start(timer)
             toks = pipe.generate_greedy(prompt, seq)
             L.ptc_timer_stop(timer)
             ms += L.ptc_timer_ms(timer)
-    ms_step = pipe.max_over_ranks(ms / args.steps)
-    value = seq / (ms_step / 1000.0)
+        ms_step = pipe.max_over_ranks(ms / args.steps)
+        pipe.ctx.ctx.sync_logits = 0
+        t0 = time.perf_counter()
+        L.ptc_timer_start(timer)
+        host_toks = pipe.decode_greedy(prompt, seq)
+        L.ptc_timer_stop(timer)
+        e2e_ms = pipe.max_over_ranks(L.ptc_timer_ms(timer))
+        e2e_wall = pipe.max_over_ranks(1000 * (time.perf_counter() - t0))
+        same = bool(np.array_equal(toks, host_toks)) if pipe.is_head else True
+        same = pipe.max_over_ranks(0.0 if same else 1.0) == 0.0
+        par = _bench.stream_parity(toks, seq) if pipe.is_head else {}
+        matched = pipe.max_over_ranks(float(par.get("matched_positions", 0)))
+        par_ok = pipe.max_over_ranks(1.0 if par.get("equal_up_to_first_near_tie") else 0.0) == 1.0
+        return ms_step, e2e_ms, e2e_wall, same, matched, par_ok
 
-    pipe.ctx.ctx.sync_logits = 0
-    t0 = time.perf_counter()
-    L.ptc_timer_start(timer)
-    host_toks = pipe.decode_greedy(prompt, seq)
-    L.ptc_timer_stop(timer)
-    e2e_ms = pipe.max_over_ranks(L.ptc_timer_ms(timer))
-    e2e_wall = pipe.max_over_ranks(1000 * (time.perf_counter() - t0))
-    same = True
-    if pipe.is_head:
-        same = bool(np.array_equal(toks, host_toks))
-    same = pipe.max_over_ranks(0.0 if same else 1.0) == 0.0
-    # the head rank's stream against the reference's 1024-position fixture
-    par = _bench.stream_parity(toks, seq) if pipe.is_head else {}
-    matched = pipe.max_over_ranks(float(par.get("matched_positions", 0)))
-    par_ok = pipe.max_over_ranks(1.0 if par.get("equal_up_to_first_near_tie") else 0.0) == 1.0
+    with _bench.ClockSampler(local) as clk:
+        ms_step, e2e_ms, e2e_wall, same, matched, par_ok = measure()
+    value = seq / (ms_step / 1000.0)
 
     dim, hidden, nl, nh, nkv, V, _ = cfg
     # kernels per position over all ranks: the layer kernels of every layer
@@ -93,11 +101,15 @@ def run(args, rank, world):
     per_layer = (L.ptc_decoder_launches_per_step(dec) - (1 if pipe.is_head else 0)) // n_local if n_local else 0
     per_layer = int(pipe.max_over_ranks(float(per_layer)))
     p2p = L.pt_dist_transport(C.byref(pipe.dist)) == 1
-    # plus, with the NVLink hop transport, one send and one receive kernel per rank
-    launches = seq * (per_layer * nl + 2 + (2 * world if p2p else 0))
+    # per position: the layer kernels, the head's classifier and, with the
+    # NVLink hops, one send kernel per layer rank (the receives and the next
+    # embedding row are inside the decode kernels); with NCCL hops the head's
+    # embedding kernel (NCCL's own kernels are not counted)
+    launches = seq * (per_layer * nl + 1 + ((world - 1) if p2p else 1))
     hbm, src = _bench.peaks()
     mean_bytes = float(np.mean([_bench.decode_bytes_per_token(cfg, p) for p in range(seq)]))
     step_gbs = mean_bytes * seq / (ms_step / 1000.0) / 1e9
+    line = None
     if rank == 0:
         line = {
             "metric": "batch-1 decode tokens/s (stories110M shape)", "value": value, "unit": "tokens/s",
@@ -129,6 +141,25 @@ def run(args, rank, world):
                        "compared": "the head rank's token stream of the last timed step",
                        "matched_positions": int(matched), "equal_up_to_first_near_tie": bool(par_ok)},
         }
+    # the same decode with the classifier split over all ranks
+    vp = None
+    if not getattr(args, "no_vocab_parallel", False):
+        pipe.vocab_parallel()
+        with _bench.ClockSampler(local) as vclk:
+            v_ms, v_e2e_ms, v_wall, v_same, v_matched, v_ok = measure()
+        v_gbs = mean_bytes * seq / (v_ms / 1000.0) / 1e9
+        vp = {"value": seq / (v_ms / 1000.0), "unit": "tokens/s", "ms_per_step": v_ms,
+              "parallelism": f"pp{world}, classifier rows split over all {world} ranks, argmax combined on the GPUs",
+              "e2e": {"value": seq / (v_e2e_ms / 1000.0), "unit": "tokens/s",
+                      "api": "pt_dist_forward_step per position", "wall_ms_per_step": v_wall,
+                      "token_stream_equals_device_loop": v_same},
+              "gpu_launches": args.steps * seq * (per_layer * nl + world + (world - 1)),
+              "step_roofline": {"achieved": v_gbs, "peak": hbm, "unit": "GB/s", "frac": v_gbs / hbm},
+              "clocks": vclk.summary(),
+              "parity": {"fixture": "tests/golden/decode_stories110M_long.npz (reference host C)",
+                         "matched_positions": int(v_matched), "equal_up_to_first_near_tie": bool(v_ok)}}
+    if rank == 0:
+        line["vocab_parallel"] = vp
         print(json.dumps(line), flush=True)
     L.ptc_timer_destroy(timer)
     pipe.close()

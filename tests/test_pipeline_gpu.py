@@ -52,6 +52,18 @@ def _worker(rank, world, port, task, q):
             host = pipe.decode_greedy(g["prompt"], n)
             q.put((rank, pipe.is_head, dev.tolist(), host.tolist()))
             pipe.close()
+        elif kind == "decode_vp":   # the classifier split over all ranks
+            g = golden(f"decode_{name}.npz")
+            n = int(g["n_pos"])
+            pipe = api.Pipeline(blob, rank, world, device=rank)
+            pipe.vocab_parallel()
+            dev = pipe.generate_greedy(g["prompt"], n)
+            rows = tuple(int(r) for r in g["rows"] if r < n)
+            host, kept = pipe.decode_greedy(g["prompt"], n, logit_rows=rows)
+            again = pipe.generate_greedy(g["prompt"], n)   # a second decode on the same links
+            q.put((rank, pipe.is_head, dev.tolist(),
+                   (host.tolist(), {k: v.tolist() for k, v in kept.items()}, again.tolist())))
+            pipe.close()
         elif kind == "train":
             g = golden(f"train_{name}.npz")
             T = int(g["T"])
@@ -110,6 +122,31 @@ def test_pipeline_decode_matches_reference(ptlib, name, world, transport):
     _, _, dev, host = head[0]
     assert np.array_equal(np.array(dev), g["tokens"][:n])
     assert np.array_equal(np.array(host), g["tokens"][:n])
+
+
+@pytest.mark.parametrize("name,world", [("tiny", 2), ("stories15M", 2), ("stories15M", 4), ("stories110M", 4),
+                                        ("stories110M", 8)])
+def test_pipeline_vocab_parallel_matches_reference(ptlib, name, world):
+    """The classifier split over all ranks (pt_dist_vocab_parallel): each
+    rank's rows, the argmax combined across ranks on the GPU. The token
+    streams of the device loop, of host-driven steps and of a second decode
+    equal the reference's, and the host logits the head gathers match the
+    reference's rows within 1e-4 of their max."""
+    if n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = run_ranks(world, (name, "decode_vp"))
+    g = golden(f"decode_{name}.npz")
+    n = int(g["n_pos"])
+    head = [o for o in out if o[1]]
+    assert len(head) == 1
+    _, _, dev, (host, kept, again) = head[0]
+    assert np.array_equal(np.array(dev), g["tokens"][:n])
+    assert np.array_equal(np.array(host), g["tokens"][:n])
+    assert np.array_equal(np.array(again), g["tokens"][:n])
+    for r, row in zip(g["rows"], g["logits_rows"]):
+        if r < n:
+            got = np.array(kept[int(r)], dtype=np.float64)
+            assert np.abs(got - row).max() <= 1e-4 * np.abs(row).max(), int(r)
 
 
 @pytest.mark.parametrize("world", [2, 4])
