@@ -303,16 +303,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) k_attn(DecodeModel m, int l) {
 #pragma unroll
     for (int i = 0; i < QK; i++) {
         const int cc = sub + 4 * i;
-        kv[i] = (cc < hd4 && js < n && js != jcur) ? __ldcg(kb + (size_t)js * hd4 + cc)
-                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        kv[i] = (cc < hd4 && js < n && js < jcur - 1) ? __ldcg(kb + (size_t)js * hd4 + cc)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int k = 0; k < VP; k++) {
         const int j = grp + ngrp * k;
-        vpre[k] = (grp < ngrp && j < n && j != jcur) ? __ldcg(vb + (size_t)j * hd4 + d4)
-                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        vpre[k] = (grp < ngrp && j < n && j < jcur - 1) ? __ldcg(vb + (size_t)j * hd4 + d4)
+                                                        : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     pdl_wait();
+    // the row of pos - 1 (written by the previous position's kernels, which
+    // a short chain of programmatic launches may not have finished when this
+    // kernel starts) is read after the wait, with the row of pos
+#pragma unroll
+    for (int i = 0; i < QK; i++) {
+        const int cc = sub + 4 * i;
+        if (cc < hd4 && js == jcur - 1 && js >= 0) kv[i] = __ldcg(kb + (size_t)js * hd4 + cc);
+    }
+#pragma unroll
+    for (int k = 0; k < VP; k++)
+        if (grp < ngrp && grp + ngrp * k == jcur - 1 && jcur >= 1) vpre[k] = __ldcg(vb + (size_t)(jcur - 1) * hd4 + d4);
     const float scale = __fdiv_rn(1.0f, pt_sqrtf((float)hd));
     float *part = m.att_part + ((size_t)h * m.n_chunks + c) * (hd + 2);
     const float4 *q4 = reinterpret_cast<const float4 *>(m.q + h * hd);
@@ -825,10 +836,18 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
 // launched without programmatic overlap, after the last layer's kernels)
 // into the next stage's mailbox with peer stores, published after a
 // system-scope fence. The last position of a stage graph (adv) then moves
-// the rank's own position and message count on.
-// With the vocab-parallel classifier the last layer rank sends its output to
-// every other rank's classifier mailbox instead (the ranks' own classifiers
-// then move the positions and counts on).
+// the rank's own position and message count on. With the vocab-parallel
+// classifier the last layer rank sends its output to every other rank's
+// classifier mailbox instead (the ranks' own classifiers then move the
+// positions and counts on).
+//
+// It must stay a full boundary: the next position's first attention block
+// reads the K/V rows of earlier positions before its griddepcontrol.wait,
+// and on a rank with one or two layers the row of the position just decoded
+// is written only a few kernels earlier. Launched programmatically (and
+// releasing its dependent at once), that block could start while the row
+// was still being written: on 8 GPUs (1-2 layers per rank) the token stream
+// then diverged at position 51.
 __global__ void k_stage_send(DecodeModel m) {
     const int pos = __ldcg(&m.step->pos) + m.tok_off;
     const bool bcast = m.vp_rows && m.n_cls_out;   // (stage graphs only: link form)
@@ -1101,8 +1120,12 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
             prefetch_l2_pol(m.vc + (head_base + tp) * hd, (unsigned)((te - tp) * hd * 4), pkk, polk);
         }
     }
-    // K/V rows of the first round's earlier positions: written by earlier
-    // tokens, so read before the wait (the row of pos comes from step 2).
+    // K/V rows of the first round's earlier positions up to pos - 2: written
+    // by earlier tokens, so read before the wait (the row of pos comes from
+    // step 2, the row of pos - 1 is read after the wait: a chain of
+    // programmatic launches only a few kernels long -- a model or pipeline
+    // stage of one or two layers -- can start this block before the previous
+    // position's attention block has written it).
     const int js = tid >> 2, sub = tid & 3;
     const int ngrp = AT_THREADS / hd4, d4 = tid % hd4, grp = tid / hd4;
     constexpr int QK = 4, VP = 4;
@@ -1114,14 +1137,14 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
 #pragma unroll
         for (int i = 0; i < QK; i++) {
             const int cc = sub + 4 * i;
-            kv[i] = (cc < hd4 && js < n0 && t0 + js != pos) ? ldcg_pol(kb + (size_t)js * hd4 + cc, pkk, polk)
-                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            kv[i] = (cc < hd4 && js < n0 && t0 + js < pos - 1) ? ldcg_pol(kb + (size_t)js * hd4 + cc, pkk, polk)
+                                                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int k = 0; k < VP; k++) {
             const int j = grp + ngrp * k;
-            vpre[k] = (grp < ngrp && j < n0 && t0 + j != pos) ? ldcg_pol(vb + (size_t)j * hd4 + d4, pkk, polk)
-                                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            vpre[k] = (grp < ngrp && j < n0 && t0 + j < pos - 1) ? ldcg_pol(vb + (size_t)j * hd4 + d4, pkk, polk)
+                                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
     float4 xr[NV], gr[NV];
@@ -1144,6 +1167,21 @@ __global__ void __launch_bounds__(AT_THREADS, 2) k_attn_fused(DecodeModel m, Att
     // ordering needed here, so the relaxed form)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
     pdl_wait();
+    {   // the row of pos - 1, if in this CTA's first round
+        const int jr = pos - 1 - t0;
+        if (jr >= 0 && jr < min(AT_ROUND, t1 - t0)) {
+            const float4 *kb = reinterpret_cast<const float4 *>(m.kc + (head_base + pos - 1) * hd);
+            const float4 *vb = reinterpret_cast<const float4 *>(m.vc + (head_base + pos - 1) * hd);
+#pragma unroll
+            for (int i = 0; i < QK; i++) {
+                const int cc = sub + 4 * i;
+                if (cc < hd4 && js == jr) kv[i] = ldcg_pol(kb + cc, pkk, polk);
+            }
+#pragma unroll
+            for (int k = 0; k < VP; k++)
+                if (grp < ngrp && grp + ngrp * k == jr) vpre[k] = ldcg_pol(vb + d4, pkk, polk);
+        }
+    }
     trace_ev(m, tr, pos, 2 * l, 1);
     if (a.recv) {   // pipeline layer rank: x is the previous stage's message
         if (tid == 0) link_poll(m, want, pos);
@@ -1464,6 +1502,7 @@ static void launch_cluster_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, 
 }
 
 __global__ void k_embed(DecodeModel m);
+
 
 template <int NV, int MODE>
 static void launch_mv(const DecodeModel &m, MvArgs a, int n_sm, cudaStream_t s) {
