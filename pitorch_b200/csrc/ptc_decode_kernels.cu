@@ -786,6 +786,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_mv(DecodeModel m, MvArgs a) {
                 // -1 sends the host to the error word, so a token computed after an
                 // expired wait is never returned as valid
                 *reinterpret_cast<volatile int *>(a.host_next) = err_seen ? -1 : next;
+                __threadfence_system();   // on its way to the host before the grid ends
             }
             if (st->mode == 1 && p < m.seq) {
                 int t = next;

@@ -12,6 +12,7 @@
 #include <stddef.h>
 #include <stdio.h>
 #include <string.h>
+#include <time.h>
 
 #include "../../include/ptc.h"
 #include "ptc_common.cuh"
@@ -344,6 +345,28 @@ extern "C" void ptc_decoder_reset(ptc_decoder *d) {
     PTC_CHECK(cudaStreamSynchronize(d->stream));
 }
 
+// io->next before the classifier of a host step has stored its token
+constexpr int NEXT_PENDING = -2;
+
+// Wait for the classifier's store into the pinned io->next (it fences after
+// the store): the token is back before the graph's completion would reach
+// the host through the stream. Bounded: after 2 s of spinning the stream is
+// synchronised instead, which reports a failed launch. Work later enqueued
+// on the stream stays ordered after the still-finishing graph.
+static void wait_next(ptc_decoder *d) {
+    volatile int *w = &d->io->next;
+    struct timespec t0, t;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for (unsigned it = 1;; it++) {
+        if (*w != NEXT_PENDING) return;
+        if ((it & 1023) == 0) {
+            clock_gettime(CLOCK_MONOTONIC, &t);
+            if ((t.tv_sec - t0.tv_sec) * 1000000000L + (t.tv_nsec - t0.tv_nsec) > 2000000000L) break;
+        }
+    }
+    PTC_CHECK(cudaStreamSynchronize(d->stream));
+}
+
 extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logits_host) {
     if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
     if (d->has_embed && (token < 0 || token >= d->m.V))
@@ -351,18 +374,24 @@ extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logit
     set_mode(d, 0);
     d->io->pos = pos;
     d->io->tok = token;
-    d->io->next = -1;   // overwritten by the classifier
+    d->io->next = d->has_head ? NEXT_PENDING : -1;   // overwritten by the classifier
     PTC_CHECK(cudaGraphLaunch(d->g_host, d->stream));
     if (logits_host && d->has_head) {
         PTC_CHECK(cudaMemcpyAsync(d->stage, d->m.logits, (size_t)d->m.V * 4, cudaMemcpyDeviceToHost,
                                   d->stream));
         PTC_CHECK(cudaStreamSynchronize(d->stream));
         memcpy(logits_host, d->stage, (size_t)d->m.V * 4);
+    } else if (d->has_head) {
+        wait_next(d);
     } else {
         PTC_CHECK(cudaStreamSynchronize(d->stream));
     }
-    if (d->io->next < 0 || d->io->next >= d->m.V) check_err(d);
-    return d->has_head ? d->io->next : -1;
+    const int next = d->io->next;
+    if (next < 0 || next >= d->m.V) {
+        PTC_CHECK(cudaStreamSynchronize(d->stream));
+        check_err(d);
+    }
+    return d->has_head ? next : -1;
 }
 
 extern "C" void ptc_decoder_set_x(ptc_decoder *d, const float *x_host) {
