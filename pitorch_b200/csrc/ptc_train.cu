@@ -576,9 +576,18 @@ struct ActSet {
 };
 constexpr int PTC_MAX_MICROBATCHES = 16;
 
+// Events of the second stream: forks after the producers of a product's
+// inputs, joins after the products. Forward (ptc_trainer_fwd_layers): k / v
+// beside q, w3 beside w1. Backward (ptc_trainer_bwd_layers): the weight
+// gradients beside the input gradients.
+enum { EV_FFN2, EV_FFN13, EV_WO, EV_QKV, EV_J_FFN2, EV_J_FFN13, EV_J_WO, EV_J_QKV,
+       EV_F_KV, EV_F_W3, EV_J_F_KV, EV_J_F_W3, N_EV };
+
 struct ptc_trainer {
     ptc_ctx *ctx;
     cudaStream_t s;
+    cudaStream_t s2;      // independent products beside those on s
+    cudaEvent_t ev[N_EV];
     int n_sm;
     int D, H, L, nh, nkv, V, seq, hd, K, maxT, T;
     int has_embed, has_head;
@@ -588,6 +597,7 @@ struct ptc_trainer {
     // backward
     float *d_res, *d_aout, *d_q, *d_k, *d_v, *d_logit, *d_xb, *d_hid, *d_hid2, *sh, *dS, *d_qpre,
         *d_kpre, *dw_rows, *partial;
+    float *partial2;      // split-K workspace of the second stream
     size_t partial_cap;
     int *tokens;
     float *loss_rows, *loss;
@@ -639,7 +649,10 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
     ptc_trainer *tr = new ptc_trainer();
     memset(tr, 0, sizeof(*tr));
     tr->ctx = c;
+    PTC_CHECK(cudaSetDevice(ptc_device(c)));
     tr->s = ptc_ctx_stream(c);
+    PTC_CHECK(cudaStreamCreateWithFlags(&tr->s2, cudaStreamNonBlocking));
+    for (int i = 0; i < N_EV; i++) PTC_CHECK(cudaEventCreateWithFlags(&tr->ev[i], cudaEventDisableTiming));
     tr->n_sm = ptc_sm_count(c);
     tr->D = cfg->dim;
     tr->H = cfg->hidden_dim;
@@ -689,6 +702,7 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
     tr->dw_rows = A(T * D);
     tr->partial_cap = 8 * T * (D > H ? D : H);
     tr->partial = A(tr->partial_cap);
+    tr->partial2 = A(tr->partial_cap);
     tr->tokens = (int *)ptc_alloc(c, T * 4);
     tr->loss_rows = A(T);
     tr->loss = A(1);
@@ -728,6 +742,9 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
 extern "C" void ptc_trainer_destroy(ptc_trainer *tr) {
     if (!tr) return;
     cudaStreamSynchronize(tr->s);
+    cudaStreamSynchronize(tr->s2);
+    for (int i = 0; i < N_EV; i++) cudaEventDestroy(tr->ev[i]);
+    cudaStreamDestroy(tr->s2);
     ptc_host_free(tr->loss_host);
     delete tr;
 }
@@ -799,6 +816,23 @@ static void run_gemm(ptc_trainer *tr, GemmArgs g) {
     ptc::gemm(g, tr->n_sm, tr->s);
 }
 
+// A weight-gradient product on the second stream, with its own split-K
+// workspace; kept on the SIMT kernel (no_alloc), whose launches own no state
+// that a product on the first stream could share.
+static void run_gemm2(ptc_trainer *tr, GemmArgs g) {
+    g.partial = tr->partial2;
+    g.partial_cap = tr->partial_cap;
+    g.no_alloc = 1;
+    ptc::gemm(g, tr->n_sm, tr->s2);
+}
+
+static void fork_to_s2(ptc_trainer *tr, int e) {
+    PTC_CHECK(cudaEventRecord(tr->ev[e], tr->s));
+    PTC_CHECK(cudaStreamWaitEvent(tr->s2, tr->ev[e], 0));
+}
+static void mark_s2(ptc_trainer *tr, int e) { PTC_CHECK(cudaEventRecord(tr->ev[e], tr->s2)); }
+static void join_s2(ptc_trainer *tr, int e) { PTC_CHECK(cudaStreamWaitEvent(tr->s, tr->ev[e], 0)); }
+
 extern "C" void ptc_trainer_set_tokens(ptc_trainer *tr, const int *tokens, int T) {
     if (T < 2 || T > tr->maxT) PTC_FATAL("T=%d outside [2, max_T=%d]", T, tr->maxT);
     if (T > tr->seq) PTC_FATAL("T=%d exceeds seq_len %d", T, tr->seq);
@@ -851,13 +885,17 @@ extern "C" void ptc_trainer_fwd_layers(ptc_trainer *tr, int l0, int l1) {
         float *rin = tr->res + LD, *rmid = tr->res_att + LD, *rout = tr->res + (size_t)(l + 1) * T * D;
         float *xa = tr->xb_att + LD, *xf = tr->xb_ffn + LD;
         ptc::k_tr_rmsnorm<<<(T + 7) / 8, 256, 0, s>>>(xa, rin, tr->w.rms_att_weight + (size_t)l * D, T, D);
-        GemmArgs g = G(T, D, D, xa, D, true, tr->w.wq + (size_t)l * D * D, D, true, tr->q + LD, D, ptc::EPI_ROPE);
+        // k and v on the second stream beside q (all read xa)
+        fork_to_s2(tr, EV_F_KV);
+        GemmArgs g = G(T, K, D, xa, D, true, tr->w.wk + (size_t)l * K * D, D, true, tr->k + LK, K, ptc::EPI_ROPE);
+        g.rope_hd = tr->hd;
+        run_gemm2(tr, g);
+        run_gemm2(tr, G(T, K, D, xa, D, true, tr->w.wv + (size_t)l * K * D, D, true, tr->v + LK, K, ptc::EPI_STORE));
+        mark_s2(tr, EV_J_F_KV);
+        g = G(T, D, D, xa, D, true, tr->w.wq + (size_t)l * D * D, D, true, tr->q + LD, D, ptc::EPI_ROPE);
         g.rope_hd = tr->hd;
         run_gemm(tr, g);
-        g = G(T, K, D, xa, D, true, tr->w.wk + (size_t)l * K * D, D, true, tr->k + LK, K, ptc::EPI_ROPE);
-        g.rope_hd = tr->hd;
-        run_gemm(tr, g);
-        run_gemm(tr, G(T, K, D, xa, D, true, tr->w.wv + (size_t)l * K * D, D, true, tr->v + LK, K, ptc::EPI_STORE));
+        join_s2(tr, EV_J_F_KV);
         if (attn_blocked(tr, T)) {
             ptc::k_tr_attn_fwd_blk<<<dim3(nh, (T + ptc::TB_R - 1) / ptc::TB_R), ptc::TB_R * 32,
                                      ptc::attn_block_smem(T, tr->hd), s>>>(
@@ -875,8 +913,12 @@ extern "C" void ptc_trainer_fwd_layers(ptc_trainer *tr, int l0, int l1) {
         g.ldr = D;
         run_gemm(tr, g);
         ptc::k_tr_rmsnorm<<<(T + 7) / 8, 256, 0, s>>>(xf, rmid, tr->w.rms_ffn_weight + (size_t)l * D, T, D);
+        // w3 on the second stream beside w1 (both read xf)
+        fork_to_s2(tr, EV_F_W3);
+        run_gemm2(tr, G(T, H, D, xf, D, true, tr->w.w3 + (size_t)l * H * D, D, true, tr->hb2 + LH, H, ptc::EPI_STORE));
+        mark_s2(tr, EV_J_F_W3);
         run_gemm(tr, G(T, H, D, xf, D, true, tr->w.w1 + (size_t)l * H * D, D, true, tr->hb + LH, H, ptc::EPI_STORE));
-        run_gemm(tr, G(T, H, D, xf, D, true, tr->w.w3 + (size_t)l * H * D, D, true, tr->hb2 + LH, H, ptc::EPI_STORE));
+        join_s2(tr, EV_J_F_W3);
         ptc::k_tr_silu_gate<<<blocks_for((size_t)T * H, 256, tr->n_sm), 256, 0, s>>>(tr->sh, tr->hb + LH,
                                                                                       tr->hb2 + LH, (size_t)T * H);
         g = G(T, D, H, tr->sh, H, true, tr->w.w2 + (size_t)l * D * H, H, true, rout, D, ptc::EPI_RESID);
@@ -941,28 +983,39 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         const float *W3 = tr->w.w3 + (size_t)l * H * D, *Wo = tr->w.wo + (size_t)l * D * D;
         const float *Wq = tr->w.wq + (size_t)l * D * D, *Wk = tr->w.wk + (size_t)l * K * D;
         const float *Wv = tr->w.wv + (size_t)l * K * D;
-        // FFN
+        // FFN. sh is the previous layer's g_w2 input: that product has been
+        // joined before this layer's first write of d_res' successor below
         ptc::k_tr_silu_gate<<<blocks_for((size_t)n * H, 256, tr->n_sm), 256, 0, s>>>(tr->sh, tr->hb + LH,
                                                                                       tr->hb2 + LH, (size_t)n * H);
+        fork_to_s2(tr, EV_FFN2);   // d_res, sh ready
+        run_gemm2(tr, G(D, H, n, tr->d_res, D, false, tr->sh, H, false, tr->g_w2 + (size_t)l * D * H, H,
+                        ptc::EPI_ACCUM));
+        mark_s2(tr, EV_J_FFN2);
+        join_s2(tr, EV_J_FFN13);   // the previous layer's g_w1 / g_w3 read d_hid, d_hid2
         run_gemm(tr, G(n, H, D, tr->d_res, D, true, W2, H, false, tr->d_hid, H, ptc::EPI_STORE));
-        run_gemm(tr, G(D, H, n, tr->d_res, D, false, tr->sh, H, false, tr->g_w2 + (size_t)l * D * H, H,
-                       ptc::EPI_ACCUM));
         ptc::k_tr_silu_bwd<<<blocks_for((size_t)n * H, 256, tr->n_sm), 256, 0, s>>>(
             tr->d_hid, tr->d_hid2, tr->hb + LH, tr->hb2 + LH, (size_t)n * H);
+        fork_to_s2(tr, EV_FFN13);   // d_hid, d_hid2 ready
+        run_gemm2(tr, G(H, D, n, tr->d_hid, H, false, tr->xb_ffn + LD, D, false, tr->g_w1 + (size_t)l * H * D, D,
+                        ptc::EPI_ACCUM));
+        run_gemm2(tr, G(H, D, n, tr->d_hid2, H, false, tr->xb_ffn + LD, D, false, tr->g_w3 + (size_t)l * H * D, D,
+                        ptc::EPI_ACCUM));
+        mark_s2(tr, EV_J_FFN13);
         run_gemm(tr, G(n, D, H, tr->d_hid, H, true, W1, D, false, tr->d_xb, D, ptc::EPI_STORE));
         run_gemm(tr, G(n, D, H, tr->d_hid2, H, true, W3, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
-        run_gemm(tr, G(H, D, n, tr->d_hid, H, false, tr->xb_ffn + LD, D, false, tr->g_w1 + (size_t)l * H * D, D,
-                       ptc::EPI_ACCUM));
-        run_gemm(tr, G(H, D, n, tr->d_hid2, H, false, tr->xb_ffn + LD, D, false, tr->g_w3 + (size_t)l * H * D, D,
-                       ptc::EPI_ACCUM));
+        join_s2(tr, EV_J_FFN2);   // g_w2 has read d_res (and sh)
         ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res_att + LD,
                                                           tr->w.rms_ffn_weight + (size_t)l * D, n, D);
         ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_ffn + (size_t)l * D, tr->dw_rows, n, D);
         // wo
+        fork_to_s2(tr, EV_WO);   // d_res of the attention half ready
+        run_gemm2(tr, G(D, D, n, tr->d_res, D, false, tr->att_out + LD, D, false, tr->g_wo + (size_t)l * D * D, D,
+                        ptc::EPI_ACCUM));
+        mark_s2(tr, EV_J_WO);
         run_gemm(tr, G(n, D, D, tr->d_res, D, true, Wo, D, false, tr->d_aout, D, ptc::EPI_STORE));
-        run_gemm(tr, G(D, D, n, tr->d_res, D, false, tr->att_out + LD, D, false, tr->g_wo + (size_t)l * D * D, D,
-                       ptc::EPI_ACCUM));
-        // attention
+        // attention (d_q, d_k, d_v, d_qpre, d_kpre are the previous layer's
+        // g_wq / g_wk / g_wv inputs)
+        join_s2(tr, EV_J_QKV);
         const float *att_l = tr->att + (size_t)l * nh * T * T;
         if (attn_blocked(tr, T)) {
             ptc::k_tr_attn_bwd_q_blk<<<dim3(nh, (n + ptc::TB_R - 1) / ptc::TB_R), ptc::TB_R * 32,
@@ -977,17 +1030,23 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
                                                               tr->d_v, T, n, nh, tr->nkv, tr->hd);
         ptc::k_tr_rope_bwd<<<blocks_for((size_t)n * D / 2, 256, tr->n_sm), 256, 0, s>>>(
             tr->d_qpre, tr->d_kpre, tr->d_q, tr->d_k, n, D, K, tr->hd);
+        const float *xa = tr->xb_att + LD;
+        fork_to_s2(tr, EV_QKV);   // d_qpre, d_kpre, d_v ready
+        run_gemm2(tr, G(D, D, n, tr->d_qpre, D, false, xa, D, false, tr->g_wq + (size_t)l * D * D, D, ptc::EPI_ACCUM));
+        run_gemm2(tr, G(K, D, n, tr->d_kpre, K, false, xa, D, false, tr->g_wk + (size_t)l * K * D, D, ptc::EPI_ACCUM));
+        run_gemm2(tr, G(K, D, n, tr->d_v, K, false, xa, D, false, tr->g_wv + (size_t)l * K * D, D, ptc::EPI_ACCUM));
+        mark_s2(tr, EV_J_QKV);
         run_gemm(tr, G(n, D, D, tr->d_qpre, D, true, Wq, D, false, tr->d_xb, D, ptc::EPI_STORE));
         run_gemm(tr, G(n, D, K, tr->d_kpre, K, true, Wk, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
         run_gemm(tr, G(n, D, K, tr->d_v, K, true, Wv, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
-        const float *xa = tr->xb_att + LD;
-        run_gemm(tr, G(D, D, n, tr->d_qpre, D, false, xa, D, false, tr->g_wq + (size_t)l * D * D, D, ptc::EPI_ACCUM));
-        run_gemm(tr, G(K, D, n, tr->d_kpre, K, false, xa, D, false, tr->g_wk + (size_t)l * K * D, D, ptc::EPI_ACCUM));
-        run_gemm(tr, G(K, D, n, tr->d_v, K, false, xa, D, false, tr->g_wv + (size_t)l * K * D, D, ptc::EPI_ACCUM));
+        join_s2(tr, EV_J_WO);   // g_wo has read d_res
         ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res + LD,
                                                           tr->w.rms_att_weight + (size_t)l * D, n, D);
         ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_att + (size_t)l * D, tr->dw_rows, n, D);
     }
+    // every weight-gradient product done before anything after the pass
+    join_s2(tr, EV_J_FFN13);
+    join_s2(tr, EV_J_QKV);
     PTC_CHECK(cudaGetLastError());
 }
 
