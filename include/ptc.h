@@ -164,6 +164,16 @@ void ptc_decoder_read_tokens(ptc_decoder *d, int *out_tokens, int n);
  * and layer / embedding launches that take them from the device (set by a
  * received message or by the previous head) instead of from the host. */
 int *ptc_decoder_pos_dev(ptc_decoder *d);
+/* Host steps of a pipeline's embedding rank with one wait per step: the
+ * position and token through the decoder's pinned block (the decoder's
+ * previous host-step work must have completed) and the embedding lookup
+ * enqueued; then the copies of the argmax, the decode kernels' error word
+ * and (logits != 0) the logits into pinned memory enqueued; and, once the
+ * caller has waited for the stream, the argmax taken (an error word aborts,
+ * as in ptc_decoder_fetch_next). */
+void ptc_decoder_enqueue_embed_at(ptc_decoder *d, int token, int pos);
+void ptc_decoder_enqueue_fetch(ptc_decoder *d, int logits);
+int ptc_decoder_take_next(ptc_decoder *d, float *logits_host);
 int *ptc_decoder_tok_dev(ptc_decoder *d);
 void ptc_decoder_enqueue_layers_devpos(ptc_decoder *d, int l_start, int l_end);
 void ptc_decoder_enqueue_embed_dev(ptc_decoder *d);

@@ -51,6 +51,7 @@ typedef struct {
     void *peer_box;       /* the successor's mailbox, mapped */
     unsigned *ctr;        /* device [0] messages sent, [1] messages received */
     int *hop_err;         /* device: a hop wait ran out */
+    int *hop_err_host;    /* pinned copy of it, fetched with each host-driven step */
     /* vocab-parallel classifier (pt_dist_vocab_parallel) */
     int vp;
     void *vp_box;                      /* this rank's classifier mailbox */
@@ -238,6 +239,8 @@ static int setup_p2p(pt_dist_t *dist, pt_context_t *ctx) {
     }
     c->ctr = (unsigned *)ptc_alloc(pc, 2 * sizeof(unsigned));
     c->hop_err = (int *)ptc_alloc(pc, sizeof(int));
+    c->hop_err_host = (int *)ptc_host_alloc(sizeof(int));
+    *c->hop_err_host = 0;
     cudaMemsetAsync(c->ctr, 0, 2 * sizeof(unsigned), s);
     cudaMemsetAsync(c->hop_err, 0, sizeof(int), s);
     c->p2p = 1;
@@ -255,6 +258,21 @@ static long long hop_timeout_ns(const pt_dist_t *dist) {
      * host's deadline still bounds the whole call) */
     const int ms = timeout_of(dist) < 60000 ? timeout_of(dist) : 60000;
     return (long long)ms * 1000000LL;
+}
+
+/* The hop error word of a host-driven step: its copy into pinned memory is
+ * enqueued with the step, so the step's one wait for the stream covers it. */
+static void hop_err_enqueue(pt_dist_t *dist, pt_context_t *ctx) {
+    dist_comm_t *c = comm_of(dist);
+    if (c->p2p)
+        cudaMemcpyAsync(c->hop_err_host, c->hop_err, sizeof(int), cudaMemcpyDeviceToHost,
+                        (cudaStream_t)ptc_stream(ctx->dev->ctx));
+}
+static int hop_err_seen(const pt_dist_t *dist) {
+    const dist_comm_t *c = (const dist_comm_t *)dist->comm;
+    const int e = c->p2p ? *(volatile int *)c->hop_err_host : 0;
+    if (e) fprintf(stderr, "R%d FAIL: decode hop wait expired\n", dist->rank);
+    return e;
 }
 
 static int hop_failed(pt_dist_t *dist, pt_context_t *ctx) {
@@ -322,6 +340,7 @@ int pt_dist_setup_ctx(pt_dist_t *dist, pt_context_t *ctx, const pt_shard_info_t 
 void pt_dist_free(pt_dist_t *dist) {
     dist_comm_t *c = comm_of(dist);
     if (!c) return;
+    if (c->hop_err_host) ptc_host_free(c->hop_err_host);
     for (int q = 0; q < PTC_VP_MAX_RANKS; q++) ptc_mailbox_close(c->vp_peer[q]);
     ptc_mailbox_free(c->vp_box);
     ptc_mailbox_close(c->peer_box);
@@ -418,8 +437,7 @@ static void enqueue_position(pt_dist_t *dist, pt_context_t *ctx, int host_token,
          * itself: in host-driven steps the token is the caller's. */
         (void)devloop;
         if (dist->has_embed && dist->has_head) {
-            cudaMemcpyAsync(pos_dev, &host_pos, 4, cudaMemcpyHostToDevice, s);
-            ptc_decoder_enqueue_embed(dec, host_token);
+            ptc_decoder_enqueue_embed_at(dec, host_token, host_pos);
             ptc_hop_send(ctx->dev->ctx, x, pos_dev, c->peer_box, c->ctr, c->dim);
         }
         ptc_decoder_enqueue_stage(dec, 1);
@@ -429,8 +447,7 @@ static void enqueue_position(pt_dist_t *dist, pt_context_t *ctx, int host_token,
         if (devloop) {
             ptc_decoder_enqueue_embed_dev(dec);
         } else {
-            cudaMemcpyAsync(pos_dev, &host_pos, 4, cudaMemcpyHostToDevice, s);
-            ptc_decoder_enqueue_embed(dec, host_token);
+            ptc_decoder_enqueue_embed_at(dec, host_token, host_pos);
         }
         cudaMemcpyAsync(c->sbuf, pos_dev, 4, cudaMemcpyDeviceToDevice, s);
         cudaMemcpyAsync(c->sbuf + 1, x, (size_t)c->dim * 4, cudaMemcpyDeviceToDevice, s);
@@ -607,10 +624,12 @@ static int vp_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token) {
     else if (dist->rank == head) ptc_decoder_set_input(dec, ctx->pos, NULL);
     ptc_decoder_enqueue_stage(dec, 1);
     if (ctx->sync_logits) vp_gather_logits(dist, ctx);
+    hop_err_enqueue(dist, ctx);
+    if (dist->rank == head) ptc_decoder_enqueue_fetch(dec, ctx->sync_logits);
     if (finish(dist, ctx, "dist forward timeout") < 0) return -1;
-    if (hop_failed(dist, ctx)) return -1;
+    if (hop_err_seen(dist)) return -1;
     int next = 0;
-    if (dist->rank == head) next = ptc_decoder_fetch_next(dec, ctx->sync_logits ? ctx->state.logits : NULL);
+    if (dist->rank == head) next = ptc_decoder_take_next(dec, ctx->sync_logits ? ctx->state.logits : NULL);
     ctx->pos++;
     return next;
 }
@@ -628,11 +647,16 @@ int pt_dist_forward_step(pt_context_t *ctx, pt_dist_t *dist, int token) {
     if (c->vp) {
         if ((next = vp_forward_step(ctx, dist, token)) < 0) return -1;
     } else {
+        /* one wait per step: the hop error word, the argmax, the kernels'
+         * error word and the logits are copied back by work enqueued with it */
         enqueue_position(dist, ctx, token, ctx->pos, 0);
+        hop_err_enqueue(dist, ctx);
+        const int head = dist->has_embed && dist->has_head;
+        if (head) ptc_decoder_enqueue_fetch(ctx->dev->dec, ctx->sync_logits);
         if (finish(dist, ctx, "dist forward recv timeout") < 0) return -1;
-        if (hop_failed(dist, ctx)) return -1;
-        if (dist->has_embed && dist->has_head) {
-            next = ptc_decoder_fetch_next(ctx->dev->dec, ctx->sync_logits ? ctx->state.logits : NULL);
+        if (hop_err_seen(dist)) return -1;
+        if (head) {
+            next = ptc_decoder_take_next(ctx->dev->dec, ctx->sync_logits ? ctx->state.logits : NULL);
             ctx->pos++;
         }
     }

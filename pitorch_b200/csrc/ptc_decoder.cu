@@ -26,7 +26,7 @@ struct HostIO {
     int pos;
     int tok;
     int next;
-    int pad;
+    int err;   // the decode kernels' error word, fetched with next
 };
 
 struct ptc_decoder {
@@ -40,6 +40,7 @@ struct ptc_decoder {
     int mode;              // current StepState.mode on the device
     cudaGraphExec_t g_host, g_dev;
     cudaGraphExec_t g_devk;  // DEV_TOKENS device-loop tokens per launch (null: not used)
+    int fetch_logits;      // ptc_decoder_enqueue_fetch copied the logits into stage
     unsigned long long *trace_buf;  // phase timeline record (m.trace while tracing)
     size_t trace_n;        // its entries
     // pipeline stage graphs (ptc_decoder_set_links): STAGE_POS positions and one
@@ -149,12 +150,16 @@ static void capture_graphs(ptc_decoder *d) {
 
 // A decode kernel whose bounded wait expired left a code in m.err; report it
 // at the next synchronisation point (the reference's panic analogue).
-static void check_err(ptc_decoder *d) {
-    int e = 0;
-    PTC_CHECK(cudaMemcpy(&e, d->m.err, sizeof(int), cudaMemcpyDeviceToHost));
+static void report_err(const ptc_decoder *d, int e) {
     if (e == ptc::ERR_POS_RANGE)
         PTC_FATAL("decode kernel reported error %d: a position at or past seq_len %d was decoded", e, d->m.seq);
     if (e) PTC_FATAL("decode kernel reported error %d (bounded wait on a weight stage expired)", e);
+}
+
+static void check_err(ptc_decoder *d) {
+    int e = 0;
+    PTC_CHECK(cudaMemcpy(&e, d->m.err, sizeof(int), cudaMemcpyDeviceToHost));
+    report_err(d, e);
 }
 
 static void set_mode(ptc_decoder *d, int mode) {
@@ -495,6 +500,36 @@ extern "C" int ptc_decoder_fetch_next(ptc_decoder *d, float *logits_host) {
     PTC_CHECK(cudaStreamSynchronize(d->stream));
     if (logits_host) memcpy(logits_host, d->stage, (size_t)d->m.V * 4);
     check_err(d);
+    return d->io->next;
+}
+
+// Host steps of the pipeline's embedding rank: position and token go through
+// the pinned io block in one copy (the previous step's copies from it have
+// completed: the pipeline step waits for its stream before returning), and
+// the argmax, the error word and the logits come back with copies enqueued
+// before the caller's single wait for the stream.
+extern "C" void ptc_decoder_enqueue_embed_at(ptc_decoder *d, int token, int pos) {
+    if (!d->has_embed) PTC_FATAL("decoder has no embedding");
+    if (token < 0 || token >= d->m.V) PTC_FATAL("token %d outside [0, %d)", token, d->m.V);
+    if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
+    set_mode(d, 0);
+    d->io->pos = pos;
+    d->io->tok = token;
+    PTC_CHECK(cudaMemcpyAsync(d->m.step, d->io, 2 * sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    ptc::launch_embed(d->m, d->stream);
+}
+
+extern "C" void ptc_decoder_enqueue_fetch(ptc_decoder *d, int logits) {
+    PTC_CHECK(cudaMemcpyAsync(&d->io->next, &d->m.step->next, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+    PTC_CHECK(cudaMemcpyAsync(&d->io->err, d->m.err, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+    d->fetch_logits = logits && d->has_head;
+    if (d->fetch_logits)
+        PTC_CHECK(cudaMemcpyAsync(d->stage, d->m.logits, (size_t)d->m.V * 4, cudaMemcpyDeviceToHost, d->stream));
+}
+
+extern "C" int ptc_decoder_take_next(ptc_decoder *d, float *logits_host) {
+    report_err(d, d->io->err);
+    if (logits_host && d->fetch_logits) memcpy(logits_host, d->stage, (size_t)d->m.V * 4);
     return d->io->next;
 }
 
