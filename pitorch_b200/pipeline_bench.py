@@ -151,8 +151,12 @@ def run(args, rank, world):
         except RuntimeError as e:
             vp = {"unavailable": str(e)}
     if vp_ok:
-        with _bench.ClockSampler(local) as vclk:
-            v_ms, v_e2e_ms, v_wall, v_same, v_matched, v_ok = measure()
+        try:   # a failed decode fails on every rank (its hops time out), before any collective
+            with _bench.ClockSampler(local) as vclk:
+                v_ms, v_e2e_ms, v_wall, v_same, v_matched, v_ok = measure()
+        except RuntimeError as e:
+            vp_ok, vp = False, {"error": str(e)}
+    if vp_ok:
         v_gbs = mean_bytes * seq / (v_ms / 1000.0) / 1e9
         vp = {"value": seq / (v_ms / 1000.0), "unit": "tokens/s", "ms_per_step": v_ms,
               "parallelism": f"pp{world}, classifier rows split over all {world} ranks, argmax combined on the GPUs",
