@@ -365,16 +365,26 @@ __global__ void k_tr_ce_backward(const float *logits, const int *tokens, int V, 
 
 // rmsnorm backward, one warp per row (pt_backward_ops.c:4-30): dx += ..., and
 // the row's weight-grad contribution d_o * x * inv into dw_rows.
-__global__ void k_tr_rmsnorm_bwd(float *dx, float *dw_rows, const float *d_o, const float *x,
-                                 const float *w, int rows, int D) {
+// d_o is the sum of up to three products computed side by side (d_o2, d_o3
+// null when absent), added here in the order in which accumulating them into
+// one buffer would have: (d_o + d_o2) + d_o3.
+__device__ __forceinline__ float sum3(const float *a, const float *b, const float *c, size_t i) {
+    float v = a[i];
+    if (b) v = __fadd_rn(v, b[i]);
+    if (c) v = __fadd_rn(v, c[i]);
+    return v;
+}
+
+__global__ void k_tr_rmsnorm_bwd(float *dx, float *dw_rows, const float *d_o, const float *d_o2, const float *d_o3,
+                                 const float *x, const float *w, int rows, int D) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     const float *xr = x + (size_t)warp * D;
-    const float *dor = d_o + (size_t)warp * D;
+    const size_t ro = (size_t)warp * D;
     float ss = 0.f, dot = 0.f;
     for (int i = lane; i < D; i += 32) {
         ss = fmaf(xr[i], xr[i], ss);
-        dot = fmaf(__fmul_rn(dor[i], w[i]), xr[i], dot);
+        dot = fmaf(__fmul_rn(sum3(d_o, d_o2, d_o3, ro + i), w[i]), xr[i], dot);
     }
     ss = warp_sum(ss);
     dot = warp_sum(dot);
@@ -383,8 +393,9 @@ __global__ void k_tr_rmsnorm_bwd(float *dx, float *dw_rows, const float *d_o, co
     float *dxr = dx + (size_t)warp * D;
     float *dwr = dw_rows + (size_t)warp * D;
     for (int i = lane; i < D; i += 32) {
-        dwr[i] = __fmul_rn(__fmul_rn(dor[i], xr[i]), inv);
-        const float a = __fmul_rn(__fmul_rn(inv, dor[i]), w[i]);
+        const float di = sum3(d_o, d_o2, d_o3, ro + i);
+        dwr[i] = __fmul_rn(__fmul_rn(di, xr[i]), inv);
+        const float a = __fmul_rn(__fmul_rn(inv, di), w[i]);
         const float b = __fmul_rn(__fmul_rn(coeff, dot), xr[i]);
         dxr[i] = __fadd_rn(dxr[i], __fsub_rn(a, b));
     }
@@ -581,12 +592,13 @@ constexpr int PTC_MAX_MICROBATCHES = 16;
 // beside q, w3 beside w1. Backward (ptc_trainer_bwd_layers): the weight
 // gradients beside the input gradients.
 enum { EV_FFN2, EV_FFN13, EV_WO, EV_QKV, EV_J_FFN2, EV_J_FFN13, EV_J_WO, EV_J_QKV,
-       EV_F_KV, EV_F_W3, EV_J_F_KV, EV_J_F_W3, N_EV };
+       EV_F_KV, EV_F_W3, EV_J_F_KV, EV_J_F_W3, EV_J_X3, EV_J_XK, EV_J_XV, N_EV };
 
 struct ptc_trainer {
     ptc_ctx *ctx;
     cudaStream_t s;
     cudaStream_t s2;      // independent products beside those on s
+    cudaStream_t s3;      // the backward's second and third input-gradient products
     cudaEvent_t ev[N_EV];
     int n_sm;
     int D, H, L, nh, nkv, V, seq, hd, K, maxT, T;
@@ -598,6 +610,8 @@ struct ptc_trainer {
     float *d_res, *d_aout, *d_q, *d_k, *d_v, *d_logit, *d_xb, *d_hid, *d_hid2, *sh, *dS, *d_qpre,
         *d_kpre, *dw_rows, *partial;
     float *partial2;      // split-K workspace of the second stream
+    float *partial3;      // ... and of the third
+    float *d_xb2, *d_xb3; // the input-gradient products computed beside d_xb
     size_t partial_cap;
     int *tokens;
     float *loss_rows, *loss;
@@ -652,6 +666,7 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
     PTC_CHECK(cudaSetDevice(ptc_device(c)));
     tr->s = ptc_ctx_stream(c);
     PTC_CHECK(cudaStreamCreateWithFlags(&tr->s2, cudaStreamNonBlocking));
+    PTC_CHECK(cudaStreamCreateWithFlags(&tr->s3, cudaStreamNonBlocking));
     for (int i = 0; i < N_EV; i++) PTC_CHECK(cudaEventCreateWithFlags(&tr->ev[i], cudaEventDisableTiming));
     tr->n_sm = ptc_sm_count(c);
     tr->D = cfg->dim;
@@ -703,6 +718,9 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
     tr->partial_cap = 8 * T * (D > H ? D : H);
     tr->partial = A(tr->partial_cap);
     tr->partial2 = A(tr->partial_cap);
+    tr->partial3 = A(tr->partial_cap);
+    tr->d_xb2 = A(T * D);
+    tr->d_xb3 = A(T * D);
     tr->tokens = (int *)ptc_alloc(c, T * 4);
     tr->loss_rows = A(T);
     tr->loss = A(1);
@@ -743,8 +761,10 @@ extern "C" void ptc_trainer_destroy(ptc_trainer *tr) {
     if (!tr) return;
     cudaStreamSynchronize(tr->s);
     cudaStreamSynchronize(tr->s2);
+    cudaStreamSynchronize(tr->s3);
     for (int i = 0; i < N_EV; i++) cudaEventDestroy(tr->ev[i]);
     cudaStreamDestroy(tr->s2);
+    cudaStreamDestroy(tr->s3);
     ptc_host_free(tr->loss_host);
     delete tr;
 }
@@ -824,6 +844,14 @@ static void run_gemm2(ptc_trainer *tr, GemmArgs g) {
     g.partial_cap = tr->partial_cap;
     g.no_alloc = 1;
     ptc::gemm(g, tr->n_sm, tr->s2);
+}
+
+// The same on the third stream (its own workspace).
+static void run_gemm3(ptc_trainer *tr, GemmArgs g) {
+    g.partial = tr->partial3;
+    g.partial_cap = tr->partial_cap;
+    g.no_alloc = 1;
+    ptc::gemm(g, tr->n_sm, tr->s3);
 }
 
 static void fork_to_s2(ptc_trainer *tr, int e) {
@@ -963,7 +991,7 @@ extern "C" void ptc_trainer_bwd_head(ptc_trainer *tr) {
     // d_xb = d_logit . Wcls   [n x D], K = V
     run_gemm(tr, G(n, D, V, tr->d_logit, V, true, tr->w.wcls, D, false, tr->d_xb, D, ptc::EPI_STORE));
     const float *rfin = tr->res + (size_t)tr->L * T * D;
-    ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, rfin,
+    ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, nullptr, nullptr, rfin,
                                                       tr->w.rms_final_weight, n, D);
     ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_final, tr->dw_rows, n, D);
     // dWcls += d_logit^T . x_final   [V x D], K = n
@@ -1001,11 +1029,16 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         run_gemm2(tr, G(H, D, n, tr->d_hid2, H, false, tr->xb_ffn + LD, D, false, tr->g_w3 + (size_t)l * H * D, D,
                         ptc::EPI_ACCUM));
         mark_s2(tr, EV_J_FFN13);
+        // d_xb = d_hid.W1 + d_hid2.W3: the second product on the third stream
+        // into its own buffer, summed in the rmsnorm backward
+        PTC_CHECK(cudaStreamWaitEvent(tr->s3, tr->ev[EV_FFN13], 0));
+        run_gemm3(tr, G(n, D, H, tr->d_hid2, H, true, W3, D, false, tr->d_xb2, D, ptc::EPI_STORE));
+        PTC_CHECK(cudaEventRecord(tr->ev[EV_J_X3], tr->s3));
         run_gemm(tr, G(n, D, H, tr->d_hid, H, true, W1, D, false, tr->d_xb, D, ptc::EPI_STORE));
-        run_gemm(tr, G(n, D, H, tr->d_hid2, H, true, W3, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
         join_s2(tr, EV_J_FFN2);   // g_w2 has read d_res (and sh)
-        ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res_att + LD,
-                                                          tr->w.rms_ffn_weight + (size_t)l * D, n, D);
+        join_s2(tr, EV_J_X3);
+        ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->d_xb2, nullptr,
+                                                          tr->res_att + LD, tr->w.rms_ffn_weight + (size_t)l * D, n, D);
         ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_ffn + (size_t)l * D, tr->dw_rows, n, D);
         // wo
         fork_to_s2(tr, EV_WO);   // d_res of the attention half ready
@@ -1031,17 +1064,25 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         ptc::k_tr_rope_bwd<<<blocks_for((size_t)n * D / 2, 256, tr->n_sm), 256, 0, s>>>(
             tr->d_qpre, tr->d_kpre, tr->d_q, tr->d_k, n, D, K, tr->hd);
         const float *xa = tr->xb_att + LD;
+        // d_xb = d_qpre.Wq + d_kpre.Wk + d_v.Wv: the k product on the third
+        // stream, the v product first on the second (then its weight
+        // gradients), each into its own buffer, summed in the rmsnorm backward
         fork_to_s2(tr, EV_QKV);   // d_qpre, d_kpre, d_v ready
+        PTC_CHECK(cudaStreamWaitEvent(tr->s3, tr->ev[EV_QKV], 0));
+        run_gemm3(tr, G(n, D, K, tr->d_kpre, K, true, Wk, D, false, tr->d_xb2, D, ptc::EPI_STORE));
+        PTC_CHECK(cudaEventRecord(tr->ev[EV_J_XK], tr->s3));
+        run_gemm2(tr, G(n, D, K, tr->d_v, K, true, Wv, D, false, tr->d_xb3, D, ptc::EPI_STORE));
+        mark_s2(tr, EV_J_XV);
         run_gemm2(tr, G(D, D, n, tr->d_qpre, D, false, xa, D, false, tr->g_wq + (size_t)l * D * D, D, ptc::EPI_ACCUM));
         run_gemm2(tr, G(K, D, n, tr->d_kpre, K, false, xa, D, false, tr->g_wk + (size_t)l * K * D, D, ptc::EPI_ACCUM));
         run_gemm2(tr, G(K, D, n, tr->d_v, K, false, xa, D, false, tr->g_wv + (size_t)l * K * D, D, ptc::EPI_ACCUM));
         mark_s2(tr, EV_J_QKV);
         run_gemm(tr, G(n, D, D, tr->d_qpre, D, true, Wq, D, false, tr->d_xb, D, ptc::EPI_STORE));
-        run_gemm(tr, G(n, D, K, tr->d_kpre, K, true, Wk, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
-        run_gemm(tr, G(n, D, K, tr->d_v, K, true, Wv, D, false, tr->d_xb, D, ptc::EPI_ACCUM));
         join_s2(tr, EV_J_WO);   // g_wo has read d_res
-        ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->res + LD,
-                                                          tr->w.rms_att_weight + (size_t)l * D, n, D);
+        join_s2(tr, EV_J_XK);
+        join_s2(tr, EV_J_XV);
+        ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->d_xb2, tr->d_xb3,
+                                                          tr->res + LD, tr->w.rms_att_weight + (size_t)l * D, n, D);
         ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_att + (size_t)l * D, tr->dw_rows, n, D);
     }
     // every weight-gradient product done before anything after the pass
