@@ -592,7 +592,7 @@ constexpr int PTC_MAX_MICROBATCHES = 16;
 // beside q, w3 beside w1. Backward (ptc_trainer_bwd_layers): the weight
 // gradients beside the input gradients.
 enum { EV_FFN2, EV_FFN13, EV_WO, EV_QKV, EV_J_FFN2, EV_J_FFN13, EV_J_WO, EV_J_QKV,
-       EV_F_KV, EV_F_W3, EV_J_F_KV, EV_J_F_W3, EV_J_X3, EV_J_XK, EV_J_XV, N_EV };
+       EV_F_KV, EV_F_W3, EV_J_F_KV, EV_J_F_W3, EV_J_X3, EV_J_XK, EV_J_XV, EV_RMS, EV_J_CS, N_EV };
 
 struct ptc_trainer {
     ptc_ctx *ctx;
@@ -1039,7 +1039,12 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         join_s2(tr, EV_J_X3);
         ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->d_xb2, nullptr,
                                                           tr->res_att + LD, tr->w.rms_ffn_weight + (size_t)l * D, n, D);
-        ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_ffn + (size_t)l * D, tr->dw_rows, n, D);
+        // the gain's column sums on the third stream (dw_rows is next written
+        // by the attention half's rmsnorm backward, after the join of that
+        // stream's k product, which follows them)
+        PTC_CHECK(cudaEventRecord(tr->ev[EV_RMS], s));
+        PTC_CHECK(cudaStreamWaitEvent(tr->s3, tr->ev[EV_RMS], 0));
+        ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, tr->s3>>>(tr->g_rms_ffn + (size_t)l * D, tr->dw_rows, n, D);
         // wo
         fork_to_s2(tr, EV_WO);   // d_res of the attention half ready
         run_gemm2(tr, G(D, D, n, tr->d_res, D, false, tr->att_out + LD, D, false, tr->g_wo + (size_t)l * D * D, D,
@@ -1083,11 +1088,17 @@ extern "C" void ptc_trainer_bwd_layers(ptc_trainer *tr, int l0, int l1) {
         join_s2(tr, EV_J_XV);
         ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, tr->d_xb2, tr->d_xb3,
                                                           tr->res + LD, tr->w.rms_att_weight + (size_t)l * D, n, D);
-        ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_att + (size_t)l * D, tr->dw_rows, n, D);
+        // (dw_rows is next written by the next layer's FFN rmsnorm backward,
+        // after the join of the third stream's d_hid2.W3 product)
+        PTC_CHECK(cudaEventRecord(tr->ev[EV_RMS], s));
+        PTC_CHECK(cudaStreamWaitEvent(tr->s3, tr->ev[EV_RMS], 0));
+        ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, tr->s3>>>(tr->g_rms_att + (size_t)l * D, tr->dw_rows, n, D);
+        PTC_CHECK(cudaEventRecord(tr->ev[EV_J_CS], tr->s3));
     }
     // every weight-gradient product done before anything after the pass
     join_s2(tr, EV_J_FFN13);
     join_s2(tr, EV_J_QKV);
+    join_s2(tr, EV_J_CS);
     PTC_CHECK(cudaGetLastError());
 }
 
