@@ -39,15 +39,20 @@ __global__ void k_tr_embed(float *res, const float *emb, const int *tokens, int 
 }
 
 // One warp per row: out = (x * s) * w, s = 1/sqrt(mean(x^2)+eps) (pt_ops.c:5-12).
-__global__ void k_tr_rmsnorm(float *out, const float *x, const float *w, int rows, int D) {
+__global__ void k_tr_rmsnorm(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w,
+                             int rows, int D) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     const float *xr = x + (size_t)warp * D;
     float ss = 0.f;
+    // unrolled so that a lane's loads are in flight together (the sums keep
+    // their order)
+#pragma unroll 8
     for (int i = lane; i < D; i += 32) ss = fmaf(xr[i], xr[i], ss);
     ss = warp_sum(ss);
     const float s = rms_scale(ss, D);
     float *o = out + (size_t)warp * D;
+#pragma unroll 8
     for (int i = lane; i < D; i += 32) o[i] = __fmul_rn(__fmul_rn(xr[i], s), w[i]);
 }
 
@@ -368,20 +373,25 @@ __global__ void k_tr_ce_backward(const float *logits, const int *tokens, int V, 
 // d_o is the sum of up to three products computed side by side (d_o2, d_o3
 // null when absent), added here in the order in which accumulating them into
 // one buffer would have: (d_o + d_o2) + d_o3.
-__device__ __forceinline__ float sum3(const float *a, const float *b, const float *c, size_t i) {
+__device__ __forceinline__ float sum3(const float *__restrict__ a, const float *__restrict__ b,
+                                      const float *__restrict__ c, size_t i) {
     float v = a[i];
     if (b) v = __fadd_rn(v, b[i]);
     if (c) v = __fadd_rn(v, c[i]);
     return v;
 }
 
-__global__ void k_tr_rmsnorm_bwd(float *dx, float *dw_rows, const float *d_o, const float *d_o2, const float *d_o3,
-                                 const float *x, const float *w, int rows, int D) {
+__global__ void k_tr_rmsnorm_bwd(float *__restrict__ dx, float *__restrict__ dw_rows, const float *__restrict__ d_o,
+                                 const float *__restrict__ d_o2, const float *__restrict__ d_o3,
+                                 const float *__restrict__ x, const float *__restrict__ w, int rows, int D) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     const float *xr = x + (size_t)warp * D;
     const size_t ro = (size_t)warp * D;
     float ss = 0.f, dot = 0.f;
+    // unrolled so that a lane's loads are in flight together (the sums keep
+    // their order)
+#pragma unroll 8
     for (int i = lane; i < D; i += 32) {
         ss = fmaf(xr[i], xr[i], ss);
         dot = fmaf(__fmul_rn(sum3(d_o, d_o2, d_o3, ro + i), w[i]), xr[i], dot);
@@ -392,6 +402,7 @@ __global__ void k_tr_rmsnorm_bwd(float *dx, float *dw_rows, const float *d_o, co
     const float coeff = __fdiv_rn(__fmul_rn(__fmul_rn(inv, inv), inv), (float)D);
     float *dxr = dx + (size_t)warp * D;
     float *dwr = dw_rows + (size_t)warp * D;
+#pragma unroll 8
     for (int i = lane; i < D; i += 32) {
         const float di = sum3(d_o, d_o2, d_o3, ro + i);
         dwr[i] = __fmul_rn(__fmul_rn(di, xr[i]), inv);
@@ -409,6 +420,7 @@ __global__ void __launch_bounds__(256) k_tr_colsum_accum(float *g, const float *
     const int i = blockIdx.x * 32 + lane;
     float acc = 0.f;
     if (i < D)
+#pragma unroll 8
         for (int t = warp; t < n_rows; t += 8) acc = __fadd_rn(acc, rows_[(size_t)t * D + i]);
     s_part[warp][lane] = acc;
     __syncthreads();
