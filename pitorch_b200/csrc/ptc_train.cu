@@ -287,11 +287,15 @@ __global__ void k_tr_silu_gate(float *sh, const float *h1, const float *h3, size
 }
 
 // Per-row cross-entropy (pt_train.c:309-325): one CTA per row t < T-1.
-__global__ void k_tr_ce_rows(const float *logits, const int *tokens, int V, float *loss_rows) {
+// Also keeps each row's max and exponential sum (row_max, row_sum) for the
+// backward, which then needs one pass over the logits instead of three.
+__global__ void k_tr_ce_rows(const float *__restrict__ logits, const int *tokens, int V, float *loss_rows,
+                             float *row_max, float *row_sum) {
     __shared__ float s_r[32];
     const int t = blockIdx.x;
-    const float *lg = logits + (size_t)t * V;
+    const float *__restrict__ lg = logits + (size_t)t * V;
     float mx = -3.4028235e+38f;
+#pragma unroll 8
     for (int v = threadIdx.x; v < V; v += blockDim.x) mx = fmaxf(mx, lg[v]);
     mx = warp_max(mx);
     if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = mx;
@@ -305,6 +309,7 @@ __global__ void k_tr_ce_rows(const float *logits, const int *tokens, int V, floa
     mx = s_r[0];
     __syncthreads();
     float sum = 0.f;
+#pragma unroll 8
     for (int v = threadIdx.x; v < V; v += blockDim.x) sum += pt_expf(__fsub_rn(lg[v], mx));
     sum = warp_sum(sum);
     if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = sum;
@@ -314,6 +319,8 @@ __global__ void k_tr_ce_rows(const float *logits, const int *tokens, int V, floa
         for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += s_r[w];
         const float tgt = lg[tokens[t + 1]];
         loss_rows[t] = -(__fsub_rn(__fsub_rn(tgt, mx), pt_logf(s)));
+        row_max[t] = mx;
+        row_sum[t] = s;
     }
 }
 
@@ -325,44 +332,22 @@ __global__ void k_tr_loss_sum(const float *loss_rows, int n, float *loss) {
     *loss = __fdiv_rn(l, (float)n);
 }
 
-// d_logit rows (pt_train.c:609-621): softmax * (1/(T-1)), minus 1/(T-1) at the target.
-__global__ void k_tr_ce_backward(const float *logits, const int *tokens, int V, float invn, float *dl_all) {
-    __shared__ float s_r[32];
+// d_logit rows (pt_train.c:609-621): softmax * (1/(T-1)), minus 1/(T-1) at the
+// target. The row's max and exponential sum are the forward's (k_tr_ce_rows
+// computed them with the same reductions), so one pass writes
+// exp(l - max) * (1/sum * 1/(T-1)) -- the same bits as storing the
+// exponentials and scaling them afterwards.
+__global__ void k_tr_ce_backward(const float *__restrict__ logits, const int *tokens, int V, float invn,
+                                 const float *row_max, const float *row_sum, float *__restrict__ dl_all) {
     const int t = blockIdx.x;
-    const float *lg = logits + (size_t)t * V;
-    float *dl = dl_all + (size_t)t * V;
-    float mx = -3.4028235e+38f;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) mx = fmaxf(mx, lg[v]);
-    mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float m = threadIdx.x < (blockDim.x >> 5) ? s_r[threadIdx.x] : -3.4028235e+38f;
-        m = warp_max(m);
-        if (threadIdx.x == 0) s_r[0] = m;
-    }
-    __syncthreads();
-    mx = s_r[0];
-    __syncthreads();
-    float sum = 0.f;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        const float e = pt_expf(__fsub_rn(lg[v], mx));
-        dl[v] = e;
-        sum += e;
-    }
-    sum = warp_sum(sum);
-    if ((threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = sum;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = 0.f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += s_r[w];
-        s_r[0] = __fmul_rn(__fdiv_rn(1.0f, s), invn);
-    }
-    __syncthreads();
-    const float f = s_r[0];
+    const float *__restrict__ lg = logits + (size_t)t * V;
+    float *__restrict__ dl = dl_all + (size_t)t * V;
+    const float mx = row_max[t];
+    const float f = __fmul_rn(__fdiv_rn(1.0f, row_sum[t]), invn);
     const int tgt = tokens[t + 1];
+#pragma unroll 8
     for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        float x = __fmul_rn(dl[v], f);
+        float x = __fmul_rn(pt_expf(__fsub_rn(lg[v], mx)), f);
         if (v == tgt) x = __fsub_rn(x, invn);
         dl[v] = x;
     }
@@ -734,7 +719,7 @@ extern "C" ptc_trainer *ptc_trainer_create(ptc_ctx *c, const ptc_config *cfg, co
     tr->d_xb2 = A(T * D);
     tr->d_xb3 = A(T * D);
     tr->tokens = (int *)ptc_alloc(c, T * 4);
-    tr->loss_rows = A(T);
+    tr->loss_rows = A(3 * T);   // loss per row, then the rows' max and exponential sum
     tr->loss = A(1);
     tr->loss_host = (float *)ptc_host_alloc(4);
 
@@ -812,7 +797,7 @@ extern "C" void ptc_trainer_set_microbatches(ptc_trainer *tr, int n) {
         a.x_final = A(T * D);
         a.logits = tr->has_head ? A(T * V) : nullptr;
         a.tokens = (int *)ptc_alloc(tr->ctx, T * 4);
-        a.loss_rows = A(T);
+        a.loss_rows = A(3 * T);
         a.loss = A(1);
         a.dres_save = A(T * D);
         a.T = 0;   // no length until its tokens or length are set
@@ -979,7 +964,8 @@ static void fwd_head_enqueue(ptc_trainer *tr) {
     const float *rfin = tr->res + (size_t)tr->L * T * D;
     ptc::k_tr_rmsnorm<<<(T + 7) / 8, 256, 0, s>>>(tr->x_final, rfin, tr->w.rms_final_weight, T, D);
     run_gemm(tr, G(T, V, D, tr->x_final, D, true, tr->w.wcls, D, true, tr->logits, V, ptc::EPI_STORE));
-    ptc::k_tr_ce_rows<<<T - 1, 512, 0, s>>>(tr->logits, tr->tokens, V, tr->loss_rows);
+    ptc::k_tr_ce_rows<<<T - 1, 512, 0, s>>>(tr->logits, tr->tokens, V, tr->loss_rows, tr->loss_rows + tr->maxT,
+                                            tr->loss_rows + 2 * (size_t)tr->maxT);
     ptc::k_tr_loss_sum<<<1, 32, 0, s>>>(tr->loss_rows, T - 1, tr->loss);
     PTC_CHECK(cudaGetLastError());
     PTC_CHECK(cudaMemcpyAsync(tr->loss_host, tr->loss, 4, cudaMemcpyDeviceToHost, s));
@@ -999,7 +985,8 @@ extern "C" void ptc_trainer_bwd_head(ptc_trainer *tr) {
     cudaStream_t s = tr->s;
     PTC_CHECK(cudaMemsetAsync(tr->d_res, 0, (size_t)T * D * 4, s));
     const float invn = 1.0f / (float)(T - 1);
-    ptc::k_tr_ce_backward<<<n, 512, 0, s>>>(tr->logits, tr->tokens, V, invn, tr->d_logit);
+    ptc::k_tr_ce_backward<<<n, 512, 0, s>>>(tr->logits, tr->tokens, V, invn, tr->loss_rows + tr->maxT,
+                                            tr->loss_rows + 2 * (size_t)tr->maxT, tr->d_logit);
     // d_xb = d_logit . Wcls   [n x D], K = V
     run_gemm(tr, G(n, D, V, tr->d_logit, V, true, tr->w.wcls, D, false, tr->d_xb, D, ptc::EPI_STORE));
     const float *rfin = tr->res + (size_t)tr->L * T * D;
