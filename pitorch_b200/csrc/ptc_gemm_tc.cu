@@ -67,15 +67,17 @@ Stride make_strides(int64_t s0, int64_t s1, int64_t s2) {
     return st;
 }
 
-// Per-device workspace of the CUTLASS kernels (grown on demand, never freed).
-void *tc_workspace(size_t bytes) {
+// Workspace of the CUTLASS kernels, one per device and stream (grown on
+// demand, never freed): products on different streams of a device may run
+// at the same time.
+void *tc_workspace(size_t bytes, cudaStream_t s) {
     static pthread_mutex_t mu = PTHREAD_MUTEX_INITIALIZER;
-    static std::map<int, std::pair<void *, size_t>> ws;
+    static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> ws;
     if (bytes == 0) return nullptr;
     int dev = 0;
     PTC_CHECK(cudaGetDevice(&dev));
     pthread_mutex_lock(&mu);
-    auto &w = ws[dev];
+    auto &w = ws[{dev, s}];
     if (w.second < bytes) {
         if (w.first) PTC_CHECK(cudaFree(w.first));
         PTC_CHECK(cudaMalloc(&w.first, bytes));
@@ -108,7 +110,7 @@ bool run_tc(int M, int N, int K, int L, const float *A, int64_t lda, int64_t bsa
                                      {{1.0f, beta}, C, sC, D, sD}};
     typename G::Gemm gemm;
     if (gemm.can_implement(args) != cutlass::Status::kSuccess) return false;
-    void *ws = tc_workspace(G::Gemm::get_workspace_size(args));
+    void *ws = tc_workspace(G::Gemm::get_workspace_size(args), s);
     if (gemm.initialize(args, ws, s) != cutlass::Status::kSuccess) return false;
     if (gemm.run(s) != cutlass::Status::kSuccess) PTC_FATAL("tensor-core GEMM launch failed (%d x %d x %d)", M, N, K);
     PTC_CHECK(cudaGetLastError());

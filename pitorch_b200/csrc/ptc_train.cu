@@ -589,7 +589,8 @@ constexpr int PTC_MAX_MICROBATCHES = 16;
 // beside q, w3 beside w1. Backward (ptc_trainer_bwd_layers): the weight
 // gradients beside the input gradients.
 enum { EV_FFN2, EV_FFN13, EV_WO, EV_QKV, EV_J_FFN2, EV_J_FFN13, EV_J_WO, EV_J_QKV,
-       EV_F_KV, EV_F_W3, EV_J_F_KV, EV_J_F_W3, EV_J_X3, EV_J_XK, EV_J_XV, EV_RMS, EV_J_CS, N_EV };
+       EV_F_KV, EV_F_W3, EV_J_F_KV, EV_J_F_W3, EV_J_X3, EV_J_XK, EV_J_XV, EV_RMS, EV_J_CS, EV_HEAD, EV_J_HEAD,
+       N_EV };
 
 struct ptc_trainer {
     ptc_ctx *ctx;
@@ -987,14 +988,23 @@ extern "C" void ptc_trainer_bwd_head(ptc_trainer *tr) {
     const float invn = 1.0f / (float)(T - 1);
     ptc::k_tr_ce_backward<<<n, 512, 0, s>>>(tr->logits, tr->tokens, V, invn, tr->loss_rows + tr->maxT,
                                             tr->loss_rows + 2 * (size_t)tr->maxT, tr->d_logit);
+    // dWcls += d_logit^T . x_final   [V x D], K = n -- on the second stream
+    // (its own split-K and tensor-core workspaces), beside the input gradient
+    fork_to_s2(tr, EV_HEAD);
+    {
+        GemmArgs g = G(V, D, n, tr->d_logit, V, false, tr->x_final, D, false, tr->g_wcls, D, ptc::EPI_ACCUM);
+        g.partial = tr->partial2;
+        g.partial_cap = tr->partial_cap;
+        ptc::gemm(g, tr->n_sm, tr->s2);
+    }
+    mark_s2(tr, EV_J_HEAD);
     // d_xb = d_logit . Wcls   [n x D], K = V
     run_gemm(tr, G(n, D, V, tr->d_logit, V, true, tr->w.wcls, D, false, tr->d_xb, D, ptc::EPI_STORE));
     const float *rfin = tr->res + (size_t)tr->L * T * D;
     ptc::k_tr_rmsnorm_bwd<<<(n + 7) / 8, 256, 0, s>>>(tr->d_res, tr->dw_rows, tr->d_xb, nullptr, nullptr, rfin,
                                                       tr->w.rms_final_weight, n, D);
     ptc::k_tr_colsum_accum<<<(D + 31) / 32, 256, 0, s>>>(tr->g_rms_final, tr->dw_rows, n, D);
-    // dWcls += d_logit^T . x_final   [V x D], K = n
-    run_gemm(tr, G(V, D, n, tr->d_logit, V, false, tr->x_final, D, false, tr->g_wcls, D, ptc::EPI_ACCUM));
+    join_s2(tr, EV_J_HEAD);   // the classifier gradient (tied: the embedding's) is complete
     PTC_CHECK(cudaGetLastError());
 }
 
