@@ -41,6 +41,7 @@ struct ptc_decoder {
     cudaGraphExec_t g_host, g_dev;
     cudaGraphExec_t g_devk;  // DEV_TOKENS device-loop tokens per launch (null: not used)
     int fetch_logits;      // ptc_decoder_enqueue_fetch copied the logits into stage
+    int w2t_stale;         // the weights changed since w2t was derived (re-derived before the next decode)
     unsigned long long *trace_buf;  // phase timeline record (m.trace while tracing)
     size_t trace_n;        // its entries
     // pipeline stage graphs (ptc_decoder_set_links): STAGE_POS positions and one
@@ -289,9 +290,17 @@ extern "C" ptc_decoder *ptc_decoder_create(ptc_ctx *c, const ptc_config *cfg, co
 
 // Re-derive device-side copies that depend on the weights (the transposed
 // w2 of the fused FFN) after an in-place update.
+// Training steps mark the transposed w2 stale; the decode entry points below
+// re-derive it (on the decoder's stream, after the update) before they
+// enqueue layer kernels, so a run of training steps pays for it once.
 extern "C" void ptc_decoder_weights_updated(ptc_decoder *d) {
-    if (!d->m.w2t) return;
+    if (d->m.w2t) d->w2t_stale = 1;
+}
+
+static void refresh_derived(ptc_decoder *d) {
+    if (!d->w2t_stale) return;
     ptc::transpose_w2(d->m, (float *)d->m.w2t, d->stream);
+    d->w2t_stale = 0;
 }
 
 // Tracing is a kernel parameter (m.trace non-null), so the untraced kernels
@@ -374,6 +383,7 @@ static void wait_next(ptc_decoder *d) {
 
 extern "C" int ptc_decoder_step(ptc_decoder *d, int token, int pos, float *logits_host) {
     if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
+    refresh_derived(d);
     if (d->has_embed && (token < 0 || token >= d->m.V))
         PTC_FATAL("token %d outside [0, %d)", token, d->m.V);
     set_mode(d, 0);
@@ -440,6 +450,7 @@ extern "C" void ptc_decoder_generate_begin(ptc_decoder *d, const int *prompt, in
 }
 
 extern "C" void ptc_decoder_enqueue_steps(ptc_decoder *d, int n) {
+    refresh_derived(d);
     int i = 0;
     if (d->g_devk)
         for (; i + DEV_TOKENS <= n; i += DEV_TOKENS) PTC_CHECK(cudaGraphLaunch(d->g_devk, d->stream));
@@ -478,6 +489,7 @@ extern "C" void ptc_decoder_enqueue_embed(ptc_decoder *d, int token) {
 }
 
 extern "C" void ptc_decoder_enqueue_layers(ptc_decoder *d, int pos, int l_start, int l_end) {
+    refresh_derived(d);
     if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
     if (l_start < 0 || l_end > d->m.L || l_start > l_end)
         PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
@@ -537,12 +549,14 @@ extern "C" int *ptc_decoder_pos_dev(ptc_decoder *d) { return &d->m.step->pos; }
 extern "C" int *ptc_decoder_tok_dev(ptc_decoder *d) { return &d->m.step->tok; }
 
 extern "C" void ptc_decoder_enqueue_layers_devpos(ptc_decoder *d, int l_start, int l_end) {
+    refresh_derived(d);
     if (l_start < 0 || l_end > d->m.L || l_start > l_end)
         PTC_FATAL("layer range [%d, %d) outside [0, %d)", l_start, l_end, d->m.L);
     ptc::launch_layers(d->m, l_start, l_end, false, d->n_sm, d->stream);
 }
 
 extern "C" void ptc_decoder_enqueue_kernel(ptc_decoder *d, int kind, int l, int pos) {
+    refresh_derived(d);
     if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
     set_mode(d, 0);
     put_step_int(d, &d->m.step->pos, pos);
@@ -640,6 +654,7 @@ extern "C" void ptc_decoder_set_stop(ptc_decoder *d, int n_pos) {
 }
 
 extern "C" void ptc_decoder_enqueue_stage(ptc_decoder *d, int n) {
+    refresh_derived(d);
     if (!d->m.in_box) PTC_FATAL("ptc_decoder_enqueue_stage without pipeline links");
     int i = 0;
     for (; i + STAGE_POS <= n; i += STAGE_POS) PTC_CHECK(cudaGraphLaunch(d->g_stage, d->stream));
