@@ -44,3 +44,49 @@ def test_reference_arm_two_ranks_rank0_only():
     lines = last_json(r.stdout)
     assert len(lines) == 1
     check_line(lines[0], 2)
+
+
+def _bench():
+    sys.path.insert(0, ROOT)
+    import bench
+    return bench
+
+
+def test_stream_parity_against_the_fixture():
+    """The N = 1 line's parity key: the reference stream itself matches all
+    1024 positions; a stream changed at position p matches p positions and
+    counts as equal only when p lies past the reference's first near-tie."""
+    import numpy as np
+    bench = _bench()
+    g = np.load(os.path.join(ROOT, "tests", "golden", "decode_stories110M_long.npz"))
+    ref = np.asarray(g["tokens"], dtype=np.int32)
+    seq = len(ref)
+    p = bench.stream_parity(ref.copy(), seq)
+    assert p["matched_positions"] == seq and p["equal_positions"] == seq and p["equal_up_to_first_near_tie"]
+    first_tie = p["first_near_tie"]
+    early = min(first_tie, seq) // 2
+    bad = ref.copy()
+    bad[early] = (bad[early] + 1) % 32000
+    q = bench.stream_parity(bad, seq)
+    assert q["matched_positions"] == early and q["equal_positions"] == seq - 1
+    assert q["equal_up_to_first_near_tie"] is False
+
+
+def test_decode_byte_model():
+    """Algorithmic bytes per token of the 110M decode: 438.04 MB of weights
+    (tied classifier read once) plus the K/V rows read and written; the mean
+    over 1024 positions is the 475.98 MB the roofline uses."""
+    import numpy as np
+    bench = _bench()
+    cfg = bench.synth.CONFIGS["stories110M"]
+    b0 = bench.decode_bytes_per_token(cfg, 0)
+    mean = np.mean([bench.decode_bytes_per_token(cfg, p) for p in range(cfg[6])])
+    assert abs(b0 / 1e6 - 438.1) < 0.2, b0
+    assert abs(mean / 1e6 - 475.98) < 0.01, mean
+
+
+def test_cpu_sample_positions_cover_the_decode():
+    bench = _bench()
+    pos = bench.stratified_positions(96, 1024)
+    assert len(pos) == 96 and pos == sorted(pos) and pos[0] >= 0 and pos[-1] < 1024
+    assert abs(sum(pos) / len(pos) - 511.5) < 1.0   # mean position of the whole decode
