@@ -245,8 +245,10 @@ typedef struct {
     unsigned *sent;          /* device counters: [0] residuals sent, [1] keys sent; zero at the start */
 } ptc_vocab_split;
 void ptc_decoder_set_vocab_parallel(ptc_decoder *d, const ptc_vocab_split *vp);
-/* Host-driven step input of a pipeline rank: mode 0, position pos, and the
- * input token copied from device memory (tok_dev; NULL keeps the token). */
+/* Host-driven step input of a pipeline rank: mode 0, position pos (through
+ * the decoder's pinned block: its previous host-step work must have
+ * completed), and the input token copied from device memory (tok_dev; NULL
+ * keeps the token). */
 void ptc_decoder_set_input(ptc_decoder *d, int pos, const int *tok_dev);
 
 /* Weights were updated in place (training): refresh derived device copies. */

@@ -642,7 +642,9 @@ extern "C" void ptc_decoder_set_vocab_parallel(ptc_decoder *d, const ptc_vocab_s
 extern "C" void ptc_decoder_set_input(ptc_decoder *d, int pos, const int *tok_dev) {
     if (pos < 0 || pos >= d->m.seq) PTC_FATAL("decode position %d outside [0, %d)", pos, d->m.seq);
     set_mode(d, 0);
-    put_step_int(d, &d->m.step->pos, pos);
+    // through the pinned io block, like ptc_decoder_enqueue_embed_at
+    d->io->pos = pos;
+    PTC_CHECK(cudaMemcpyAsync(&d->m.step->pos, &d->io->pos, sizeof(int), cudaMemcpyHostToDevice, d->stream));
     if (tok_dev)
         PTC_CHECK(cudaMemcpyAsync(&d->m.step->tok, tok_dev, sizeof(int), cudaMemcpyDeviceToDevice, d->stream));
 }
